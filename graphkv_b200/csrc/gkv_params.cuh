@@ -1,0 +1,84 @@
+// Launch parameters resolved on the host from a gkv_plan (passed by value as
+// __grid_constant__ kernel arguments, kept under the classic 4 KiB limit).
+#pragma once
+
+#include "gkv_common.cuh"
+
+namespace gkv {
+
+constexpr int kThreads = 256;    // threads per block of the tile kernels
+constexpr int kMaxLayers = 40;   // layers per launch (larger calls are split)
+constexpr int kRetTile = 64;     // retained rows per tile
+
+// Tier numbering inside the kernels: 0 retained, 1 standard, 2 cold.
+// Tensor numbering follows gkv_tensor_slot: 0 std K, 1 std V, 2 cold K, 3 cold V.
+
+struct TensorDesc {
+  int bits;         // 2, 4, 8
+  int quantizer;    // GKV_SYMMETRIC / GKV_AFFINE
+  int axis;         // GKV_AXIS_TOKEN / GKV_AXIS_CHANNEL
+  int gs;           // effective group size
+  int log2gs;       // log2(gs) when gs is a power of two, else -1
+  int rotation;     // GKV_ROT_*
+  int packed;       // 1: sub-byte packing
+  int sbits;        // stored bits per code (bits when packed, else 8)
+  int scale_dtype;  // GKV_F16 / GKV_BF16 / GKV_F32
+  int n;            // tier length
+  int n_pad;        // token axis: padded tier length; channel axis: padded head_dim
+  int groups_row;   // token axis: groups per channel (n_pad / gs); channel: groups per token
+  int64_t elems_slice;   // codes per slice
+  int64_t groups_slice;  // groups per slice
+  uint8_t* codes;
+  void* scales;
+  uint8_t* zps;     // affine only
+  float* scale32;   // general path workspace: fp32 coding scales per group
+  void* rot;        // general path workspace: rotated tier rows [S, n, D]
+};
+
+struct LayerDesc {
+  const void* k;
+  const void* v;
+  int64_t ks[3];    // batch, head, token strides (elements)
+  int64_t vs[3];
+  int heads;
+  int slice_begin;  // first slice of this layer within the launch
+};
+
+struct QuantParams {
+  int B, T, D, S, n_layers;
+  const int* idx[3];
+  int n_tier[3];
+  TensorDesc t[4];
+  void* ret_k;
+  void* ret_v;
+  float had_div, had_inv;
+  int tt;            // tile rows of the fast path (64 or 128)
+  int tiles[3];      // fast-path tiles per slice per tier (0 when the tier is not in this launch)
+  int tiles_slice;
+  int slice_offset;  // global index of slice 0 of this launch (retained / codes addressing)
+  LayerDesc layers[kMaxLayers];
+};
+
+struct DequantParams {
+  int T, D, S;
+  const int* idx[3];
+  int n_tier[3];
+  TensorDesc t[4];
+  const void* ret_k;
+  const void* ret_v;
+  void* out_k;       // [S, T, D]
+  void* out_v;
+  float had_div, had_inv;
+  int tt;
+  int tiles[3];
+  int tiles_slice;
+};
+
+// Slice -> layer lookup (layers sorted by slice_begin).
+__device__ __forceinline__ int find_layer(const QuantParams& p, int s) {
+  int l = 0;
+  while (l + 1 < p.n_layers && s >= p.layers[l + 1].slice_begin) ++l;
+  return l;
+}
+
+}  // namespace gkv
