@@ -1,0 +1,392 @@
+// extern "C" entry points of libgraphkv_b200.so (declared in include/graphkv_b200.h):
+// argument validation, routing of each tier to the tile kernels or the general
+// kernels, workspace layout, and launches.  Nothing here allocates device memory.
+// The library is one translation unit: the kernel sources are included below.
+#include <cmath>
+#include <cstdio>
+#include <string>
+
+#include "dequantize.cuh"
+#include "gkv_params.cuh"
+#include "quantize.cuh"
+#include "select.cuh"
+
+namespace gkv {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(GKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
+int ilog2(int x) { int l = 0; while ((1 << l) < x) ++l; return l; }
+int elem_size(int dtype) { return dtype == GKV_F32 ? 4 : 2; }
+
+// tile-kernel instantiations: (D, TT) per element size
+bool tile_instantiated(int esize, int D, int TT) {
+  if (D == 64) return TT == 64 || TT == 128;
+  if (D == 128) return TT == 64 || (TT == 128 && esize == 2);
+  if (D == 256) return TT == 64 && esize == 2;
+  return false;
+}
+
+// rows per thread segment of the token-axis quantizer (quant_token_tile)
+int token_seg_rows(int esize, int D, int TT) {
+  const int words = D * esize / 4;
+  return TT / (kThreads / words);
+}
+
+const int kTierOf[4] = {1, 1, 2, 2};
+
+struct Resolved {
+  TensorDesc t[4];
+  int n[3];
+  bool fast[3];   // [0]: retained copy inside the tile kernel; [1], [2]: tiers
+  int tt;
+  size_t ws_scale[4], ws_rot[4], ws_bytes;
+};
+
+int resolve_tensor(const gkv_plan& p, int i, int n, TensorDesc& d) {
+  const gkv_tensor_spec& sp = p.spec[i];
+  char buf[160];
+  if (sp.bits != 2 && sp.bits != 4 && sp.bits != 8) {
+    std::snprintf(buf, sizeof buf, "tensor %d: bits must be 2, 4 or 8 (got %d)", i, sp.bits);
+    return fail(GKV_ERR_INVALID, buf);
+  }
+  if (sp.quantizer != GKV_SYMMETRIC && sp.quantizer != GKV_AFFINE) return fail(GKV_ERR_INVALID, "bad quantizer");
+  if (sp.axis != GKV_AXIS_TOKEN && sp.axis != GKV_AXIS_CHANNEL) return fail(GKV_ERR_INVALID, "bad axis");
+  if (sp.rotation != GKV_ROT_NONE && sp.rotation != GKV_ROT_HADAMARD) return fail(GKV_ERR_INVALID, "bad rotation");
+  if (sp.scale_dtype < GKV_F32 || sp.scale_dtype > GKV_BF16) return fail(GKV_ERR_INVALID, "bad scale dtype");
+  if (sp.packed && sp.bits == 8) return fail(GKV_ERR_INVALID, "8-bit codes are never packed");
+  const int D = p.head_dim;
+  const int axis_len = sp.axis == GKV_AXIS_TOKEN ? n : D;
+  if (sp.group_size < 1 || sp.group_size > axis_len) {
+    std::snprintf(buf, sizeof buf, "tensor %d: group_size %d outside [1, %d]", i, sp.group_size, axis_len);
+    return fail(GKV_ERR_INVALID, buf);
+  }
+  if (sp.rotation && (!is_pow2(D) || D > 1024))
+    return fail(GKV_ERR_INVALID, "hadamard rotation requires a power-of-two head dimension (<= 1024).");
+  if (!p.codes[i] || !p.scales[i]) return fail(GKV_ERR_INVALID, "missing codes/scales storage");
+  if (sp.quantizer == GKV_AFFINE && !p.zero_points[i]) return fail(GKV_ERR_INVALID, "affine tensor needs zero points");
+  d.bits = sp.bits;
+  d.quantizer = sp.quantizer;
+  d.axis = sp.axis;
+  d.gs = sp.group_size;
+  d.log2gs = is_pow2(d.gs) ? ilog2(d.gs) : -1;
+  d.rotation = sp.rotation;
+  d.packed = sp.packed ? 1 : 0;
+  d.sbits = d.packed ? d.bits : 8;
+  d.scale_dtype = sp.scale_dtype;
+  d.n = n;
+  const int len = axis_len;
+  d.n_pad = (int)(ceil_div(len, d.gs) * d.gs);
+  d.groups_row = d.n_pad / d.gs;
+  if (sp.axis == GKV_AXIS_TOKEN) {
+    d.elems_slice = (int64_t)D * d.n_pad;
+    d.groups_slice = (int64_t)D * d.groups_row;
+  } else {
+    d.elems_slice = (int64_t)n * d.n_pad;
+    d.groups_slice = (int64_t)n * d.groups_row;
+  }
+  d.codes = p.codes[i];
+  d.scales = p.scales[i];
+  d.zps = sp.quantizer == GKV_AFFINE ? p.zero_points[i] : nullptr;
+  d.scale32 = nullptr;
+  d.rot = nullptr;
+  return GKV_OK;
+}
+
+// Can tensor d run in the tile kernels with tile height TT?
+bool tensor_fast(const TensorDesc& d, int esize, int D, int TT, bool quantize) {
+  if (d.log2gs < 0 || d.gs < 16 || !aligned16(d.codes)) return false;
+  if (d.axis == GKV_AXIS_TOKEN) {
+    if (d.gs > TT || TT % d.gs) return false;
+    if (quantize && d.gs < token_seg_rows(esize, D, TT)) return false;
+    return true;
+  }
+  const int vec = 16 / esize;
+  if (D % d.gs || d.gs % vec || d.gs / vec > 32) return false;
+  return true;
+}
+
+bool layers_aligned(const gkv_layer_in* layers, int n_layers, int esize) {
+  for (int l = 0; l < n_layers; ++l) {
+    const gkv_layer_in& L = layers[l];
+    if (!aligned16(L.k) || !aligned16(L.v)) return false;
+    for (int q = 0; q < 3; ++q)
+      if ((L.k_stride[q] * esize) % 16 || (L.v_stride[q] * esize) % 16) return false;
+  }
+  return true;
+}
+
+int resolve_plan(const gkv_plan* pp, int64_t S, bool quantize, const gkv_layer_in* layers, int n_layers,
+                 bool outputs_aligned, Resolved& r) {
+  if (!pp) return fail(GKV_ERR_INVALID, "plan is NULL");
+  const gkv_plan& p = *pp;
+  if (p.batch < 1 || p.head_dim < 1 || p.seq_len < 1) return fail(GKV_ERR_INVALID, "batch, head_dim, seq_len >= 1");
+  if (p.dtype < GKV_F32 || p.dtype > GKV_BF16) return fail(GKV_ERR_INVALID, "bad dtype");
+  if (p.n_retained < 0 || p.n_standard < 0 || p.n_cold < 0 ||
+      (int64_t)p.n_retained + p.n_standard + p.n_cold != p.seq_len)
+    return fail(GKV_ERR_INVALID, "tier lengths must be >= 0 and sum to seq_len");
+  if ((p.n_retained && !p.idx_retained) || (p.n_standard && !p.idx_standard) || (p.n_cold && !p.idx_cold))
+    return fail(GKV_ERR_INVALID, "missing index list");
+  if (p.n_retained && (!p.retained_k || !p.retained_v)) return fail(GKV_ERR_INVALID, "missing retained storage");
+  r.n[0] = p.n_retained;
+  r.n[1] = p.n_standard;
+  r.n[2] = p.n_cold;
+  const int D = p.head_dim;
+  const int esize = elem_size(p.dtype);
+  bool any_rot = false;
+  for (int i = 0; i < 4; ++i) {
+    r.t[i] = TensorDesc{};
+    const int n = r.n[kTierOf[i]];
+    if (n == 0) continue;
+    const int st = resolve_tensor(p, i, n, r.t[i]);
+    if (st != GKV_OK) return st;
+    any_rot |= r.t[i].rotation != 0;
+    if (quantize && n_layers > 1 && r.t[i].packed && (r.t[i].elems_slice * r.t[i].sbits) % 8)
+      return fail(GKV_ERR_INVALID, "codes of one slice are not whole bytes: call one layer at a time");
+  }
+  if (any_rot && !(p.hadamard_divisor > 0.f)) return fail(GKV_ERR_INVALID, "hadamard_divisor must be > 0");
+
+  // tile routing
+  const bool geom_ok = (D * esize) % 16 == 0 && tile_instantiated(esize, D, 64) && outputs_aligned &&
+                       (!quantize || layers_aligned(layers, n_layers, esize));
+  const bool ret_ok = p.n_retained == 0 || (aligned16(p.retained_k) && aligned16(p.retained_v));
+  int tt = 64;
+  bool want[3] = {false, false, false};
+  for (int tier = 1; tier <= 2; ++tier) {
+    if (!geom_ok || r.n[tier] == 0) continue;
+    int need = 64;
+    for (int i = 0; i < 4; ++i)
+      if (kTierOf[i] == tier && r.t[i].axis == GKV_AXIS_TOKEN) need = need > r.t[i].gs ? need : r.t[i].gs;
+    if (need > 128 || !tile_instantiated(esize, D, need)) continue;
+    want[tier] = true;
+    tt = tt > need ? tt : need;
+  }
+  r.tt = tt;
+  for (int tier = 1; tier <= 2; ++tier) {
+    bool ok = want[tier];
+    for (int i = 0; i < 4 && ok; ++i)
+      if (kTierOf[i] == tier) ok = tensor_fast(r.t[i], esize, D, tt, quantize);
+    r.fast[tier] = ok;
+  }
+  r.fast[0] = geom_ok && ret_ok && p.n_retained > 0;
+
+  // workspace of the general quantize path
+  size_t off = 0;
+  for (int i = 0; i < 4; ++i) {
+    r.ws_scale[i] = r.ws_rot[i] = 0;
+    const int tier = kTierOf[i];
+    if (!quantize || r.n[tier] == 0 || r.fast[tier]) continue;
+    r.ws_scale[i] = off;
+    off = align256(off + (size_t)S * r.t[i].groups_slice * sizeof(float));
+    if (r.t[i].rotation) {
+      r.ws_rot[i] = off;
+      off = align256(off + (size_t)S * r.t[i].n * D * esize);
+    }
+  }
+  r.ws_bytes = off;
+  return GKV_OK;
+}
+
+int64_t total_slices(const gkv_plan& p, const gkv_layer_in* layers, int n_layers) {
+  int64_t s = 0;
+  for (int l = 0; l < n_layers; ++l) s += (int64_t)p.batch * layers[l].heads;
+  return s;
+}
+
+}  // namespace
+}  // namespace gkv
+
+using namespace gkv;
+
+extern "C" {
+
+int32_t gkv_abi_version(void) { return GKV_ABI_VERSION; }
+
+const char* gkv_last_error(void) { return g_last_error.c_str(); }
+
+int32_t gkv_device_error(int32_t* code) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int v = 0;
+  if ((e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int))) != cudaSuccess)
+    return cuda_fail(e, "reading the device error word");
+  const int zero = 0;
+  if ((e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int))) != cudaSuccess)
+    return cuda_fail(e, "clearing the device error word");
+  if (code) *code = v;
+  return GKV_OK;
+}
+
+size_t gkv_select_workspace_bytes(int32_t seq_len) { return seq_len > 0 ? align256((size_t)seq_len) : 0; }
+
+int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const gkv_select_policy* pol,
+                         int32_t* idx_retained, int32_t* idx_standard, int32_t* idx_cold, void* workspace,
+                         size_t workspace_bytes, gkv_stream_t stream) {
+  if (!pol) return fail(GKV_ERR_INVALID, "policy is NULL");
+  const gkv_select_policy& p = *pol;
+  const int T = p.seq_len;
+  if (T < 1) return fail(GKV_ERR_INVALID, "seq_len must be >= 1");
+  if (p.sink < 0 || p.sink > T || p.tail < 0 || p.tail > T || p.keep_protect < 0 || p.keep_outlier < 0 ||
+      p.keep_cold < 0)
+    return fail(GKV_ERR_INVALID, "sink/tail/keep counts out of range");
+  if (p.n_retained < 0 || p.n_standard < 0 || p.n_cold < 0 ||
+      (int64_t)p.n_retained + p.n_standard + p.n_cold != T)
+    return fail(GKV_ERR_INVALID, "tier lengths must sum to seq_len");
+  if ((p.keep_protect || p.keep_cold) && !scores) return fail(GKV_ERR_INVALID, "scores required");
+  if (p.keep_outlier && !outlier_scores) return fail(GKV_ERR_INVALID, "outlier scores required");
+  if ((p.n_retained && !idx_retained) || (p.n_standard && !idx_standard) || (p.n_cold && !idx_cold))
+    return fail(GKV_ERR_INVALID, "missing index list output");
+  if (!workspace || workspace_bytes < (size_t)T) return fail(GKV_ERR_WORKSPACE, "selection workspace too small");
+  cudaError_t e = launch_select(scores, outlier_scores, p, idx_retained, idx_standard, idx_cold,
+                                static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GKV_OK : cuda_fail(e, "select kernel launch");
+}
+
+int32_t gkv_outlier_scores(const gkv_layer_in* layer, int32_t batch, int32_t seq_len, int32_t head_dim,
+                           int32_t dtype, float* out, gkv_stream_t stream) {
+  if (!layer || !layer->k || !layer->v || !out) return fail(GKV_ERR_INVALID, "NULL argument");
+  if (batch < 1 || seq_len < 1 || head_dim < 1 || layer->heads < 1) return fail(GKV_ERR_INVALID, "bad geometry");
+  if (dtype < GKV_F32 || dtype > GKV_BF16) return fail(GKV_ERR_INVALID, "bad dtype");
+  cudaError_t e = launch_outlier(*layer, batch, seq_len, head_dim, dtype, out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GKV_OK : cuda_fail(e, "outlier kernel launch");
+}
+
+size_t gkv_quantize_workspace_bytes(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n_layers) {
+  if (!plan || !layers || n_layers < 1) return 0;
+  Resolved r;
+  if (resolve_plan(plan, total_slices(*plan, layers, n_layers), true, layers, n_layers, true, r) != GKV_OK) return 0;
+  return r.ws_bytes;
+}
+
+int32_t gkv_quantize(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n_layers, void* workspace,
+                     size_t workspace_bytes, gkv_stream_t stream) {
+  if (!plan || !layers || n_layers < 1) return fail(GKV_ERR_INVALID, "plan/layers missing");
+  for (int l = 0; l < n_layers; ++l)
+    if (!layers[l].k || !layers[l].v || layers[l].heads < 1) return fail(GKV_ERR_INVALID, "bad layer input");
+  const int64_t S_total = total_slices(*plan, layers, n_layers);
+  if (S_total > (int64_t)1 << 30) return fail(GKV_ERR_TOO_LARGE, "too many slices");
+  Resolved r;
+  int st = resolve_plan(plan, S_total, true, layers, n_layers, true, r);
+  if (st != GKV_OK) return st;
+  if (r.ws_bytes && (!workspace || workspace_bytes < r.ws_bytes))
+    return fail(GKV_ERR_WORKSPACE, "workspace too small: need " + std::to_string(r.ws_bytes) + " bytes");
+  for (int i = 0; i < 4; ++i) {
+    if (r.ws_bytes == 0 || r.fast[kTierOf[i]] || r.n[kTierOf[i]] == 0) continue;
+    r.t[i].scale32 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + r.ws_scale[i]);
+    if (r.t[i].rotation) r.t[i].rot = static_cast<uint8_t*>(workspace) + r.ws_rot[i];
+  }
+  const gkv_plan& p = *plan;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  QuantParams q;
+  q.B = p.batch;
+  q.T = p.seq_len;
+  q.D = p.head_dim;
+  q.idx[0] = p.idx_retained;
+  q.idx[1] = p.idx_standard;
+  q.idx[2] = p.idx_cold;
+  for (int k = 0; k < 3; ++k) q.n_tier[k] = r.n[k];
+  for (int i = 0; i < 4; ++i) q.t[i] = r.t[i];
+  q.ret_k = p.retained_k;
+  q.ret_v = p.retained_v;
+  q.had_div = p.hadamard_divisor;
+  q.had_inv = p.hadamard_divisor > 0.f ? 1.0f / p.hadamard_divisor : 0.f;
+  q.tt = r.tt;
+  q.tiles[0] = r.fast[0] ? (int)ceil_div(r.n[0], kRetTile) : 0;
+  for (int k = 1; k <= 2; ++k) q.tiles[k] = r.fast[k] ? (int)ceil_div(r.n[k], r.tt) : 0;
+  q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
+  int64_t slice0 = 0;
+  for (int l0 = 0; l0 < n_layers; l0 += kMaxLayers) {
+    const int nl = n_layers - l0 < kMaxLayers ? n_layers - l0 : kMaxLayers;
+    int S = 0;
+    for (int l = 0; l < nl; ++l) {
+      const gkv_layer_in& L = layers[l0 + l];
+      LayerDesc& d = q.layers[l];
+      d.k = L.k;
+      d.v = L.v;
+      for (int c = 0; c < 3; ++c) { d.ks[c] = L.k_stride[c]; d.vs[c] = L.v_stride[c]; }
+      d.heads = L.heads;
+      d.slice_begin = S;
+      S += p.batch * L.heads;
+    }
+    q.n_layers = nl;
+    q.S = S;
+    q.slice_offset = (int)slice0;
+    cudaError_t e = cudaSuccess;
+    if (q.tiles_slice > 0 && (e = launch_quantize_tiles(q, p.dtype, s)) != cudaSuccess)
+      return cuda_fail(e, "quantize tile kernel");
+    if (!r.fast[0] && r.n[0] > 0 && (e = launch_retained_general(q, p.dtype, s)) != cudaSuccess)
+      return cuda_fail(e, "retained copy kernel");
+    for (int i = 0; i < 4; ++i) {
+      const int tier = kTierOf[i];
+      if (r.n[tier] == 0 || r.fast[tier]) continue;
+      if ((e = launch_quantize_general(q, p.dtype, i, tier, s)) != cudaSuccess)
+        return cuda_fail(e, "general quantize kernels");
+    }
+    slice0 += S;
+  }
+  return GKV_OK;
+}
+
+size_t gkv_dequantize_workspace_bytes(const gkv_plan* plan, int32_t n_slices) {
+  (void)plan;
+  (void)n_slices;
+  return 0;
+}
+
+int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void* v_out, void* workspace,
+                       size_t workspace_bytes, gkv_stream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!plan || !k_out || !v_out || n_slices < 1) return fail(GKV_ERR_INVALID, "plan/outputs missing");
+  Resolved r;
+  const bool out_aligned = aligned16(k_out) && aligned16(v_out);
+  int st = resolve_plan(plan, n_slices, false, nullptr, 0, out_aligned, r);
+  if (st != GKV_OK) return st;
+  const gkv_plan& p = *plan;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DequantParams q;
+  q.T = p.seq_len;
+  q.D = p.head_dim;
+  q.S = n_slices;
+  q.idx[0] = p.idx_retained;
+  q.idx[1] = p.idx_standard;
+  q.idx[2] = p.idx_cold;
+  for (int k = 0; k < 3; ++k) q.n_tier[k] = r.n[k];
+  for (int i = 0; i < 4; ++i) q.t[i] = r.t[i];
+  q.ret_k = p.retained_k;
+  q.ret_v = p.retained_v;
+  q.out_k = k_out;
+  q.out_v = v_out;
+  q.had_div = p.hadamard_divisor;
+  q.had_inv = p.hadamard_divisor > 0.f ? 1.0f / p.hadamard_divisor : 0.f;
+  q.tt = r.tt;
+  q.tiles[0] = r.fast[0] ? (int)ceil_div(r.n[0], kRetTile) : 0;
+  for (int k = 1; k <= 2; ++k) q.tiles[k] = r.fast[k] ? (int)ceil_div(r.n[k], r.tt) : 0;
+  q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
+  cudaError_t e;
+  if (q.tiles_slice > 0 && (e = launch_dequantize_tiles(q, p.dtype, s)) != cudaSuccess)
+    return cuda_fail(e, "dequantize tile kernel");
+  if (!r.fast[0] && r.n[0] > 0 && (e = launch_dequantize_retained_general(q, p.dtype, s)) != cudaSuccess)
+    return cuda_fail(e, "retained scatter kernel");
+  for (int tier = 1; tier <= 2; ++tier) {
+    if (r.n[tier] == 0 || r.fast[tier]) continue;
+    if ((e = launch_dequantize_general(q, p.dtype, tier, s)) != cudaSuccess)
+      return cuda_fail(e, "general dequantize kernel");
+  }
+  return GKV_OK;
+}
+
+}  // extern "C"

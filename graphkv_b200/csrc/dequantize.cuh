@@ -10,6 +10,8 @@
 // tensors decode a [TT, D] fp32 tile in shared memory (thread per channel and
 // run of 16 rows), channel-axis tensors decode straight from the packed rows
 // (warp per row); both leave through warp-per-row stores of whole output rows.
+#pragma once
+
 #include "gkv_params.cuh"
 
 namespace gkv {

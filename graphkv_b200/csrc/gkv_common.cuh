@@ -20,7 +20,8 @@ enum DeviceError : int {
   kErrBadIndex = 3,         // an index list entry outside [0, T)
 };
 
-extern __device__ int g_device_error;
+// defined once: the library is a single translation unit (capi.cu)
+__device__ int g_device_error = 0;
 
 __device__ __forceinline__ void raise_error(int code) { atomicCAS(&g_device_error, 0, code); }
 

@@ -10,6 +10,8 @@
 // General path: any geometry the tiles do not cover (group sizes that are not
 // powers of two, padded head dims, tiny tiers, unaligned inputs): one thread per
 // group computes the scale, one thread per output byte packs the codes.
+#pragma once
+
 #include "gkv_params.cuh"
 
 namespace gkv {

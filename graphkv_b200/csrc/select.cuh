@@ -7,6 +7,8 @@
 // k-th key; an ordered pass then marks every candidate beyond that key plus the
 // lowest-position candidates equal to it.  A final ordered pass compacts the three
 // ascending index lists.  A one-byte tier per token lives in the workspace.
+#pragma once
+
 #include "gkv_common.cuh"
 
 namespace gkv {
@@ -162,21 +164,21 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(const SelectParams 
 }
 
 // mean(K^2) + mean(V^2) per token: warp per token, fp64 accumulation
-template <typename T>
+template <typename E>
 __global__ void outlier_kernel(const gkv_layer_in L, int B, int T, int D, float* out) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (t >= T) return;
   double acc[2] = {0.0, 0.0};
   for (int which = 0; which < 2; ++which) {
-    const T* base = reinterpret_cast<const T*>(which ? L.v : L.k);
+    const E* base = reinterpret_cast<const E*>(which ? L.v : L.k);
     const int64_t* st = which ? L.v_stride : L.k_stride;
     double a = 0.0;
     for (int b = 0; b < B; ++b)
       for (int h = 0; h < L.heads; ++h) {
-        const T* row = base + b * st[0] + h * st[1] + (int64_t)t * st[2];
+        const E* row = base + b * st[0] + h * st[1] + (int64_t)t * st[2];
         for (int c = lane; c < D; c += 32) {
-          const double x = (double)Elem<T>::to_f32(row[c]);
+          const double x = (double)Elem<E>::to_f32(row[c]);
           a += x * x;
         }
       }
