@@ -1,0 +1,909 @@
+"""Compressed KV containers and the quantize / dequantize orchestration.
+
+Mirrors the public surface of the reference's ``src/graphkv/core.py``
+(``QuantizedTensor``, ``QuantizedKvLayer``, ``QuantizedKvCache``,
+``quantize_kv_layer``, ``build_retention_mask``, ``hf_cache_to_tuple``, ...) with
+the same field names, tensor shapes, byte layouts, statistics and exceptions.
+The data path runs in the CUDA kernels of ``libgraphkv_b200.so``:
+
+* layers of one cache that share a geometry and an importance-score tensor are
+  compressed by ONE selection launch and ONE quantize launch; their outputs
+  live in one device arena and each layer's tensors are views into it;
+* tier sizes and byte counts are computed on the host before any kernel runs,
+  so the passthrough decision (core.py:770-772) needs no device sync;
+* dequantization of consecutive layers of one arena is one launch that writes
+  every output row exactly once.
+
+Inputs may live on the host: they are copied to the current CUDA device, and
+the exported (dequantized) caches are returned on the input's device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from math import sqrt
+from typing import Iterable, Literal, Sequence
+
+import torch
+from torch.nn import functional as F
+
+from . import _lib as L
+from .config import (
+    KvQuantConfig,
+    TensorPlan,
+    TierSizes,
+    effective_low_priority_ratio,
+    keep_count,
+    layer_memory_bytes,
+    resolve_tiers,
+    tensor_plans,
+)
+
+_ALIGN = 256
+
+
+def _tensor_nbytes(tensor: torch.Tensor | None) -> int:
+    if tensor is None:
+        return 0
+    return tensor.numel() * tensor.element_size()
+
+
+def _dtype_element_size(dtype: torch.dtype) -> int:
+    return torch.empty((), dtype=dtype).element_size()
+
+
+def _compute_device(t: torch.Tensor) -> torch.device:
+    if t.is_cuda:
+        return t.device
+    if not torch.cuda.is_available():
+        raise RuntimeError("graphkv_b200 needs a CUDA device; there is no CPU fallback.")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    if t.device == device:
+        return t
+    return t.to(device, non_blocking=t.is_pinned())
+
+
+# ---------------------------------------------------------------------------
+# containers
+# ---------------------------------------------------------------------------
+
+@dataclass
+class QuantizedTensor:
+    """One compressed tensor (core.py:130-173): packed codes ``q`` (one
+    little-end-first byte stream of the moved, padded ``q_shape`` tensor),
+    ``scales`` ``[..., n_groups, 1]`` and optional uint8 ``zero_points``."""
+
+    q: torch.Tensor
+    scales: torch.Tensor
+    zero_points: torch.Tensor | None
+    original_shape: tuple[int, ...]
+    axis: int
+    group_size: int
+    bits: int
+    padded: int
+    q_shape: tuple[int, ...]
+    original_dtype: torch.dtype
+    packed: bool
+    packed_offset: int
+    rotation: str = "none"
+
+    @property
+    def qmin(self) -> int:
+        return -(1 << (self.bits - 1))
+
+    def memory_bytes(self) -> int:
+        return _tensor_nbytes(self.q) + _tensor_nbytes(self.scales) + _tensor_nbytes(self.zero_points)
+
+    def _spec(self) -> L.TensorSpec:
+        return L.TensorSpec(self.bits, L.GKV_AFFINE if self.zero_points is not None else L.GKV_SYMMETRIC,
+                            L.GKV_AXIS_TOKEN if self.axis == 2 else L.GKV_AXIS_CHANNEL, self.group_size,
+                            L.GKV_ROT_HADAMARD if self.rotation == "hadamard" else L.GKV_ROT_NONE,
+                            1 if self.packed else 0, L.DTYPE_CODE[self.scales.dtype], 0)
+
+    def dequantize(self) -> torch.Tensor:
+        """The dequantized tier tensor ``original_shape`` (core.py:153-173)."""
+        lib = L.lib()
+        B, H, n, D = self.original_shape
+        dev = self.q.device
+        plan = L.Plan()
+        plan.batch, plan.head_dim, plan.seq_len = B, D, n
+        plan.dtype = L.DTYPE_CODE[self.original_dtype]
+        plan.n_retained, plan.n_standard, plan.n_cold = 0, n, 0
+        ident = torch.arange(n, dtype=torch.int32, device=dev)
+        plan.idx_standard = ident.data_ptr()
+        for slot in (L.STD_K, L.STD_V):
+            plan.spec[slot] = self._spec()
+            plan.codes[slot] = self.q.data_ptr()
+            plan.scales[slot] = self.scales.data_ptr()
+            plan.zero_points[slot] = L.ptr(self.zero_points)
+        plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+        out = torch.empty((2, B, H, n, D), dtype=self.original_dtype, device=dev)
+        L.check(lib.gkv_dequantize(ctypes.byref(plan), B * H, out[0].data_ptr(), out[1].data_ptr(), None, 0,
+                                   L.stream_handle(dev)))
+        return out[0]
+
+
+@dataclass
+class QuantizedKvLayer:
+    """One quantized layer of a transformer KV cache (core.py:176-348)."""
+
+    compressed_keys: QuantizedTensor | None
+    compressed_values: QuantizedTensor | None
+    compressed_indices: torch.Tensor
+    retained_keys: torch.Tensor
+    retained_values: torch.Tensor
+    retained_indices: torch.Tensor
+    original_shape: tuple[int, ...]
+    seq_dim: int = 2
+    passthrough_keys: torch.Tensor | None = None
+    passthrough_values: torch.Tensor | None = None
+    low_priority_compressed_keys: QuantizedTensor | None = None
+    low_priority_compressed_values: QuantizedTensor | None = None
+    low_priority_compressed_indices: torch.Tensor | None = None
+    home_device: torch.device | None = None  # device of the input tensors (outputs return there)
+
+    def memory_bytes(self) -> int:
+        if self.passthrough_keys is not None and self.passthrough_values is not None:
+            return _tensor_nbytes(self.passthrough_keys) + _tensor_nbytes(self.passthrough_values)
+        n = 0
+        for t in (self.compressed_keys, self.compressed_values, self.low_priority_compressed_keys,
+                  self.low_priority_compressed_values):
+            if t is not None:
+                n += t.memory_bytes()
+        return (n + _tensor_nbytes(self.compressed_indices) + _tensor_nbytes(self.low_priority_compressed_indices)
+                + _tensor_nbytes(self.retained_keys) + _tensor_nbytes(self.retained_values)
+                + _tensor_nbytes(self.retained_indices))
+
+    def original_memory_bytes(self) -> int:
+        dtype = self.retained_keys.dtype
+        if self.passthrough_keys is not None:
+            dtype = self.passthrough_keys.dtype
+        if self.compressed_keys is not None:
+            dtype = self.compressed_keys.original_dtype
+        elements = 1
+        for dim in self.original_shape:
+            elements *= dim
+        return 2 * elements * _dtype_element_size(dtype)
+
+    def compression_ratio(self) -> float:
+        return self.original_memory_bytes() / max(self.memory_bytes(), 1)
+
+    def stats(self) -> dict[str, float]:
+        original_bytes = self.original_memory_bytes()
+        compressed_bytes = self.memory_bytes()
+        retained = self.retained_token_count()
+        compressed = self.compressed_token_count()
+        low = self.low_priority_token_count()
+        total = retained + compressed
+        return {
+            "original_bytes": float(original_bytes),
+            "compressed_bytes": float(compressed_bytes),
+            "compression_ratio": original_bytes / max(compressed_bytes, 1),
+            "retained_tokens": float(retained),
+            "compressed_tokens": float(compressed),
+            "standard_compressed_tokens": float(compressed - low),
+            "low_priority_tokens": float(low),
+            "retained_fraction": retained / max(total, 1),
+            "compressed_fraction": compressed / max(total, 1),
+        }
+
+    def retained_token_count(self) -> int:
+        if self.passthrough_keys is not None:
+            return self.original_shape[self.seq_dim]
+        return int(self.retained_indices.numel())
+
+    def compressed_token_count(self) -> int:
+        if self.passthrough_keys is not None:
+            return 0
+        return int(self.compressed_indices.numel()) + self.low_priority_token_count()
+
+    def low_priority_token_count(self) -> int:
+        if self.passthrough_keys is not None or self.low_priority_compressed_indices is None:
+            return 0
+        return int(self.low_priority_compressed_indices.numel())
+
+    def dequantize(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Keys and values ``[B, H, T, D]`` (core.py:265-307), on the input's device."""
+        if self.passthrough_keys is not None and self.passthrough_values is not None:
+            return self.passthrough_keys, self.passthrough_values
+        return _dequantize_layers([self])[0]
+
+    def report(self, original_keys: torch.Tensor, original_values: torch.Tensor) -> dict[str, float]:
+        """Fidelity report (core.py:309-323)."""
+        keys, values = self.dequantize()
+        original_bytes = _tensor_nbytes(original_keys) + _tensor_nbytes(original_values)
+        quantized_bytes = self.memory_bytes()
+        ok = original_keys.to(keys.device)
+        ov = original_values.to(values.device)
+        return {
+            "original_bytes": float(original_bytes),
+            "quantized_bytes": float(quantized_bytes),
+            "compression_ratio": original_bytes / max(quantized_bytes, 1),
+            "retained_tokens": float(self.retained_token_count()),
+            "compressed_tokens": float(self.compressed_token_count()),
+            "key_mse": float(F.mse_loss(keys.float(), ok.float()).cpu()),
+            "value_mse": float(F.mse_loss(values.float(), ov.float()).cpu()),
+            "key_cosine": _flat_cosine(keys, ok),
+            "value_cosine": _flat_cosine(values, ov),
+        }
+
+    def append(self, new_keys: torch.Tensor, new_values: torch.Tensor, config: KvQuantConfig,
+               importance_scores: torch.Tensor | None = None) -> "QuantizedKvLayer":
+        """Append tokens and requantize (core.py:325-348)."""
+        old_keys, old_values = self.dequantize()
+        if old_keys.shape[: self.seq_dim] != new_keys.shape[: self.seq_dim]:
+            raise ValueError("new_keys batch/head dimensions must match the cached layer.")
+        if old_keys.shape[self.seq_dim + 1:] != new_keys.shape[self.seq_dim + 1:]:
+            raise ValueError("new_keys head_dim dimensions must match the cached layer.")
+        if new_keys.shape != new_values.shape:
+            raise ValueError("new_keys and new_values must have the same shape.")
+        keys = torch.cat([old_keys, new_keys.to(old_keys.device)], dim=self.seq_dim)
+        values = torch.cat([old_values, new_values.to(old_values.device)], dim=self.seq_dim)
+        return quantize_kv_layer(keys, values, config, importance_scores=importance_scores)
+
+
+@dataclass
+class QuantizedKvCache:
+    layers: list[QuantizedKvLayer]
+
+    @classmethod
+    def from_past_key_values(
+        cls,
+        past_key_values: Sequence[tuple[torch.Tensor, torch.Tensor]],
+        config: KvQuantConfig,
+        importance_scores: Sequence[torch.Tensor] | torch.Tensor | None = None,
+    ) -> "QuantizedKvCache":
+        """core.py:355-369, batched: one selection and one quantize launch per run
+        of layers with the same geometry and scores."""
+        pairs = list(past_key_values)
+        per_layer = []
+        for layer_idx, (keys, values) in enumerate(pairs):
+            if isinstance(importance_scores, torch.Tensor) or importance_scores is None:
+                per_layer.append(importance_scores)
+            else:
+                per_layer.append(importance_scores[layer_idx])
+        return cls(_quantize_layers(pairs, config, per_layer))
+
+    def dequantize(self) -> tuple[tuple[torch.Tensor, torch.Tensor], ...]:
+        return tuple(_dequantize_layers(self.layers))
+
+    def memory_bytes(self) -> int:
+        return sum(layer.memory_bytes() for layer in self.layers)
+
+    def original_memory_bytes(self) -> int:
+        return sum(layer.original_memory_bytes() for layer in self.layers)
+
+    def compression_ratio(self) -> float:
+        return self.original_memory_bytes() / max(self.memory_bytes(), 1)
+
+    def retained_token_count(self) -> int:
+        return sum(layer.retained_token_count() for layer in self.layers)
+
+    def compressed_token_count(self) -> int:
+        return sum(layer.compressed_token_count() for layer in self.layers)
+
+    def low_priority_token_count(self) -> int:
+        return sum(layer.low_priority_token_count() for layer in self.layers)
+
+    def stats(self) -> dict[str, float]:
+        """core.py:392-413."""
+        original_bytes = self.original_memory_bytes()
+        compressed_bytes = self.memory_bytes()
+        retained = self.retained_token_count()
+        compressed = self.compressed_token_count()
+        low = self.low_priority_token_count()
+        total = retained + compressed
+        ratios = [layer.compression_ratio() for layer in self.layers]
+        return {
+            "layers": float(len(self.layers)),
+            "original_bytes": float(original_bytes),
+            "compressed_bytes": float(compressed_bytes),
+            "compression_ratio": original_bytes / max(compressed_bytes, 1),
+            "retained_tokens": float(retained),
+            "compressed_tokens": float(compressed),
+            "standard_compressed_tokens": float(compressed - low),
+            "low_priority_tokens": float(low),
+            "retained_fraction": retained / max(total, 1),
+            "compressed_fraction": compressed / max(total, 1),
+            "min_layer_compression_ratio": min(ratios, default=0.0),
+            "max_layer_compression_ratio": max(ratios, default=0.0),
+        }
+
+    def layer_stats(self) -> tuple[dict[str, float], ...]:
+        return tuple(layer.stats() for layer in self.layers)
+
+    def append(self, new_past_key_values: Sequence[tuple[torch.Tensor, torch.Tensor]], config: KvQuantConfig,
+               importance_scores: Sequence[torch.Tensor] | torch.Tensor | None = None) -> "QuantizedKvCache":
+        """core.py:418-433: dequantize, concatenate, requantize (batched)."""
+        if len(new_past_key_values) != len(self.layers):
+            raise ValueError("new_past_key_values must have one (key, value) pair per cached layer.")
+        old = self.dequantize()
+        pairs = []
+        for (ok, ov), (nk, nv), layer in zip(old, new_past_key_values, self.layers):
+            if ok.shape[:2] != nk.shape[:2]:
+                raise ValueError("new_keys batch/head dimensions must match the cached layer.")
+            if ok.shape[3:] != nk.shape[3:]:
+                raise ValueError("new_keys head_dim dimensions must match the cached layer.")
+            if nk.shape != nv.shape:
+                raise ValueError("new_keys and new_values must have the same shape.")
+            pairs.append((torch.cat([ok, nk.to(ok.device)], dim=2), torch.cat([ov, nv.to(ov.device)], dim=2)))
+        return QuantizedKvCache.from_past_key_values(pairs, config, importance_scores)
+
+    @classmethod
+    def from_hf_cache(cls, cache: object, config: KvQuantConfig,
+                      importance_scores: Sequence[torch.Tensor] | torch.Tensor | None = None,
+                      cache_role: Literal["self", "cross"] = "self") -> "QuantizedKvCache":
+        return cls.from_past_key_values(hf_cache_to_tuple(cache, cache_role=cache_role), config, importance_scores)
+
+    def to_legacy_cache(self) -> tuple[tuple[torch.Tensor, torch.Tensor], ...]:
+        return self.dequantize()
+
+    def to_hf_cache(self, implementation: Literal["dynamic", "static", "sliding_window", "legacy"] = "dynamic", *,
+                    config: object | None = None, max_cache_len: int | None = None) -> object:
+        """core.py:450-470."""
+        if implementation == "legacy":
+            return self.to_legacy_cache()
+        if implementation == "dynamic":
+            return self.to_hf_dynamic_cache(config=config)
+        if implementation in {"static", "sliding_window"}:
+            return self._to_hf_positioned_cache(implementation, config=config, max_cache_len=max_cache_len)
+        raise ValueError("implementation must be 'dynamic', 'static', 'sliding_window', or 'legacy'.")
+
+    def to_hf_dynamic_cache(self, *, config: object | None = None) -> object:
+        """core.py:472-481.  A plain ``DynamicLayer`` receives the dequantized
+        tensors directly (its ``update`` would concatenate them onto an empty
+        tensor, a full copy with the same result); other layer types go through
+        ``update``."""
+        try:
+            from transformers.cache_utils import DynamicCache, DynamicLayer
+        except ImportError as exc:
+            raise RuntimeError("transformers is required to build a DynamicCache.") from exc
+        cache = DynamicCache(config=config)
+        for layer_idx, (keys, values) in enumerate(self.dequantize()):
+            if not getattr(cache, "offloading", False) and getattr(cache, "layer_class_to_replicate", None) is not None:
+                while len(cache.layers) <= layer_idx:
+                    cache.layers.append(cache.layer_class_to_replicate())
+            target = cache.layers[layer_idx] if layer_idx < len(cache.layers) else None
+            if (type(target) is DynamicLayer and not getattr(target, "is_initialized", True)
+                    and not getattr(cache, "offloading", False)):
+                target.lazy_initialization(keys, values)
+                target.keys = keys
+                target.values = values
+            else:
+                cache.update(keys, values, layer_idx)
+        return cache
+
+    def _to_hf_positioned_cache(self, implementation: Literal["static", "sliding_window"], *,
+                                config: object | None, max_cache_len: int | None) -> object:
+        """core.py:483-508 (same imports, checks and update calls)."""
+        if config is None:
+            raise ValueError("config is required for static or sliding_window HF cache export.")
+        try:
+            from transformers.cache_utils import SlidingWindowCache, StaticCache
+        except ImportError as exc:
+            raise RuntimeError("transformers is required to build a positioned cache.") from exc
+        dequantized = self.dequantize()
+        required = max((keys.shape[2] for keys, _ in dequantized), default=0)
+        if max_cache_len is None:
+            max_cache_len = required
+        if max_cache_len < required:
+            raise ValueError("max_cache_len must be at least the longest KV sequence length.")
+        cache_cls = StaticCache if implementation == "static" else SlidingWindowCache
+        cache = cache_cls(config, max_cache_len=max_cache_len)
+        for layer_idx, (keys, values) in enumerate(dequantized):
+            positions = torch.arange(keys.shape[2], device=keys.device, dtype=torch.long)
+            cache.update(keys, values, layer_idx, cache_kwargs={"cache_position": positions})
+        return cache
+
+
+# ---------------------------------------------------------------------------
+# HF cache extraction (core.py:511-592)
+# ---------------------------------------------------------------------------
+
+def hf_cache_to_tuple(cache: object, *, cache_role: Literal["self", "cross"] = "self"
+                      ) -> tuple[tuple[torch.Tensor, torch.Tensor], ...]:
+    """Extract ``(keys, values)`` tuples from legacy or modern HF caches."""
+    if hasattr(cache, "self_attention_cache") or hasattr(cache, "cross_attention_cache"):
+        if cache_role == "self":
+            selected = getattr(cache, "self_attention_cache", None)
+        elif cache_role == "cross":
+            selected = getattr(cache, "cross_attention_cache", None)
+        else:
+            raise ValueError("cache_role must be 'self' or 'cross'.")
+        if selected is None:
+            raise TypeError(f"HF encoder-decoder cache has no {cache_role!r} attention cache.")
+        return hf_cache_to_tuple(selected)
+    if isinstance(cache, (tuple, list)):
+        layers = []
+        for layer in cache:
+            if layer is None:
+                continue
+            if not isinstance(layer, (tuple, list)) or len(layer) < 2:
+                raise TypeError("Legacy cache layers must be tuples/lists with at least key and value tensors.")
+            keys, values = layer[0], layer[1]
+            if keys is None or values is None:
+                continue
+            layers.append((keys, values))
+        return tuple(layers)
+    layers = getattr(cache, "layers", None)
+    if layers is not None:
+        extracted = []
+        for layer in layers:
+            keys = getattr(layer, "keys", None)
+            values = getattr(layer, "values", None)
+            if keys is None or values is None:
+                continue
+            seq_len = _cache_layer_seq_length(layer, keys)
+            if seq_len == 0:
+                continue
+            if seq_len < keys.shape[2]:
+                keys = keys.narrow(2, 0, seq_len).contiguous()
+                values = values.narrow(2, 0, seq_len).contiguous()
+            extracted.append((keys, values))
+        return tuple(extracted)
+    key_cache = getattr(cache, "key_cache", None)
+    value_cache = getattr(cache, "value_cache", None)
+    if key_cache is not None and value_cache is not None:
+        return tuple((k, v) for k, v in zip(key_cache, value_cache) if k is not None and v is not None)
+    raise TypeError(f"Unsupported cache type: {type(cache)!r}")
+
+
+def _cache_layer_seq_length(layer: object, keys: torch.Tensor) -> int:
+    if "dynamic" in type(layer).__name__.lower():
+        return keys.shape[2]
+    seq_len = None
+    get_seq_length = getattr(layer, "get_seq_length", None)
+    if callable(get_seq_length):
+        try:
+            seq_len = get_seq_length()
+        except TypeError:
+            seq_len = None
+    if seq_len is None:
+        seq_len = getattr(layer, "cumulative_length", None)
+    if seq_len is None:
+        return keys.shape[2]
+    if isinstance(seq_len, torch.Tensor):
+        if seq_len.numel() == 0:
+            return 0
+        seq_len = int(seq_len.max().item())
+    else:
+        seq_len = int(seq_len)
+    return min(max(seq_len, 0), keys.shape[2])
+
+
+# ---------------------------------------------------------------------------
+# selection helpers with the reference's signatures
+# ---------------------------------------------------------------------------
+
+def _normalize_token_scores(seq_len: int, scores: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """core.py:1019-1031 (computed on ``device``)."""
+    scores = scores.to(device=device, dtype=torch.float32)
+    if scores.numel() == seq_len:
+        return scores.reshape(seq_len)
+    if scores.ndim >= 1 and scores.shape[-1] == seq_len:
+        return scores.reshape(-1, seq_len).mean(dim=0)
+    if scores.ndim >= 1 and scores.shape[0] == seq_len:
+        return scores.reshape(seq_len, -1).mean(dim=1)
+    raise ValueError("importance_scores must have one score per token or a final token dimension.")
+
+
+def _select(T: int, config: KvQuantConfig, scores: torch.Tensor | None, device: torch.device,
+            outlier: torch.Tensor | None = None, tiers: TierSizes | None = None):
+    """Run the selection kernel; returns (tiers, idx_ret, idx_std, idx_cold) int32 device tensors."""
+    lib = L.lib()
+    tiers = tiers or resolve_tiers(config, T, scores is not None)
+    s = None
+    if scores is not None:
+        s = _normalize_token_scores(T, scores, device).contiguous()
+    idx = torch.empty(T, dtype=torch.int32, device=device)
+    idx_ret, idx_std, idx_cold = torch.split(idx, [tiers.n_retained, tiers.n_standard, tiers.n_cold])
+    ws = torch.empty(max(int(lib.gkv_select_workspace_bytes(T)), 1), dtype=torch.uint8, device=device)
+    pol = tiers.policy()
+    L.check(lib.gkv_select_tiers(L.ptr(s), L.ptr(outlier), ctypes.byref(pol), idx_ret.data_ptr(),
+                                 idx_std.data_ptr(), idx_cold.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 L.stream_handle(device)))
+    return tiers, idx_ret, idx_std, idx_cold
+
+
+def build_retention_mask(seq_len: int, config: KvQuantConfig, importance_scores: torch.Tensor | None = None,
+                         device: torch.device | None = None) -> torch.Tensor:
+    """Token mask for full-precision retention (core.py:595-644): sink, tail and
+    top importance scores, computed by the selection kernel."""
+    config.validate()
+    if device is None:
+        device = importance_scores.device if importance_scores is not None else torch.device("cpu")
+    device = torch.device(device)
+    cdev = device if device.type == "cuda" else _compute_device(torch.empty(0))
+    no_outlier = KvQuantConfig(**{**config.__dict__, "outlier_protection_ratio": 0.0, "min_outlier_tokens": 0,
+                                  "low_priority_ratio": 0.0, "long_low_priority_ratio": None,
+                                  "min_low_priority_tokens": 0})
+    _, idx_ret, _, _ = _select(seq_len, no_outlier, importance_scores, cdev)
+    mask = torch.zeros(seq_len, dtype=torch.bool, device=cdev)
+    mask[idx_ret.long()] = True
+    return mask.to(device)
+
+
+def chunk_scores_to_token_scores(seq_len: int, chunk_spans: Iterable[tuple[int, int]], chunk_scores: torch.Tensor,
+                                 device: torch.device | None = None) -> torch.Tensor:
+    """Spread chunk-level scores over token positions (core.py:775-797): max over
+    the covering chunks, 0 for uncovered tokens."""
+    if device is None:
+        device = chunk_scores.device
+    token_scores = torch.full((seq_len,), -torch.inf, dtype=torch.float32, device=device)
+    scores = chunk_scores.to(device=device, dtype=torch.float32).flatten()
+    for idx, (start, end) in enumerate(chunk_spans):
+        if idx >= scores.numel():
+            break
+        lo, hi = max(0, int(start)), min(seq_len, int(end))
+        if hi <= lo:
+            continue
+        token_scores[lo:hi] = torch.maximum(token_scores[lo:hi], scores[idx])
+    return torch.nan_to_num(token_scores, neginf=0.0)
+
+
+# ---------------------------------------------------------------------------
+# quantize orchestration
+# ---------------------------------------------------------------------------
+
+def _check_pair(keys: torch.Tensor, values: torch.Tensor) -> None:
+    if keys.shape != values.shape:
+        raise ValueError("keys and values must have the same shape.")
+    if keys.ndim != 4:
+        raise ValueError("keys and values must use [batch, heads, tokens, head_dim] layout.")
+    if keys.dtype not in L.DTYPE_CODE or values.dtype != keys.dtype:
+        raise ValueError("keys and values must be float32, float16 or bfloat16 tensors of one dtype.")
+
+
+def _full_precision_layer(keys: torch.Tensor, values: torch.Tensor, seq_dim: int = 2) -> QuantizedKvLayer:
+    """core.py:959-976."""
+    empty_indices = torch.empty(0, dtype=torch.int32, device=keys.device)
+    shape = list(keys.shape)
+    shape[seq_dim] = 0
+    return QuantizedKvLayer(compressed_keys=None, compressed_values=None, compressed_indices=empty_indices,
+                            retained_keys=keys.new_empty(tuple(shape)), retained_values=values.new_empty(tuple(shape)),
+                            retained_indices=empty_indices, original_shape=tuple(keys.shape), seq_dim=seq_dim,
+                            passthrough_keys=keys.detach().contiguous(),
+                            passthrough_values=values.detach().contiguous(), home_device=keys.device)
+
+
+class _Arena:
+    """One uint8 device allocation carved into 256-byte aligned regions."""
+
+    def __init__(self):
+        self.sizes = []
+
+    def reserve(self, nbytes: int) -> int:
+        self.sizes.append(nbytes)
+        return len(self.sizes) - 1
+
+    def allocate(self, device: torch.device):
+        offs, off = [], 0
+        for n in self.sizes:
+            offs.append(off)
+            off += (n + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.buf = torch.empty(max(off, 1), dtype=torch.uint8, device=device)
+        self.offs = offs
+
+    def view(self, handle: int, start: int, nbytes: int, dtype: torch.dtype, shape: tuple) -> torch.Tensor:
+        o = self.offs[handle] + start
+        return self.buf.narrow(0, o, nbytes).view(dtype).view(shape)
+
+    def ptr(self, handle: int) -> int:
+        return self.buf.data_ptr() + self.offs[handle]
+
+
+def _quantize_layers(pairs, config: KvQuantConfig, per_layer_scores) -> list[QuantizedKvLayer]:
+    config.validate()
+    for keys, values in pairs:
+        _check_pair(keys, values)
+    out: list[QuantizedKvLayer] = []
+    i = 0
+    while i < len(pairs):
+        k0 = pairs[i][0]
+        s0 = per_layer_scores[i]
+        j = i + 1
+        while (j < len(pairs) and pairs[j][0].shape == k0.shape and pairs[j][0].dtype == k0.dtype
+               and pairs[j][0].device == k0.device and per_layer_scores[j] is s0):
+            j += 1
+        out.extend(_quantize_group(pairs[i:j], config, s0))
+        i = j
+    return out
+
+
+def _layer_input(keys: torch.Tensor, values: torch.Tensor) -> L.LayerIn:
+    li = L.LayerIn()
+    li.k, li.v = keys.data_ptr(), values.data_ptr()
+    for q in range(3):
+        li.k_stride[q] = keys.stride(q)
+        li.v_stride[q] = values.stride(q)
+    li.heads = keys.shape[1]
+    return li
+
+
+def _quantize_group(pairs, config: KvQuantConfig, scores, retain_mask: torch.Tensor | None = None
+                    ) -> list[QuantizedKvLayer]:
+    """Compress layers of one geometry sharing one scores tensor."""
+    k0 = pairs[0][0]
+    shape = tuple(k0.shape)
+    B, H, T, D = shape
+    dtype = k0.dtype
+    home = k0.device
+    device = _compute_device(k0)
+    outlier_needed = config.outlier_protection_ratio > 0.0 or config.min_outlier_tokens > 0
+    if retain_mask is None and outlier_needed and len(pairs) > 1:
+        # outlier scores differ per layer, so each layer has its own selection
+        return [lay for p in pairs for lay in _quantize_group([p], config, scores)]
+
+    # inputs on the compute device with a contiguous head_dim
+    dev_pairs = []
+    for keys, values in pairs:
+        keys = _to_device(keys.detach(), device)
+        values = _to_device(values.detach(), device)
+        if keys.stride(3) != 1:
+            keys = keys.contiguous()
+        if values.stride(3) != 1:
+            values = values.contiguous()
+        dev_pairs.append((keys, values))
+
+    if retain_mask is not None:
+        tiers, idx_ret, idx_std, idx_cold = _tiers_from_mask(retain_mask, T, config, scores, device)
+    else:
+        tiers = resolve_tiers(config, T, scores is not None)
+        idx_ret = idx_std = idx_cold = None
+    plans = tensor_plans(config, shape, tiers)
+    if config.skip_if_not_smaller and \
+            layer_memory_bytes(shape, dtype, tiers, plans) >= 2 * B * H * T * D * _dtype_element_size(dtype):
+        return [_full_precision_layer(k.detach(), v.detach()) for k, v in pairs]
+    if len(pairs) > 1 and any(p is not None and not p.slice_bits_aligned for p in plans):
+        return [lay for p in pairs for lay in _quantize_group([p], config, scores)]
+
+    lib = L.lib()
+    if idx_ret is None:
+        outlier = None
+        if tiers.keep_outlier > 0:
+            outlier = torch.empty(T, dtype=torch.float32, device=device)
+            li = _layer_input(*dev_pairs[0])
+            L.check(lib.gkv_outlier_scores(ctypes.byref(li), B, T, D, L.DTYPE_CODE[dtype], outlier.data_ptr(),
+                                           L.stream_handle(device)))
+        tiers, idx_ret, idx_std, idx_cold = _select(T, config, scores, device, outlier, tiers)
+
+    nl = len(dev_pairs)
+    esize = _dtype_element_size(dtype)
+    ar = _Arena()
+    h_ret = [ar.reserve(nl * B * H * tiers.n_retained * D * esize) for _ in range(2)]
+    h_codes, h_scales, h_zps = [None] * 4, [None] * 4, [None] * 4
+    for i, p in enumerate(plans):
+        if p is None:
+            continue
+        h_codes[i] = ar.reserve(nl * p.code_bytes)
+        h_scales[i] = ar.reserve(nl * p.n_groups * _dtype_element_size(p.scale_dtype))
+        if p.quantizer == "affine":
+            h_zps[i] = ar.reserve(nl * p.n_groups)
+    ar.allocate(device)
+
+    plan = L.Plan()
+    plan.batch, plan.head_dim, plan.seq_len, plan.dtype = B, D, T, L.DTYPE_CODE[dtype]
+    plan.n_retained, plan.n_standard, plan.n_cold = tiers.n_retained, tiers.n_standard, tiers.n_cold
+    plan.idx_retained, plan.idx_standard, plan.idx_cold = idx_ret.data_ptr(), idx_std.data_ptr(), idx_cold.data_ptr()
+    plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+    plan.retained_k, plan.retained_v = ar.ptr(h_ret[0]), ar.ptr(h_ret[1])
+    for i, p in enumerate(plans):
+        if p is None:
+            continue
+        plan.spec[i] = p.spec()
+        plan.codes[i] = ar.ptr(h_codes[i])
+        plan.scales[i] = ar.ptr(h_scales[i])
+        plan.zero_points[i] = ar.ptr(h_zps[i]) if h_zps[i] is not None else 0
+    layer_ins = (L.LayerIn * nl)(*[_layer_input(k, v) for k, v in dev_pairs])
+    ws_bytes = int(lib.gkv_quantize_workspace_bytes(ctypes.byref(plan), layer_ins, nl))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+    L.check(lib.gkv_quantize(ctypes.byref(plan), layer_ins, nl, ws.data_ptr(), ws_bytes, L.stream_handle(device)))
+
+    layers = []
+    ret_shape = (B, H, tiers.n_retained, D)
+    ret_bytes = B * H * tiers.n_retained * D * esize
+    for l in range(nl):
+        qts = []
+        for i, p in enumerate(plans):
+            if p is None:
+                qts.append(None)
+                continue
+            ssize = _dtype_element_size(p.scale_dtype)
+            q_dtype = torch.uint8 if (p.packed or p.quantizer == "affine") else torch.int8
+            q_shape_store = (p.code_bytes,) if p.packed else p.q_shape
+            q = ar.view(h_codes[i], l * p.code_bytes, p.code_bytes, q_dtype, q_shape_store)
+            sc = ar.view(h_scales[i], l * p.n_groups * ssize, p.n_groups * ssize, p.scale_dtype, p.scales_shape)
+            zp = None
+            if h_zps[i] is not None:
+                zp = ar.view(h_zps[i], l * p.n_groups, p.n_groups, torch.uint8, p.scales_shape)
+            qts.append(QuantizedTensor(q=q, scales=sc, zero_points=zp, original_shape=(B, H, p.n, D), axis=p.axis,
+                                       group_size=p.group_size, bits=p.bits, padded=p.padded, q_shape=p.q_shape,
+                                       original_dtype=dtype, packed=p.packed,
+                                       packed_offset=0 if p.quantizer == "affine" else -(1 << (p.bits - 1)),
+                                       rotation=p.rotation))
+        layers.append(QuantizedKvLayer(
+            compressed_keys=qts[0], compressed_values=qts[1], compressed_indices=idx_std,
+            retained_keys=ar.view(h_ret[0], l * ret_bytes, ret_bytes, dtype, ret_shape),
+            retained_values=ar.view(h_ret[1], l * ret_bytes, ret_bytes, dtype, ret_shape),
+            retained_indices=idx_ret, original_shape=shape, seq_dim=2,
+            low_priority_compressed_keys=qts[2], low_priority_compressed_values=qts[3],
+            low_priority_compressed_indices=idx_cold, home_device=home))
+    return layers
+
+
+def _tiers_from_mask(retain_mask: torch.Tensor, T: int, config: KvQuantConfig, scores, device):
+    """Tiers of a caller-supplied retention mask (core.py:680-719).  The cold tier
+    among the remaining tokens follows the same rule as the selection kernel
+    (smallest scores, lower position first among equals)."""
+    mask = retain_mask.to(device=device, dtype=torch.bool)
+    if mask.numel() != T:
+        raise ValueError("retain_mask must have one value per token.")
+    mask = mask.reshape(T)
+    positions = torch.arange(T, device=device, dtype=torch.int32)
+    cold = torch.zeros(T, dtype=torch.bool, device=device)
+    compressed = ~mask
+    n_comp = int(compressed.sum().item())
+    ratio = effective_low_priority_ratio(config, T)
+    if (scores is not None and T >= config.low_priority_min_context
+            and (ratio > 0.0 or config.min_low_priority_tokens > 0)
+            and (config.low_priority_bits is not None or config.low_priority_key_bits is not None
+                 or config.low_priority_value_bits is not None) and n_comp > 0):
+        keep = keep_count(n_comp, ratio, config.min_low_priority_tokens)
+        if keep > 0:
+            s = _normalize_token_scores(T, scores, device)
+            cand = positions[compressed]
+            order = torch.sort(s[cand.long()], stable=True).indices[:keep]
+            cold[cand[order].long()] = True
+    standard = compressed & ~cold
+    idx_ret, idx_std, idx_cold = positions[mask], positions[standard], positions[cold]
+    n_ret, n_std, n_cold = idx_ret.numel(), idx_std.numel(), idx_cold.numel()
+    tiers = TierSizes(T, 0, 0, 0, 0, n_cold, n_ret, n_std, n_cold)
+    return tiers, idx_ret.contiguous(), idx_std.contiguous(), idx_cold.contiguous()
+
+
+def quantize_kv_layer(keys: torch.Tensor, values: torch.Tensor, config: KvQuantConfig,
+                      importance_scores: torch.Tensor | None = None,
+                      retain_mask: torch.Tensor | None = None) -> QuantizedKvLayer:
+    """Quantize one layer of KV tensors with layout [B, H, T, D] (core.py:647-772)."""
+    config.validate()
+    _check_pair(keys, values)
+    return _quantize_group([(keys, values)], config, importance_scores, retain_mask=retain_mask)[0]
+
+
+# ---------------------------------------------------------------------------
+# dequantize orchestration
+# ---------------------------------------------------------------------------
+
+def _layer_tensors(layer: QuantizedKvLayer):
+    return (layer.compressed_keys, layer.compressed_values, layer.low_priority_compressed_keys,
+            layer.low_priority_compressed_values)
+
+
+def _storage_list(layer: QuantizedKvLayer):
+    out = [layer.retained_keys, layer.retained_values]
+    for t in _layer_tensors(layer):
+        if t is not None:
+            out.extend([t.q, t.scales] + ([t.zero_points] if t.zero_points is not None else []))
+    return out
+
+
+def _signature(layer: QuantizedKvLayer):
+    specs = tuple(None if t is None else (bytes(t._spec()), t.q.dtype, t.q_shape) for t in _layer_tensors(layer))
+    lp = layer.low_priority_compressed_indices
+    return (layer.original_shape, layer.retained_keys.dtype, layer.retained_keys.device, specs,
+            layer.retained_indices.data_ptr(), layer.compressed_indices.data_ptr(),
+            lp.data_ptr() if lp is not None else 0, layer.home_device)
+
+
+def _follows(a: QuantizedKvLayer, b: QuantizedKvLayer) -> bool:
+    """True when b's storage directly follows a's in every region (same arena run)."""
+    if _signature(a) != _signature(b):
+        return False
+    for x, y in zip(_storage_list(a), _storage_list(b)):
+        if not (x.is_contiguous() and y.is_contiguous()) or y.data_ptr() != x.data_ptr() + _tensor_nbytes(x):
+            return False
+    return True
+
+
+def _dequantize_layers(layers: list[QuantizedKvLayer]) -> list:
+    out = []
+    i = 0
+    while i < len(layers):
+        lay = layers[i]
+        if lay.passthrough_keys is not None and lay.passthrough_values is not None:
+            out.append((lay.passthrough_keys, lay.passthrough_values))
+            i += 1
+            continue
+        j = i + 1
+        while j < len(layers) and layers[j].passthrough_keys is None and _follows(layers[j - 1], layers[j]):
+            j += 1
+        out.extend(_dequantize_run(layers[i:j]))
+        i = j
+    if any(o[0].device.type == "cpu" for o in out):
+        torch.cuda.synchronize()
+    return out
+
+
+def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
+    """One launch for consecutive layers of one arena; returns [(K, V), ...]."""
+    lib = L.lib()
+    first = run[0]
+    B, H, T, D = first.original_shape
+    qts = _layer_tensors(first)
+    ref = next((t for t in qts if t is not None), None)
+    dtype = ref.original_dtype if ref is not None else first.retained_keys.dtype
+    dev = ref.q.device if ref is not None else first.retained_keys.device
+    plan = L.Plan()
+    plan.batch, plan.head_dim, plan.seq_len, plan.dtype = B, D, T, L.DTYPE_CODE[dtype]
+    lp = first.low_priority_compressed_indices
+    plan.n_retained = first.retained_indices.numel()
+    plan.n_standard = first.compressed_indices.numel()
+    plan.n_cold = lp.numel() if lp is not None else 0
+    plan.idx_retained = first.retained_indices.data_ptr()
+    plan.idx_standard = first.compressed_indices.data_ptr()
+    plan.idx_cold = lp.data_ptr() if lp is not None else 0
+    plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+    plan.retained_k, plan.retained_v = first.retained_keys.data_ptr(), first.retained_values.data_ptr()
+    for i, t in enumerate(qts):
+        if t is None:
+            continue
+        plan.spec[i] = t._spec()
+        plan.codes[i] = t.q.data_ptr()
+        plan.scales[i] = t.scales.data_ptr()
+        plan.zero_points[i] = L.ptr(t.zero_points)
+    nl = len(run)
+    outk = torch.empty((nl, B, H, T, D), dtype=dtype, device=dev)
+    outv = torch.empty((nl, B, H, T, D), dtype=dtype, device=dev)
+    L.check(lib.gkv_dequantize(ctypes.byref(plan), nl * B * H, outk.data_ptr(), outv.data_ptr(), None, 0,
+                               L.stream_handle(dev)))
+    home = first.home_device
+    if home is not None and home.type == "cpu":
+        hk = torch.empty(outk.shape, dtype=dtype, pin_memory=True)
+        hv = torch.empty(outv.shape, dtype=dtype, pin_memory=True)
+        hk.copy_(outk, non_blocking=True)
+        hv.copy_(outv, non_blocking=True)
+        outk, outv = hk, hv
+    return [(outk[l], outv[l]) for l in range(nl)]
+
+
+# ---------------------------------------------------------------------------
+# diagnostics (core.py:800-845, 1010-1012)
+# ---------------------------------------------------------------------------
+
+def attention_from_kv(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                      mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Scaled dot-product attention for [B, H, Q, D] x [B, H, T, D] in fp32."""
+    if query.ndim != 4 or keys.ndim != 4 or values.ndim != 4:
+        raise ValueError("query, keys, and values must be rank-4 tensors.")
+    if keys.shape != values.shape:
+        raise ValueError("keys and values must have the same shape.")
+    if query.shape[:2] != keys.shape[:2] or query.shape[-1] != keys.shape[-1]:
+        raise ValueError("query and KV batch/head/head_dim dimensions must match.")
+    scores = query.float().matmul(keys.float().transpose(-2, -1)) / sqrt(query.size(-1))
+    if mask is not None:
+        scores = scores.masked_fill(~mask.to(device=scores.device, dtype=torch.bool), -1.0e9)
+    weights = F.softmax(scores, dim=-1)
+    return weights.matmul(values.float()), weights
+
+
+def attention_report(query: torch.Tensor, original_keys: torch.Tensor, original_values: torch.Tensor,
+                     quantized_layer: QuantizedKvLayer, mask: torch.Tensor | None = None) -> dict[str, float]:
+    """Attention output / weight drift caused by the compression."""
+    qk, qv = quantized_layer.dequantize()
+    dev = qk.device
+    oo, ow = attention_from_kv(query.to(dev), original_keys.to(dev), original_values.to(dev), mask)
+    qo, qw = attention_from_kv(query.to(dev), qk, qv, mask)
+    kl = (ow.clamp_min(1.0e-9) * (ow.clamp_min(1.0e-9).log() - qw.clamp_min(1.0e-9).log())).sum(dim=-1).mean()
+    return {
+        "attention_output_mse": float(F.mse_loss(qo, oo).cpu()),
+        "attention_output_cosine": _flat_cosine(qo, oo),
+        "attention_output_max_abs": float((qo - oo).abs().max().cpu()),
+        "attention_weight_kl": float(kl.cpu()),
+    }
+
+
+def _flat_cosine(a: torch.Tensor, b: torch.Tensor) -> float:
+    return float(F.cosine_similarity(a.float().flatten(), b.float().flatten(), dim=0).cpu())
