@@ -1,0 +1,428 @@
+#!/usr/bin/env python
+"""Throughput of the GraphKV compression path on B200: quantize+pack and
+dequant of a Qwen2.5-7B-shaped 32k-token bf16 cache (28 layers x 4 kv-heads x
+head_dim 128, graphkv profile with importance scores: sink/tail/top-1% kept,
+symmetric int4, 35% cold tier with Hadamard-rotated int2 values).
+
+One step = selection + quantize+pack of the whole cache, then dequant of the
+whole cache back to [B, H, T, D] bf16.  ``value`` is GB/s of input cache
+(K+V bytes) per step with inputs resident in HBM; ``phases`` gives each phase
+against the HBM roofline (algorithmic bytes = bytes read + bytes written).
+
+N GPUs (torchrun): weak scaling.  The global cache is the same model with batch
+N; its 28 x 4 (layer, kv-head) units are sharded contiguously over the ranks,
+each unit holding all N batch rows, so every rank compresses exactly the work
+of one 32k cache.  The only collective is an all-gather of the per-shard byte
+and token counts each step.
+
+``--impl reference`` times the CPU port of the reference algorithm (the numpy
+oracle) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = "qwen7b-32k"
+METRIC = "KV quant+pack and dequant GB/s (% HBM peak), Qwen2.5-7B-shape 32k cache"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=WORKLOAD)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle port on a bounded sample (process pool, spawn)
+# ---------------------------------------------------------------------------
+
+def _oracle_slice(args):
+    """Quantize + dequantize one (layer, head) slice with the numpy oracle."""
+    wkey, layer, head = args
+    import numpy as np  # noqa: F401
+
+    from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
+    from oracle import graphkv_oracle as orc
+
+    w = WORKLOADS[wkey]
+    k, v = make_layer(w, layer, heads=range(head, head + 1), batch=range(1))
+    s = make_scores(w)
+    K, V = k.float().numpy(), v.float().numpy()
+    sn = s.numpy() if s is not None else None
+    t0 = time.perf_counter()
+    ql = orc.quantize_layer(K, V, "bf16" if w.dtype.itemsize == 2 else "f32", orc.POLICIES[w.profile], sn)
+    orc.dequantize_layer(ql)
+    return time.perf_counter() - t0, 2 * K.size * w.dtype.itemsize
+
+
+def cpu_sample(wkey, n_slices, workers):
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    jobs = [(wkey, i % 28, (i // 28) % 4) for i in range(n_slices)]
+    with ctx.Pool(workers) as pool:
+        pool.map(_oracle_slice, jobs[:workers])  # import / page-in warm-up
+        t0 = time.perf_counter()
+        res = pool.map(_oracle_slice, jobs)
+        wall = time.perf_counter() - t0
+    nbytes = sum(r[1] for r in res)
+    return nbytes / wall / 1e9, wall, nbytes
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    workers = os.cpu_count() or 1
+    per_step = workers  # one (layer, head) slice of the 32k cache per worker per step
+    # size each step so the whole run stays within a few minutes (~0.65 s per slice round trip)
+    total_budget = 150.0
+    est = 0.65 * math.ceil(per_step / workers)
+    steps_total = args.steps + args.warmup
+    if est * steps_total > total_budget:
+        per_step = max(1, int(workers * total_budget / (0.65 * steps_total)))
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    times, nbytes = [], 0
+    with ctx.Pool(workers) as pool:
+        for step in range(steps_total):
+            jobs = [(args.workload, (step * per_step + i) % 28, ((step * per_step + i) // 28) % 4)
+                    for i in range(per_step)]
+            t0 = time.perf_counter()
+            res = pool.map(_oracle_slice, jobs)
+            dt = time.perf_counter() - t0
+            if step >= args.warmup:
+                times.append(dt)
+                nbytes += sum(r[1] for r in res)
+    total = sum(times)
+    value = nbytes / total / 1e9
+    sample = (f"{per_step} (layer, kv-head) slices [1, 1, 32768, 128] bf16 per step, one per process, "
+              f"quantize+pack then dequant with the numpy port of the reference algorithm")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / max(len(times), 1), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "device": "host CPU", "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": workers, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """NVML clocks and clock-event reasons sampled every 20 ms while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x1: "gpu_idle"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.ok = [], set(), False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            import torch
+
+            try:  # CUDA ordinal -> NVML index (honours CUDA_VISIBLE_DEVICES)
+                index = torch.cuda._get_nvml_device_index(index)
+            except Exception:
+                pass
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # NVML unavailable: report nothing rather than guess
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _run(self):
+        get_reasons = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = get_reasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def shard_units(layers, heads, world, rank):
+    """Contiguous range of (layer, kv-head) units of one rank -> [(layer, h0, h1), ...]."""
+    units = layers * heads
+    lo, hi = units * rank // world, units * (rank + 1) // world
+    out = []
+    u = lo
+    while u < hi:
+        l, h0 = divmod(u, heads)
+        h1 = min(heads, h0 + (hi - u))
+        out.append((l, h0, h1))
+        u += h1 - h0
+    return out
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(workload):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", f"dram_traffic_{workload}.txt")
+    out = {}
+    if os.path.exists(path):
+        for line in open(path):
+            parts = line.split()
+            if len(parts) == 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from dataclasses import replace
+
+    import graphkv_b200 as g
+    from graphkv_b200 import _lib
+    from graphkv_b200.config import layer_memory_bytes, resolve_tiers, tensor_plans
+    from graphkv_b200.engine import CompressionEngine
+    from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
+
+    w = WORKLOADS[args.workload]
+    wN = replace(w, batch=w.batch * world)
+    shard = shard_units(w.layers, w.heads, world, rank)
+    pairs = [make_layer(wN, l, device=str(dev), heads=range(h0, h1)) for (l, h0, h1) in shard]
+    scores = make_scores(w, device=str(dev))
+    cfg = g.get_profile(w.profile).config
+    in_bytes = sum(k.numel() * k.element_size() * 2 for k, _ in pairs)
+    comp_bytes = 0
+    for k, _ in pairs:
+        t = resolve_tiers(cfg, k.shape[2], scores is not None)
+        comp_bytes += layer_memory_bytes(tuple(k.shape), k.dtype, t, tensor_plans(cfg, tuple(k.shape), t))
+    eng = CompressionEngine(pairs, cfg, scores)
+    runs = eng.runs
+    launches = eng.launches_per_step()
+    stats_vec = torch.tensor([float(comp_bytes), float(in_bytes)], device=dev, dtype=torch.float64)
+    gathered = torch.empty(world * 2, device=dev, dtype=torch.float64)
+
+    stream = torch.cuda.current_stream(dev)
+    work = [(it[1], it[2], it[3]) for it in eng.items if it[0] == "run"]
+
+    def step(ev=None):
+        # ev[i] = 4 events per run: before select, after select, after quantize, after dequantize
+        for i, (run, s, needs_select) in enumerate(work):
+            if ev is not None:
+                ev[i][0].record(stream)
+            if needs_select:
+                run.select(s)
+            if ev is not None:
+                ev[i][1].record(stream)
+            run.quantize()
+            if ev is not None:
+                ev[i][2].record(stream)
+        for i, (run, _, _) in enumerate(work):
+            run.dequantize()
+            if ev is not None:
+                ev[i][3].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, stats_vec)
+
+    # warm-up
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert _lib.device_error() == 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+    nr = len(work)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nr)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for s in range(args.steps):
+            step(evs[s])
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    t_sel = t_q = t_dq = 0.0
+    for e in evs:
+        for i in range(nr):
+            t_sel += e[i][0].elapsed_time(e[i][1])
+            t_q += e[i][1].elapsed_time(e[i][2])
+            t_dq += (e[nr - 1][2] if i == 0 else e[i - 1][3]).elapsed_time(e[i][3])
+    if world > 1:
+        t = torch.tensor([elapsed_ms, t_sel, t_q, t_dq], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, t_sel, t_q, t_dq = (float(x) for x in t.tolist())
+    assert _lib.device_error() == 0
+
+    # end to end through the public API with host (pinned) buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        host_pairs = []
+        for k, v in pairs:
+            hk = torch.empty(k.shape, dtype=k.dtype, pin_memory=True)
+            hv = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+            hk.copy_(k)
+            hv.copy_(v)
+            host_pairs.append((hk, hv))
+        del eng, runs, work
+        torch.cuda.empty_cache()
+        host_scores = scores.cpu()
+        out = g.quantize_hf_cache(tuple(host_pairs), w.profile, importance_scores=host_scores, output="legacy")
+        del out
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            out = g.quantize_hf_cache(tuple(host_pairs), w.profile, importance_scores=host_scores, output="legacy")
+            torch.cuda.synchronize(dev)
+            del out
+        if world > 1:
+            dist.barrier()
+        e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e = {"value": round(world * in_bytes / e2e_s / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": in_bytes + 4 * w.seq, "d2h_bytes_per_step": in_bytes,
+               "ms_per_step": round(1e3 * e2e_s, 3), "steps": args.e2e_steps,
+               "path": "quantize_hf_cache(host pinned legacy cache, output='legacy') -> host tensors"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    ms = elapsed_ms / args.steps
+    peak, peak_kind = measured_peak()
+    q_ms, dq_ms, sel_ms = t_q / args.steps, t_dq / args.steps, t_sel / args.steps
+    algo_q = in_bytes + comp_bytes
+    algo_dq = comp_bytes + in_bytes
+    phases = {
+        "select": {"ms": round(sel_ms, 4)},
+        "quantize": {"ms": round(q_ms, 4), "input_gbs": round(in_bytes / q_ms / 1e6, 1),
+                     "algo_gbs": round(algo_q / q_ms / 1e6, 1), "frac": round(algo_q / q_ms / 1e6 / peak, 4)},
+        "dequant": {"ms": round(dq_ms, 4), "input_gbs": round(in_bytes / dq_ms / 1e6, 1),
+                    "algo_gbs": round(algo_dq / dq_ms / 1e6, 1), "frac": round(algo_dq / dq_ms / 1e6 / peak, 4)},
+    }
+    dominant = "quantize" if q_ms >= dq_ms else "dequant"
+    dom_ms = (q_ms if dominant == "quantize" else dq_ms) / nr
+    dom_bytes = (algo_q if dominant == "quantize" else algo_dq) / nr
+    achieved = dom_bytes / dom_ms / 1e6
+    traffic = committed_traffic(args.workload).get(dominant)
+    roofline = {"bound": "hbm", "kernel": "quantize_tile_kernel" if dominant == "quantize" else "dequantize_tile_kernel",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+                "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        workers = os.cpu_count() or 1
+        gbs, wall, nb = cpu_sample(args.workload, workers * 2, workers)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": workers, "kind": "port",
+               "sample": f"{workers * 2} (layer, kv-head) slices [1, 1, 32768, 128] bf16 "
+                         f"({nb / 1e6:.0f} MB of K+V), quantize+pack then dequant, numpy oracle, "
+                         f"{workers} processes, {wall:.1f} s"}
+    line = {
+        "metric": METRIC,
+        "value": round(world * in_bytes / (ms * 1e6), 2),
+        "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "layers": w.layers, "kv_heads": w.heads, "head_dim": w.head_dim,
+                   "batch_per_gpu": w.batch, "seq_len": w.seq, "profile": w.profile,
+                   "input_bytes_per_gpu": in_bytes, "compressed_bytes_per_gpu": comp_bytes,
+                   "l2": "inputs (1.88 GB) larger than L2; no flush",
+                   "value_definition": "K+V input bytes of all ranks / device time of one "
+                                       "select+quantize+pack+dequant step",
+                   "parallelism": f"weak shards of (layer, kv-head) units over {world} GPU(s)"},
+        "phases": phases,
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps * launches,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -623,9 +623,133 @@ def _layer_input(keys: torch.Tensor, values: torch.Tensor) -> L.LayerIn:
     return li
 
 
-def _quantize_group(pairs, config: KvQuantConfig, scores, retain_mask: torch.Tensor | None = None
-                    ) -> list[QuantizedKvLayer]:
-    """Compress layers of one geometry sharing one scores tensor."""
+class _GroupRun:
+    """Compression of a run of layers of one geometry sharing one selection:
+    device arena for every stored tensor, the C plan, the layer inputs and the
+    workspaces, built once.  ``select()`` / ``quantize()`` / ``dequantize()``
+    only launch kernels, so a prepared run can be executed repeatedly."""
+
+    def __init__(self, dev_pairs, config: KvQuantConfig, tiers: TierSizes, plans: list, device: torch.device,
+                 home: torch.device, idx=None):
+        lib = L.lib()
+        k0 = dev_pairs[0][0]
+        B, H, T, D = k0.shape
+        dtype = k0.dtype
+        self.device, self.home, self.dtype, self.shape = device, home, dtype, (B, H, T, D)
+        self.pairs, self.tiers, self.plans, self.config = dev_pairs, tiers, plans, config
+        nl = len(dev_pairs)
+        esize = _dtype_element_size(dtype)
+        ar = _Arena()
+        h_idx = ar.reserve(4 * T) if idx is None else None
+        h_ret = [ar.reserve(nl * B * H * tiers.n_retained * D * esize) for _ in range(2)]
+        h_codes, h_scales, h_zps = [None] * 4, [None] * 4, [None] * 4
+        for i, p in enumerate(plans):
+            if p is None:
+                continue
+            h_codes[i] = ar.reserve(nl * p.code_bytes)
+            h_scales[i] = ar.reserve(nl * p.n_groups * _dtype_element_size(p.scale_dtype))
+            if p.quantizer == "affine":
+                h_zps[i] = ar.reserve(nl * p.n_groups)
+        ar.allocate(device)
+        self.arena, self.h_ret, self.h_codes, self.h_scales, self.h_zps = ar, h_ret, h_codes, h_scales, h_zps
+        if idx is None:
+            all_idx = ar.view(h_idx, 0, 4 * T, torch.int32, (T,))
+            idx = torch.split(all_idx, [tiers.n_retained, tiers.n_standard, tiers.n_cold])
+        self.idx_ret, self.idx_std, self.idx_cold = idx
+
+        plan = L.Plan()
+        plan.batch, plan.head_dim, plan.seq_len, plan.dtype = B, D, T, L.DTYPE_CODE[dtype]
+        plan.n_retained, plan.n_standard, plan.n_cold = tiers.n_retained, tiers.n_standard, tiers.n_cold
+        plan.idx_retained = self.idx_ret.data_ptr()
+        plan.idx_standard = self.idx_std.data_ptr()
+        plan.idx_cold = self.idx_cold.data_ptr()
+        plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+        plan.retained_k, plan.retained_v = ar.ptr(h_ret[0]), ar.ptr(h_ret[1])
+        for i, p in enumerate(plans):
+            if p is None:
+                continue
+            plan.spec[i] = p.spec()
+            plan.codes[i] = ar.ptr(h_codes[i])
+            plan.scales[i] = ar.ptr(h_scales[i])
+            plan.zero_points[i] = ar.ptr(h_zps[i]) if h_zps[i] is not None else 0
+        self.plan = plan
+        self.layer_ins = (L.LayerIn * nl)(*[_layer_input(k, v) for k, v in dev_pairs])
+        ws_bytes = int(lib.gkv_quantize_workspace_bytes(ctypes.byref(plan), self.layer_ins, nl))
+        self.ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+        self.ws_bytes = ws_bytes
+        self.sel_ws = torch.empty(max(int(lib.gkv_select_workspace_bytes(T)), 1), dtype=torch.uint8, device=device)
+        self.policy = tiers.policy()
+        self.outlier = torch.empty(T, dtype=torch.float32, device=device) if tiers.keep_outlier > 0 else None
+        self.out_k = self.out_v = None
+
+    def select(self, scores: torch.Tensor | None) -> None:
+        """Selection kernel(s) for normalized fp32 [T] scores on the device."""
+        lib = L.lib()
+        st = L.stream_handle(self.device)
+        if self.outlier is not None:
+            li = self.layer_ins[0]
+            B, _, T, D = self.shape
+            L.check(lib.gkv_outlier_scores(ctypes.byref(li), B, T, D, L.DTYPE_CODE[self.dtype],
+                                           self.outlier.data_ptr(), st))
+        L.check(lib.gkv_select_tiers(L.ptr(scores), L.ptr(self.outlier), ctypes.byref(self.policy),
+                                     self.idx_ret.data_ptr(), self.idx_std.data_ptr(), self.idx_cold.data_ptr(),
+                                     self.sel_ws.data_ptr(), self.sel_ws.numel(), st))
+
+    def quantize(self) -> None:
+        L.check(L.lib().gkv_quantize(ctypes.byref(self.plan), self.layer_ins, len(self.pairs), self.ws.data_ptr(),
+                                     self.ws_bytes, L.stream_handle(self.device)))
+
+    def dequantize(self) -> None:
+        """Dequantize every layer of the run into preallocated [L, B, H, T, D] outputs."""
+        if self.out_k is None:
+            shp = (len(self.pairs), *self.shape)
+            self.out_k = torch.empty(shp, dtype=self.dtype, device=self.device)
+            self.out_v = torch.empty(shp, dtype=self.dtype, device=self.device)
+        B, H = self.shape[:2]
+        L.check(L.lib().gkv_dequantize(ctypes.byref(self.plan), len(self.pairs) * B * H, self.out_k.data_ptr(),
+                                       self.out_v.data_ptr(), None, 0, L.stream_handle(self.device)))
+
+    def layers(self) -> list:
+        """QuantizedKvLayer objects whose tensors are views into the arena."""
+        B, H, T, D = self.shape
+        dtype, ar, tiers = self.dtype, self.arena, self.tiers
+        esize = _dtype_element_size(dtype)
+        out = []
+        ret_shape = (B, H, tiers.n_retained, D)
+        ret_bytes = B * H * tiers.n_retained * D * esize
+        for l in range(len(self.pairs)):
+            qts = []
+            for i, p in enumerate(self.plans):
+                if p is None:
+                    qts.append(None)
+                    continue
+                ssize = _dtype_element_size(p.scale_dtype)
+                q_dtype = torch.uint8 if (p.packed or p.quantizer == "affine") else torch.int8
+                q_shape_store = (p.code_bytes,) if p.packed else p.q_shape
+                q = ar.view(self.h_codes[i], l * p.code_bytes, p.code_bytes, q_dtype, q_shape_store)
+                sc = ar.view(self.h_scales[i], l * p.n_groups * ssize, p.n_groups * ssize, p.scale_dtype,
+                             p.scales_shape)
+                zp = None
+                if self.h_zps[i] is not None:
+                    zp = ar.view(self.h_zps[i], l * p.n_groups, p.n_groups, torch.uint8, p.scales_shape)
+                qts.append(QuantizedTensor(q=q, scales=sc, zero_points=zp, original_shape=(B, H, p.n, D),
+                                           axis=p.axis, group_size=p.group_size, bits=p.bits, padded=p.padded,
+                                           q_shape=p.q_shape, original_dtype=dtype, packed=p.packed,
+                                           packed_offset=0 if p.quantizer == "affine" else -(1 << (p.bits - 1)),
+                                           rotation=p.rotation))
+            out.append(QuantizedKvLayer(
+                compressed_keys=qts[0], compressed_values=qts[1], compressed_indices=self.idx_std,
+                retained_keys=ar.view(self.h_ret[0], l * ret_bytes, ret_bytes, dtype, ret_shape),
+                retained_values=ar.view(self.h_ret[1], l * ret_bytes, ret_bytes, dtype, ret_shape),
+                retained_indices=self.idx_ret, original_shape=(B, H, T, D), seq_dim=2,
+                low_priority_compressed_keys=qts[2], low_priority_compressed_values=qts[3],
+                low_priority_compressed_indices=self.idx_cold, home_device=self.home))
+        return out
+
+
+def _prepare_group(pairs, config: KvQuantConfig, scores, retain_mask: torch.Tensor | None = None):
+    """Split a run of same-geometry layers into prepared _GroupRun objects (or
+    passthrough layers).  Returns a list of ("run", run, scores) / ("pass", layer)."""
     k0 = pairs[0][0]
     shape = tuple(k0.shape)
     B, H, T, D = shape
@@ -635,9 +759,7 @@ def _quantize_group(pairs, config: KvQuantConfig, scores, retain_mask: torch.Ten
     outlier_needed = config.outlier_protection_ratio > 0.0 or config.min_outlier_tokens > 0
     if retain_mask is None and outlier_needed and len(pairs) > 1:
         # outlier scores differ per layer, so each layer has its own selection
-        return [lay for p in pairs for lay in _quantize_group([p], config, scores)]
-
-    # inputs on the compute device with a contiguous head_dim
+        return [item for p in pairs for item in _prepare_group([p], config, scores)]
     dev_pairs = []
     for keys, values in pairs:
         keys = _to_device(keys.detach(), device)
@@ -647,91 +769,35 @@ def _quantize_group(pairs, config: KvQuantConfig, scores, retain_mask: torch.Ten
         if values.stride(3) != 1:
             values = values.contiguous()
         dev_pairs.append((keys, values))
-
+    idx = None
     if retain_mask is not None:
-        tiers, idx_ret, idx_std, idx_cold = _tiers_from_mask(retain_mask, T, config, scores, device)
+        tiers, *idx = _tiers_from_mask(retain_mask, T, config, scores, device)
     else:
         tiers = resolve_tiers(config, T, scores is not None)
-        idx_ret = idx_std = idx_cold = None
     plans = tensor_plans(config, shape, tiers)
     if config.skip_if_not_smaller and \
             layer_memory_bytes(shape, dtype, tiers, plans) >= 2 * B * H * T * D * _dtype_element_size(dtype):
-        return [_full_precision_layer(k.detach(), v.detach()) for k, v in pairs]
+        return [("pass", _full_precision_layer(k.detach(), v.detach())) for k, v in pairs]
     if len(pairs) > 1 and any(p is not None and not p.slice_bits_aligned for p in plans):
-        return [lay for p in pairs for lay in _quantize_group([p], config, scores)]
+        return [item for p in pairs for item in _prepare_group([p], config, scores)]
+    s = _normalize_token_scores(T, scores, device).contiguous() if (scores is not None and idx is None) else None
+    return [("run", _GroupRun(dev_pairs, config, tiers, plans, device, home, idx), s, idx is None)]
 
-    lib = L.lib()
-    if idx_ret is None:
-        outlier = None
-        if tiers.keep_outlier > 0:
-            outlier = torch.empty(T, dtype=torch.float32, device=device)
-            li = _layer_input(*dev_pairs[0])
-            L.check(lib.gkv_outlier_scores(ctypes.byref(li), B, T, D, L.DTYPE_CODE[dtype], outlier.data_ptr(),
-                                           L.stream_handle(device)))
-        tiers, idx_ret, idx_std, idx_cold = _select(T, config, scores, device, outlier, tiers)
 
-    nl = len(dev_pairs)
-    esize = _dtype_element_size(dtype)
-    ar = _Arena()
-    h_ret = [ar.reserve(nl * B * H * tiers.n_retained * D * esize) for _ in range(2)]
-    h_codes, h_scales, h_zps = [None] * 4, [None] * 4, [None] * 4
-    for i, p in enumerate(plans):
-        if p is None:
+def _quantize_group(pairs, config: KvQuantConfig, scores, retain_mask: torch.Tensor | None = None
+                    ) -> list[QuantizedKvLayer]:
+    """Compress layers of one geometry sharing one scores tensor."""
+    out = []
+    for item in _prepare_group(pairs, config, scores, retain_mask):
+        if item[0] == "pass":
+            out.append(item[1])
             continue
-        h_codes[i] = ar.reserve(nl * p.code_bytes)
-        h_scales[i] = ar.reserve(nl * p.n_groups * _dtype_element_size(p.scale_dtype))
-        if p.quantizer == "affine":
-            h_zps[i] = ar.reserve(nl * p.n_groups)
-    ar.allocate(device)
-
-    plan = L.Plan()
-    plan.batch, plan.head_dim, plan.seq_len, plan.dtype = B, D, T, L.DTYPE_CODE[dtype]
-    plan.n_retained, plan.n_standard, plan.n_cold = tiers.n_retained, tiers.n_standard, tiers.n_cold
-    plan.idx_retained, plan.idx_standard, plan.idx_cold = idx_ret.data_ptr(), idx_std.data_ptr(), idx_cold.data_ptr()
-    plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
-    plan.retained_k, plan.retained_v = ar.ptr(h_ret[0]), ar.ptr(h_ret[1])
-    for i, p in enumerate(plans):
-        if p is None:
-            continue
-        plan.spec[i] = p.spec()
-        plan.codes[i] = ar.ptr(h_codes[i])
-        plan.scales[i] = ar.ptr(h_scales[i])
-        plan.zero_points[i] = ar.ptr(h_zps[i]) if h_zps[i] is not None else 0
-    layer_ins = (L.LayerIn * nl)(*[_layer_input(k, v) for k, v in dev_pairs])
-    ws_bytes = int(lib.gkv_quantize_workspace_bytes(ctypes.byref(plan), layer_ins, nl))
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
-    L.check(lib.gkv_quantize(ctypes.byref(plan), layer_ins, nl, ws.data_ptr(), ws_bytes, L.stream_handle(device)))
-
-    layers = []
-    ret_shape = (B, H, tiers.n_retained, D)
-    ret_bytes = B * H * tiers.n_retained * D * esize
-    for l in range(nl):
-        qts = []
-        for i, p in enumerate(plans):
-            if p is None:
-                qts.append(None)
-                continue
-            ssize = _dtype_element_size(p.scale_dtype)
-            q_dtype = torch.uint8 if (p.packed or p.quantizer == "affine") else torch.int8
-            q_shape_store = (p.code_bytes,) if p.packed else p.q_shape
-            q = ar.view(h_codes[i], l * p.code_bytes, p.code_bytes, q_dtype, q_shape_store)
-            sc = ar.view(h_scales[i], l * p.n_groups * ssize, p.n_groups * ssize, p.scale_dtype, p.scales_shape)
-            zp = None
-            if h_zps[i] is not None:
-                zp = ar.view(h_zps[i], l * p.n_groups, p.n_groups, torch.uint8, p.scales_shape)
-            qts.append(QuantizedTensor(q=q, scales=sc, zero_points=zp, original_shape=(B, H, p.n, D), axis=p.axis,
-                                       group_size=p.group_size, bits=p.bits, padded=p.padded, q_shape=p.q_shape,
-                                       original_dtype=dtype, packed=p.packed,
-                                       packed_offset=0 if p.quantizer == "affine" else -(1 << (p.bits - 1)),
-                                       rotation=p.rotation))
-        layers.append(QuantizedKvLayer(
-            compressed_keys=qts[0], compressed_values=qts[1], compressed_indices=idx_std,
-            retained_keys=ar.view(h_ret[0], l * ret_bytes, ret_bytes, dtype, ret_shape),
-            retained_values=ar.view(h_ret[1], l * ret_bytes, ret_bytes, dtype, ret_shape),
-            retained_indices=idx_ret, original_shape=shape, seq_dim=2,
-            low_priority_compressed_keys=qts[2], low_priority_compressed_values=qts[3],
-            low_priority_compressed_indices=idx_cold, home_device=home))
-    return layers
+        _, run, s, needs_select = item
+        if needs_select:
+            run.select(s)
+        run.quantize()
+        out.extend(run.layers())
+    return out
 
 
 def _tiers_from_mask(retain_mask: torch.Tensor, T: int, config: KvQuantConfig, scores, device):

@@ -1,0 +1,98 @@
+"""The public API on the GPU: HF cache in/out, host-resident inputs, the
+stand-alone tensor dequantize, append, and error reporting."""
+import numpy as np
+import pytest
+import torch
+
+import graphkv_b200 as g
+from graphkv_b200 import _lib as L
+from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
+from oracle import graphkv_oracle as orc
+from tests.golden.cases import bits_of
+
+pytestmark = pytest.mark.gpu
+
+
+def _small_cache(T=2048, layers=3, dtype=torch.bfloat16, device="cuda"):
+    g_ = torch.Generator().manual_seed(5)
+    return tuple((torch.randn(1, 2, T, 128, generator=g_).to(dtype).to(device),
+                  torch.randn(1, 2, T, 128, generator=g_).to(dtype).to(device)) for _ in range(layers))
+
+
+def test_dynamic_cache_export_matches_dequantize():
+    from transformers.cache_utils import DynamicCache
+    cache = _small_cache()
+    scores = torch.exp(torch.randn(2048, generator=torch.Generator().manual_seed(1))).cuda()
+    dyn = g.quantize_hf_cache(cache, "graphkv", importance_scores=scores, output="dynamic")
+    comp = g.quantize_hf_cache(cache, "graphkv", importance_scores=scores, output="compressed")
+    assert isinstance(dyn, DynamicCache)
+    for i, (k, v) in enumerate(comp.dequantize()):
+        assert torch.equal(dyn.layers[i].keys, k) and torch.equal(dyn.layers[i].values, v)
+    assert dyn.get_seq_length() == 2048
+    # an HF cache goes back in
+    again = g.quantize_hf_cache(dyn, "graphkv-int4-balanced", output="compressed")
+    assert again.stats()["layers"] == 3.0
+
+
+def test_host_inputs_round_trip_to_host():
+    cache = _small_cache(device="cpu")
+    out = g.quantize_hf_cache(cache, "graphkv-int4-balanced", output="legacy")
+    dev = g.quantize_hf_cache(tuple((k.cuda(), v.cuda()) for k, v in cache), "graphkv-int4-balanced",
+                              output="legacy")
+    for (hk, hv), (dk, dv) in zip(out, dev):
+        assert hk.device.type == "cpu"
+        assert torch.equal(hk, dk.cpu()) and torch.equal(hv, dv.cpu())
+
+
+def test_quantized_tensor_dequantize_matches_oracle():
+    cache = _small_cache(T=512, layers=1)
+    cfg = g.get_profile("graphkv-int4-balanced").config
+    layer = g.quantize_kv_layer(*cache[0], cfg)
+    k = layer.compressed_keys.dequantize()
+    K = cache[0][0].float().cpu().numpy()
+    qt = orc.quantize_tensor(K, "bf16", 4, 64, "symmetric", 2)
+    assert np.array_equal(bits_of(k), orc.storage_bits(orc.dequantize_tensor(qt), "bf16"))
+
+
+def test_append_requantizes():
+    cache = _small_cache(T=512, layers=2)
+    cfg = g.get_profile("graphkv-int4-balanced").config
+    comp = g.QuantizedKvCache.from_past_key_values(cache, cfg)
+    new = tuple((torch.randn(1, 2, 64, 128, device="cuda").bfloat16(),
+                 torch.randn(1, 2, 64, 128, device="cuda").bfloat16()) for _ in range(2))
+    grown = comp.append(new, cfg)
+    assert grown.layers[0].original_shape == (1, 2, 576, 128)
+    k, v = grown.layers[1].dequantize()
+    assert k.shape == (1, 2, 576, 128)
+
+
+def test_reference_shaped_workload_stats():
+    w = WORKLOADS["qwen7b-16k"]
+    layers = [make_layer(w, l, device="cuda") for l in range(2)]
+    comp = g.quantize_hf_cache(tuple(layers), "graphkv", importance_scores=make_scores(w, "cuda"),
+                               output="compressed")
+    st = comp.stats()
+    assert st["compressed_bytes"] == 2 * 255_437_952 // 28
+    assert st["low_priority_tokens"] == 2 * 3992 * 1
+
+
+def test_bad_index_is_reported_not_faulted():
+    """A caller-supplied index outside [0, T) is skipped and reported through
+    the device error word (the kernels check every gathered position)."""
+    cache = _small_cache(T=256, layers=1)
+    cfg = g.get_profile("graphkv-int4-balanced").config
+    layer = g.quantize_kv_layer(*cache[0], cfg)
+    assert L.device_error() == 0
+    layer.compressed_indices[3] = 10_000
+    layer.dequantize()
+    assert L.device_error() == 3
+    assert L.device_error() == 0
+
+
+def test_static_export_follows_reference_behaviour():
+    cache = _small_cache(T=256, layers=1)
+    comp = g.quantize_hf_cache(cache, "graphkv-int4-balanced", output="compressed")
+    with pytest.raises(ValueError, match="config is required"):
+        comp.to_hf_cache("static")
+    with pytest.raises(ValueError, match="implementation must be"):
+        comp.to_hf_cache("paged")
