@@ -390,3 +390,66 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Tier selection without any device allocation.
+//
+// The selection kernel needs one byte of tier state per token.  gkv_select_tiers
+// takes that scratch from the caller; this variant uses a fixed array owned by
+// the library instead, for callers that cannot allocate device memory when they
+// select (for instance an engine that has handed all free device memory to its
+// own pool, or a latency-critical path where cudaMalloc's implicit device-wide
+// synchronisation is not acceptable).
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace gkv {
+namespace {
+
+constexpr int kStaticSelectMaxTokens = GKV_STATIC_SELECT_MAX_TOKENS;
+constexpr int kMaxDevices = 64;
+
+// 1 MiB of tier bytes.  Every GPU that loads this library holds it until the
+// process exits.  In host code `g_select_scratch` only names a host-side handle
+// of the symbol; the device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) uint8_t g_select_scratch[kStaticSelectMaxTokens];
+
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kMaxDevices] = {};
+
+// Device address of the scratch on the current device, looked up once per device.
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GKV_ERR_UNSUPPORTED, "device ordinal beyond 63");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_select_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(selection scratch)");
+    g_scratch_address[dev] = p;
+  }
+  *out = g_scratch_address[dev];
+  return GKV_OK;
+}
+
+}  // namespace
+}  // namespace gkv
+
+extern "C" int32_t gkv_select_tiers_static(const float* scores, const float* outlier_scores,
+                                           const gkv_select_policy* policy, int32_t* idx_retained,
+                                           int32_t* idx_standard, int32_t* idx_cold, gkv_stream_t stream) {
+  if (!policy) return fail(GKV_ERR_INVALID, "policy is NULL");
+  if (policy->seq_len > kStaticSelectMaxTokens)
+    return fail(GKV_ERR_TOO_LARGE, "seq_len " + std::to_string(policy->seq_len) +
+                                       " exceeds the library's static selection scratch of " +
+                                       std::to_string(kStaticSelectMaxTokens) + " tokens");
+  void* scratch = nullptr;
+  const int st = static_scratch_address(&scratch);
+  if (st != GKV_OK) return st;
+  // the kernel writes the tier byte of every token before reading it, so the
+  // previous call's contents need no clearing
+  return gkv_select_tiers(scores, outlier_scores, policy, idx_retained, idx_standard, idx_cold, scratch,
+                          (size_t)kStaticSelectMaxTokens, stream);
+}

@@ -147,6 +147,29 @@ int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const
                          int32_t* idx_retained, int32_t* idx_standard, int32_t* idx_cold,
                          void* workspace, size_t workspace_bytes, gkv_stream_t stream);
 
+/* Same selection as gkv_select_tiers, but the library supplies the scratch:
+ * no workspace argument, and nothing is allocated by the caller or by the
+ * library during the call.  This entry point has no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory when they
+ * select -- e.g. an engine that has given all free device memory to its own
+ * pool, or a latency-critical path that cannot afford cudaMalloc's implicit
+ * device-wide synchronisation.
+ *  - Limit: seq_len <= GKV_STATIC_SELECT_MAX_TOKENS; larger sizes return
+ *    GKV_ERR_TOO_LARGE without launching anything.
+ *  - The scratch is a 1 MiB device array inside the library; every GPU that
+ *    loads the library keeps it until the process exits.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array: calls whose kernels can overlap on the GPU
+ *    (different streams, or several host threads) race and must be ordered by
+ *    the caller.  No clearing is needed between calls: the kernel writes every
+ *    token's tier byte before reading it. */
+#define GKV_STATIC_SELECT_MAX_TOKENS 1048576
+int32_t gkv_select_tiers_static(const float* scores, const float* outlier_scores, const gkv_select_policy* policy,
+                                int32_t* idx_retained, int32_t* idx_standard, int32_t* idx_cold,
+                                gkv_stream_t stream);
+
 /* Per-token outlier score mean(K^2) + mean(V^2) over (batch, head, head_dim)
  * for one layer, fp32 [T].  Replaces _kv_outlier_scores (core.py:1051-1054);
  * sums are accumulated in fp64 and rounded once. */
