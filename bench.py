@@ -45,6 +45,7 @@ def parse_args():
     ap.add_argument("--workload", default=WORKLOAD)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling case)")
     return ap.parse_args()
 
 
@@ -250,6 +251,8 @@ def run_ours(args):
     from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
 
     w = WORKLOADS[args.workload]
+    if args.layers:
+        w = replace(w, layers=args.layers)
     wN = replace(w, batch=w.batch * world)
     shard = shard_units(w.layers, w.heads, world, rank)
     pairs = [make_layer(wN, l, device=str(dev), heads=range(h0, h1)) for (l, h0, h1) in shard]

@@ -34,16 +34,8 @@ int elem_size(int dtype) { return dtype == GKV_F32 ? 4 : 2; }
 
 // tile-kernel instantiations: (D, TT) per element size
 bool tile_instantiated(int esize, int D, int TT) {
-  if (D == 64) return TT == 64 || TT == 128;
-  if (D == 128) return TT == 64 || (TT == 128 && esize == 2);
-  if (D == 256) return TT == 64 && esize == 2;
-  return false;
-}
-
-// rows per thread segment of the token-axis quantizer (quant_token_tile)
-int token_seg_rows(int esize, int D, int TT) {
-  const int words = D * esize / 4;
-  return TT / (kThreads / words);
+  (void)esize;
+  return (D == 64 || D == 128) && (TT == 64 || TT == 128);
 }
 
 const int kTierOf[4] = {1, 1, 2, 2};
@@ -107,16 +99,17 @@ int resolve_tensor(const gkv_plan& p, int i, int n, TensorDesc& d) {
 }
 
 // Can tensor d run in the tile kernels with tile height TT?
+// Tile kernels work on runs of 32 elements along the grouped axis: groups of
+// 32, 64 or 128 (powers of two dividing the tile height or head_dim).
 bool tensor_fast(const TensorDesc& d, int esize, int D, int TT, bool quantize) {
-  if (d.log2gs < 0 || d.gs < 16 || !aligned16(d.codes)) return false;
+  (void)esize;
+  if (d.log2gs < 0 || d.gs < 32 || !aligned16(d.codes)) return false;
   if (d.axis == GKV_AXIS_TOKEN) {
     if (d.gs > TT || TT % d.gs) return false;
-    if (quantize && d.gs < token_seg_rows(esize, D, TT)) return false;
+    if (!quantize && d.rotation) return false;  // rotated token-axis dequant: general path
     return true;
   }
-  const int vec = 16 / esize;
-  if (D % d.gs || d.gs % vec || d.gs / vec > 32) return false;
-  return true;
+  return D % d.gs == 0;
 }
 
 bool layers_aligned(const gkv_layer_in* layers, int n_layers, int esize) {

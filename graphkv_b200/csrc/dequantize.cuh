@@ -46,155 +46,271 @@ __device__ __forceinline__ float decode(uint32_t enc, const Decoder& dc) {
   return __fmul_rn(q, dc.scale);
 }
 
+// two codes at once: (enc ^ xor) + off, times the scale, in packed fp32
+__device__ __forceinline__ uint64_t decode2(uint32_t e0, uint32_t e1, const Decoder& dc) {
+  const uint64_t q = sub2(pk2(__uint_as_float(0x4B000000u | (e0 ^ dc.xor_mask)),
+                              __uint_as_float(0x4B000000u | (e1 ^ dc.xor_mask))),
+                          pk2(dc.base, dc.base));
+  return mul2(q, pk2(dc.scale, dc.scale));
+}
+
 __device__ __forceinline__ int load_zp(const TensorDesc& d, int64_t gi) {
   return d.quantizer == GKV_AFFINE ? (int)d.zps[gi] : 0;
 }
 
-// Output of one decoded row: optional inverse rotation across the warp, cast, store.
-template <typename T, int D>
-__device__ __forceinline__ void emit_row(float (&v)[D / 32], bool rotate, float div, float inv, T* dst) {
+// Output of one decoded row (lane holds D/32 consecutive channels): optional
+// inverse rotation across the warp, cast to T, one vector store per lane.
+// Cross-lane butterfly stages compute o + sign * v with one fused multiply-add:
+// sign = +1 gives v + o, sign = -1 gives o - v, each rounded once as the
+// reference's add / subtract.
+template <typename T, int D, bool ROT>
+__device__ __forceinline__ void emit_row(float (&v)[D / 32], float div, float inv, T* dst) {
   constexpr int EPL = D / 32;
   const int lane = threadIdx.x & 31;
-  if (rotate) {
-#pragma unroll
-    for (int h = 1; h < EPL; h <<= 1) {
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) {
-        if ((i & h) == 0) {
-          const float a = v[i], b = v[i + h];
-          v[i] = __fadd_rn(a, b);
-          v[i + h] = __fsub_rn(a, b);
-        }
-      }
-    }
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-      const bool right = (lane & m) != 0;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) {
-        const float o = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
-        v[i] = right ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
-      }
-    }
-  }
+  if constexpr (ROT) fwht_warp<EPL>(v);
   constexpr int NB = EPL * (int)sizeof(T);
   constexpr int NW = NB / 4;
   uint32_t w[NW];
+  if constexpr (sizeof(T) == 4) {
 #pragma unroll
-  for (int q = 0; q < NW; ++q) w[q] = 0;
+    for (int i = 0; i < EPL; ++i) w[i] = __float_as_uint(ROT ? __fdiv_rn(v[i], div) : v[i]);
+  } else {
 #pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const T o = rotate ? hadamard_scale<T>(v[i], div, inv) : Elem<T>::from_f32(v[i]);
-    w[(i * (int)sizeof(T)) / 4] |= tbits(o) << (((i * (int)sizeof(T)) % 4) * 8);
+    for (int i = 0; i < EPL; i += 2) {
+      uint32_t lo, hi;
+      if constexpr (ROT) {
+        lo = tbits(hadamard_scale<T>(v[i], div, inv));
+        hi = tbits(hadamard_scale<T>(v[i + 1], div, inv));
+        w[i / 2] = lo | (hi << 16);
+      } else if constexpr (Elem<T>::kTag == GKV_BF16) {
+        const __nv_bfloat162 p = __floats2bfloat162_rn(v[i], v[i + 1]);
+        w[i / 2] = *reinterpret_cast<const uint32_t*>(&p);
+      } else {
+        const __half2 p = __floats2half2_rn(v[i], v[i + 1]);
+        w[i / 2] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+    }
   }
   store_bytes<NB>(reinterpret_cast<uint8_t*>(dst + lane * EPL), w);
 }
 
-// load NBITS (power of two <= 64) bits starting at bit offset `bit` (aligned to NBITS)
-template <int NBITS>
-__device__ __forceinline__ uint64_t load_bits(const uint8_t* codes, int64_t bit) {
-  if constexpr (NBITS <= 8) {
-    return (uint64_t)((codes[bit >> 3] >> (bit & 7)) & ((1u << NBITS) - 1u));
-  } else if constexpr (NBITS == 16) {
-    return reinterpret_cast<const uint16_t*>(codes)[bit >> 4];
-  } else if constexpr (NBITS == 32) {
-    return reinterpret_cast<const uint32_t*>(codes)[bit >> 5];
+
+// 32 codes of a run (SB bits each) as fp32 bit patterns 2^23 + code
+template <int SB>
+__device__ __forceinline__ void run_codes(const uint32_t (&w)[SB], uint32_t (&c)[kRun]) {
+#pragma unroll
+  for (int q = 0; q < SB; ++q) {
+    uint32_t t[32 / SB];
+    word_codes<SB>(w[q], t);
+#pragma unroll
+    for (int i = 0; i < 32 / SB; ++i) c[q * (32 / SB) + i] = t[i];
+  }
+}
+
+template <int SB>
+__device__ __forceinline__ void load_run(const uint8_t* p, uint32_t (&w)[SB]) {
+  if constexpr (SB == 2) {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    w[0] = t.x; w[1] = t.y;
+  } else if constexpr (SB == 4) {
+    const uint4 t = *reinterpret_cast<const uint4*>(p);
+    w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
   } else {
-    return reinterpret_cast<const uint64_t*>(codes)[bit >> 6];
+    const uint4 t0 = reinterpret_cast<const uint4*>(p)[0], t1 = reinterpret_cast<const uint4*>(p)[1];
+    w[0] = t0.x; w[1] = t0.y; w[2] = t0.z; w[3] = t0.w; w[4] = t1.x; w[5] = t1.y; w[6] = t1.z; w[7] = t1.w;
   }
 }
 
-// channel-axis tensor: warp per tier row
-template <typename T, int D, int SB>
-__device__ void dequant_channel_tile(const DequantParams& p, const TensorDesc& d, T* out, const int* idx, int s,
+// decoded values of a run: ((2^23 + code) ^ xor) - base, times the scale, in packed pairs
+__device__ __forceinline__ void decode_run(const uint32_t (&c)[kRun], const Decoder& dc, float (&v)[kRun]) {
+  const uint64_t base2 = pk2(dc.base, dc.base), sc2 = pk2(dc.scale, dc.scale);
+#pragma unroll
+  for (int i = 0; i < kRun; i += 2) {
+    const uint64_t q = sub2(pk2(__uint_as_float(c[i] ^ dc.xor_mask), __uint_as_float(c[i + 1] ^ dc.xor_mask)), base2);
+    const uint64_t r = mul2(q, sc2);
+    v[i] = lo2(r);
+    v[i + 1] = hi2(r);
+  }
+}
+
+// pack two fp32 values into one 32-bit word of T (round to nearest even)
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
+  if constexpr (Elem<T>::kTag == GKV_BF16) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&p);
+  } else {
+    const __half2 p = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&p);
+  }
+}
+
+// Channel-axis tensor (values by default): item = (tier row, run of 32 channels),
+// the runs of a row in adjacent lanes (the Hadamard rotation crosses them with
+// shuffles).  Codes, scale and zero point are loaded once per run, decoded in
+// registers and stored with 16-byte vector stores at the row's output position.
+template <typename T, int D, int TT, int SB, bool ROT>
+__device__ void dequant_channel_half(const DequantParams& p, const TensorDesc& d, T* out, const int* tok, int s,
                                      int j0, int rows) {
-  constexpr int EPL = D / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int r = warp; r < rows; r += kThreads / 32) {
-    const int64_t row = (int64_t)s * d.n + j0 + r;
-    const uint64_t bits = load_bits<EPL * SB>(d.codes, (row * d.n_pad + lane * EPL) * SB);
-    const int64_t gi = row * d.groups_row + ((lane * EPL) >> d.log2gs);
-    const Decoder dc = make_decoder(d, load_scale(d.scales, gi, d.scale_dtype), load_zp(d, gi));
-    float v[EPL];
+  constexpr int RPR = D / kRun;
+  constexpr int ITEMS = TT * RPR;
+  constexpr int ITER = (ITEMS + 127) / 128;
+  const int ht = threadIdx.x & 127;
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int itn = 0; itn < ITER; ++itn) {
+    const int item = ht + itn * 128;
+    const int r = item / RPR, run = item % RPR;
+    const bool act = item < ITEMS && r < rows;
+    uint32_t w[SB];
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) v[i] = decode((uint32_t)(bits >> (i * SB)) & ((1u << SB) - 1u), dc);
-    const int tok = idx[j0 + r];
-    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); continue; }
-    emit_row<T, D>(v, d.rotation != 0, p.had_div, p.had_inv, out + (int64_t)tok * D);
-  }
-}
-
-// token-axis tensor: decode the tile into shared memory, then warp-per-row stores
-template <typename T, int D, int TT, int SB>
-__device__ void dequant_token_tile(const DequantParams& p, const TensorDesc& d, T* out, const int* idx, int s, int j0,
-                                   int rows, float* tile) {
-  constexpr int PARTS = kThreads / D;
-  constexpr int PR = TT / PARTS;
-  constexpr int TP = D + 4;  // fp32 pitch
-  const int c = threadIdx.x % D, part = threadIdx.x / D;
-  const int64_t crow = (int64_t)s * D + c;
+    for (int q = 0; q < SB; ++q) w[q] = 0;
+    float scale = 0.f;
+    int zp = 0;
+    if (act) {
+      const int64_t row = (int64_t)s * d.n + j0 + r;
+      load_run<SB>(d.codes + ((row * d.n_pad + run * kRun) * SB) / 8, w);
+      const int64_t gi = row * d.groups_row + ((run * kRun) >> d.log2gs);
+      scale = load_scale(d.scales, gi, d.scale_dtype);
+      zp = load_zp(d, gi);
+    }
+    uint32_t c[kRun];
+    run_codes<SB>(w, c);
+    float v[kRun];
+    decode_run(c, make_decoder(d, scale, zp), v);
+    if constexpr (ROT) {
+      // in-thread stages h = 1 .. 16, then across the RPR lanes of the row
 #pragma unroll
-  for (int q = 0; q < PR / 16; ++q) {
-    const int r0 = part * PR + q * 16;
-    const int tok = j0 + r0;
-    if (tok < d.n_pad) {
-      const int64_t gi = crow * d.groups_row + (tok >> d.log2gs);
-      const Decoder dc = make_decoder(d, load_scale(d.scales, gi, d.scale_dtype), load_zp(d, gi));
-      const int64_t bit = (crow * d.n_pad + tok) * SB;
-      uint32_t w[SB / 2];  // 16 codes
-      if constexpr (SB == 2) {
-        w[0] = reinterpret_cast<const uint32_t*>(d.codes)[bit >> 5];
-      } else if constexpr (SB == 4) {
-        const uint2 t = reinterpret_cast<const uint2*>(d.codes)[bit >> 6];
-        w[0] = t.x; w[1] = t.y;
-      } else {
-        const uint4 t = reinterpret_cast<const uint4*>(d.codes)[bit >> 7];
-        w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
+      for (int h = 1; h < kRun; h <<= 1) {
+#pragma unroll
+        for (int i = 0; i < kRun; i += 2 * h) {
+#pragma unroll
+          for (int j = 0; j < h; ++j) {
+            const float a = v[i + j], bb = v[i + j + h];
+            v[i + j] = __fadd_rn(a, bb);
+            v[i + j + h] = __fsub_rn(a, bb);
+          }
+        }
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t enc = (w[(i * SB) / 32] >> ((i * SB) % 32)) & ((1u << SB) - 1u);
-        tile[(r0 + i) * TP + c] = decode(enc, dc);
+      for (int m = 1; m < RPR; m <<= 1) {
+        const float sg = (lane & m) ? -1.f : 1.f;
+        const uint64_t sg2 = pk2(sg, sg);
+#pragma unroll
+        for (int i = 0; i < kRun; i += 2) {
+          const float o0 = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+          const float o1 = __shfl_xor_sync(0xFFFFFFFFu, v[i + 1], m);
+          const uint64_t rr = fma2(sg2, pk2(v[i], v[i + 1]), pk2(o0, o1));
+          v[i] = lo2(rr);
+          v[i + 1] = hi2(rr);
+        }
+      }
+    }
+    if (act && tok[r] >= 0) {
+      T* dst = out + (int64_t)tok[r] * D + run * kRun;
+      if constexpr (sizeof(T) == 4) {
+#pragma unroll
+        for (int q = 0; q < kRun / 4; ++q) {
+          float o[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) o[u] = ROT ? __fdiv_rn(v[4 * q + u], p.had_div) : v[4 * q + u];
+          reinterpret_cast<uint4*>(dst)[q] =
+              make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < kRun / 8; ++q) {
+          uint32_t o[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float a = v[8 * q + 2 * u], bb = v[8 * q + 2 * u + 1];
+            if constexpr (ROT)
+              o[u] = tbits(hadamard_scale<T>(a, p.had_div, p.had_inv)) |
+                     (tbits(hadamard_scale<T>(bb, p.had_div, p.had_inv)) << 16);
+            else
+              o[u] = pack_pair<T>(a, bb);
+          }
+          reinterpret_cast<uint4*>(dst)[q] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
     }
   }
-  __syncthreads();
-  constexpr int EPL = D / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int r = warp; r < rows; r += kThreads / 32) {
-    float v[EPL];
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) v[i] = tile[r * TP + lane * EPL + i];
-    const int tok = idx[j0 + r];
-    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); continue; }
-    emit_row<T, D>(v, d.rotation != 0, p.had_div, p.had_inv, out + (int64_t)tok * D);
-  }
-  __syncthreads();
 }
 
-template <typename T, int D, int TT>
-__device__ __forceinline__ void dequant_tensor(const DequantParams& p, const TensorDesc& d, T* out, const int* idx,
-                                               int s, int j0, int rows, float* tile) {
+// Token-axis tensor (keys by default): item = (32-bit column word, run of 32 rows);
+// the decoded values are written into the half's shared tile [TT][D + pad] of T,
+// then whole rows leave with 16-byte vector stores.  (Rotated token-axis tensors
+// take the general path.)
+template <typename T, int D, int TT, int SB>
+__device__ void dequant_token_half(const DequantParams& p, const TensorDesc& d, T* out, const int* tok, int s, int j0,
+                                   int rows, T* tile, int half) {
+  constexpr int CPW = 4 / (int)sizeof(T);
+  constexpr int W = D / CPW;
+  constexpr int NRUN = TT / kRun;
+  constexpr int ITEMS = W * NRUN;
+  constexpr int ITER = (ITEMS + 127) / 128;
+  constexpr int TP = D + 16 / (int)sizeof(T);  // tile pitch (elements)
+  const int ht = threadIdx.x & 127;
+#pragma unroll 1
+  for (int itn = 0; itn < ITER; ++itn) {
+    const int item = ht + itn * 128;
+    if (item >= ITEMS) break;
+    const int w = item % W, run = item / W;
+    const int tk = j0 + run * kRun;
+    if (tk >= d.n_pad) continue;
+    float v[CPW][kRun];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int64_t crow = (int64_t)s * D + w * CPW + c;
+      uint32_t cw[SB];
+      load_run<SB>(d.codes + ((crow * d.n_pad + tk) * SB) / 8, cw);
+      const int64_t gi = crow * d.groups_row + (tk >> d.log2gs);
+      uint32_t codes[kRun];
+      run_codes<SB>(cw, codes);
+      decode_run(codes, make_decoder(d, load_scale(d.scales, gi, d.scale_dtype), load_zp(d, gi)), v[c]);
+    }
+    uint32_t* col = reinterpret_cast<uint32_t*>(tile + (run * kRun) * TP) + w;
+#pragma unroll
+    for (int i = 0; i < kRun; ++i) {
+      if constexpr (CPW == 2) col[i * (TP / 2)] = pack_pair<T>(v[0][i], v[1][i]);
+      else col[i * TP] = __float_as_uint(v[0][i]);
+    }
+  }
+  bar_half(half);
+  constexpr int CPR = D * (int)sizeof(T) / 16;  // 16-byte chunks per row
+  for (int e = ht; e < rows * CPR; e += 128) {
+    const int r = e / CPR, c = e - r * CPR;
+    if (tok[r] < 0) continue;
+    reinterpret_cast<uint4*>(out + (int64_t)tok[r] * D)[c] = reinterpret_cast<const uint4*>(tile + r * TP)[c];
+  }
+}
+
+template <typename T, int D, int TT, bool ROT>
+__device__ __forceinline__ void dequant_half_rot(const DequantParams& p, const TensorDesc& d, T* out, const int* tok,
+                                                 int s, int j0, int rows, T* tile, int half) {
   if (d.axis == GKV_AXIS_TOKEN) {
-    if (d.sbits == 4) dequant_token_tile<T, D, TT, 4>(p, d, out, idx, s, j0, rows, tile);
-    else if (d.sbits == 2) dequant_token_tile<T, D, TT, 2>(p, d, out, idx, s, j0, rows, tile);
-    else dequant_token_tile<T, D, TT, 8>(p, d, out, idx, s, j0, rows, tile);
+    if constexpr (!ROT) {
+      if (d.sbits == 4) dequant_token_half<T, D, TT, 4>(p, d, out, tok, s, j0, rows, tile, half);
+      else if (d.sbits == 2) dequant_token_half<T, D, TT, 2>(p, d, out, tok, s, j0, rows, tile, half);
+      else dequant_token_half<T, D, TT, 8>(p, d, out, tok, s, j0, rows, tile, half);
+    }
   } else {
-    if (d.sbits == 4) dequant_channel_tile<T, D, 4>(p, d, out, idx, s, j0, rows);
-    else if (d.sbits == 2) dequant_channel_tile<T, D, 2>(p, d, out, idx, s, j0, rows);
-    else dequant_channel_tile<T, D, 8>(p, d, out, idx, s, j0, rows);
+    if (d.sbits == 4) dequant_channel_half<T, D, TT, 4, ROT>(p, d, out, tok, s, j0, rows);
+    else if (d.sbits == 2) dequant_channel_half<T, D, TT, 2, ROT>(p, d, out, tok, s, j0, rows);
+    else dequant_channel_half<T, D, TT, 8, ROT>(p, d, out, tok, s, j0, rows);
   }
 }
 
 template <typename T, int D, int TT>
 constexpr size_t dequant_tile_smem() {
-  return (size_t)TT * (D + 4) * sizeof(float);
+  return 2 * (size_t)TT * (D + 16 / sizeof(T)) * sizeof(T) + (size_t)TT * sizeof(int);
 }
 
+// One block per tile: retained tiles scatter their rows; standard / cold tiles load
+// the tile's output positions once, then warps 0-3 decode K and warps 4-7 decode V.
 template <typename T, int D, int TT>
-__global__ void __launch_bounds__(kThreads) dequantize_tile_kernel(const __grid_constant__ DequantParams p) {
+__global__ void __launch_bounds__(kThreads, 3) dequantize_tile_kernel(const __grid_constant__ DequantParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  float* tile = reinterpret_cast<float*>(smem);
   const int s = blockIdx.x / p.tiles_slice;
   int k = blockIdx.x - s * p.tiles_slice;
   T* ok = reinterpret_cast<T*>(p.out_k) + (int64_t)s * p.T * D;
@@ -217,13 +333,26 @@ __global__ void __launch_bounds__(kThreads) dequantize_tile_kernel(const __grid_
   k -= p.tiles[0];
   int tier = 1;
   if (k >= p.tiles[1]) { k -= p.tiles[1]; tier = 2; }
-  const TensorDesc& dk = p.t[tier == 1 ? GKV_STD_K : GKV_COLD_K];
-  const TensorDesc& dv = p.t[tier == 1 ? GKV_STD_V : GKV_COLD_V];
   const int* idx = p.idx[tier];
   const int j0 = k * TT;
   const int rows = min(TT, p.n_tier[tier] - j0);
-  dequant_tensor<T, D, TT>(p, dk, ok, idx, s, j0, rows, tile);
-  dequant_tensor<T, D, TT>(p, dv, ov, idx, s, j0, rows, tile);
+  constexpr int TP = D + 16 / (int)sizeof(T);
+  T* tiles = reinterpret_cast<T*>(smem);
+  int* tok = reinterpret_cast<int*>(smem + 2 * (size_t)TT * TP * sizeof(T));
+  for (int r = threadIdx.x; r < TT; r += kThreads) {
+    int t = -1;
+    if (r < rows) {
+      t = idx[j0 + r];
+      if ((unsigned)t >= (unsigned)p.T) { raise_error(kErrBadIndex); t = -1; }
+    }
+    tok[r] = t;
+  }
+  __syncthreads();
+  const int half = threadIdx.x >> 7;
+  const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + half];
+  T* out = half ? ov : ok;
+  if (d.rotation) dequant_half_rot<T, D, TT, true>(p, d, out, tok, s, j0, rows, tiles + half * TT * TP, half);
+  else dequant_half_rot<T, D, TT, false>(p, d, out, tok, s, j0, rows, tiles + half * TT * TP, half);
 }
 
 // ---------------------------------------------------------------------------
@@ -313,13 +442,7 @@ static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st) {
 template <typename T>
 static cudaError_t launch_dq_tile_d(const DequantParams& p, cudaStream_t st) {
   if (p.D == 64) return p.tt == 64 ? launch_dq_tile<T, 64, 64>(p, st) : launch_dq_tile<T, 64, 128>(p, st);
-  if (p.D == 128) {
-    if (p.tt == 64) return launch_dq_tile<T, 128, 64>(p, st);
-    if constexpr (sizeof(T) == 2) return launch_dq_tile<T, 128, 128>(p, st);
-  }
-  if constexpr (sizeof(T) == 2) {
-    if (p.D == 256 && p.tt == 64) return launch_dq_tile<T, 256, 64>(p, st);
-  }
+  if (p.D == 128) return p.tt == 64 ? launch_dq_tile<T, 128, 64>(p, st) : launch_dq_tile<T, 128, 128>(p, st);
   return cudaErrorInvalidConfiguration;
 }
 

@@ -139,6 +139,217 @@ __device__ __forceinline__ uint32_t code_of(float x, const GroupCoder& c) {
 }
 
 // ---------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest
+// operations per instruction, bitwise the same as two scalar ones)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ float lo2(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi2(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// Packed encoding of a run of N (even) elements of one group.
+//
+// Per pair of elements: a = x * inv; t = fl(a [+ zp, clamped] + magic) holds the
+// code in its low mantissa bits (bits(t) = bits(kMagic) + code); d = a - rint(a).
+// A pair whose |d| comes within tolerance of 0.5 sets its bit in the returned
+// mask; encode_fixup re-encodes only those pairs with the exact IEEE quotient.
+// Codes are packed little-end-first by Horner steps acc = acc * 2^SB + bits(t)
+// (mod 2^32); the constant contribution of bits(kMagic) is subtracted once per
+// word.
+// ---------------------------------------------------------------------------
+struct FastCoder {
+  float scale;  // fp32 coding scale
+  float inv;    // fl(1 / scale)
+  float zp;     // affine zero point (0 for symmetric)
+  float hi;     // affine clamp: qmax
+  float magic;  // kMagic + offset: packed symmetric -qmin, unpacked symmetric 128, affine 0
+  uint32_t flip;  // per-byte XOR applied to unpacked symmetric codes (0x80808080) or 0
+};
+
+template <bool AFF>
+__device__ __forceinline__ FastCoder fast_coder(const GroupCoder& g, bool packed, int bits) {
+  FastCoder c;
+  c.scale = g.scale;
+  c.inv = g.inv;
+  c.zp = g.zp;
+  c.hi = g.hi;
+  if (AFF) {
+    c.magic = kMagic;
+    c.flip = 0u;
+  } else if (packed) {
+    c.magic = kMagic + (float)(1 << (bits - 1));
+    c.flip = 0u;
+  } else {
+    c.magic = kMagic + 128.f;
+    c.flip = 0x80808080u;
+  }
+  return c;
+}
+
+// sum over the first `cnt` element slots of a word of bits(kMagic) << (SB * i), mod 2^32
+template <int SB>
+__host__ __device__ constexpr uint32_t magic_sum(int cnt) {
+  uint32_t s = 0;
+  for (int i = 0; i < cnt; ++i) s += 0x4B400000u << (SB * i);
+  return s;
+}
+
+// per-byte flip restricted to the bytes of `cnt` slots
+template <int SB>
+__host__ __device__ constexpr uint32_t slot_mask(int cnt) {
+  return cnt * SB >= 32 ? 0xFFFFFFFFu : ((1u << (cnt * SB)) - 1u);
+}
+
+// Symmetric quotients are bounded by qmax (|a| <= 127): the fast quotient's error
+// stays below 2^-15, the tolerance below is 2^-12.  Affine quotients scale with
+// |a|: tolerance 2^-16 + |a| 2^-21.
+constexpr float kSymLimit = 0.5f - 2.44140625e-04f;
+
+template <int SB, bool AFF, int N>
+__device__ __forceinline__ uint32_t encode_fast(const float* x, const FastCoder& c, uint32_t* w) {
+  static_assert(N % 2 == 0, "pairs");
+  constexpr int EPW = 32 / SB;  // elements per 32-bit word
+  constexpr int NW = (N * SB + 31) / 32;
+  const uint64_t inv2 = pk2(c.inv, c.inv), mg2 = pk2(c.magic, c.magic), zp2 = pk2(c.zp, c.zp);
+  uint32_t near = 0;
+#pragma unroll
+  for (int q = 0; q < NW; ++q) {
+    const int first = q * EPW;
+    const int cnt = (N - first) < EPW ? (N - first) : EPW;
+    uint32_t acc = 0;
+#pragma unroll
+    for (int j = EPW / 2 - 1; j >= 0; --j) {
+      if (2 * j >= cnt) continue;
+      const int e = first + 2 * j;
+      uint64_t a2 = mul2(pk2(x[e], x[e + 1]), inv2);
+      float tol0 = 0.f, tol1 = 0.f;
+      if (AFF) {
+        tol0 = __fmaf_rn(fabsf(lo2(a2)), 4.76837158203125e-07f, 1.52587890625e-05f);
+        tol1 = __fmaf_rn(fabsf(hi2(a2)), 4.76837158203125e-07f, 1.52587890625e-05f);
+        a2 = add2(a2, zp2);
+        a2 = pk2(fminf(fmaxf(lo2(a2), 0.f), c.hi), fminf(fmaxf(hi2(a2), 0.f), c.hi));
+      }
+      const uint64_t t2 = add2(a2, mg2);
+      const uint64_t d2 = sub2(a2, sub2(t2, mg2));
+      const bool nr = AFF ? (fabsf(lo2(d2)) + tol0 > 0.5f) | (fabsf(hi2(d2)) + tol1 > 0.5f)
+                          : fmaxf(fabsf(lo2(d2)), fabsf(hi2(d2))) > kSymLimit;
+      if (nr) near |= 1u << (e >> 1);
+      acc = acc * (1u << SB) + (uint32_t)(t2 >> 32);
+      acc = acc * (1u << SB) + (uint32_t)t2;
+    }
+    w[q] = (acc - magic_sum<SB>(cnt)) ^ (c.flip & slot_mask<SB>(cnt));
+  }
+  return near;
+}
+
+// Exact re-encoding of the flagged pairs: `fetch(i)` re-reads element i (from
+// shared memory); each element of a flagged pair takes the IEEE quotient, the
+// reference's operation.  Rare, kept out of line so it costs no registers on the
+// fast path.
+template <int SB, bool AFF, int N, typename Fetch>
+__device__ __noinline__ void encode_fixup(Fetch fetch, const FastCoder& c, uint32_t* w, uint32_t near) {
+  constexpr int EPW = 32 / SB;
+  constexpr int NW = (N * SB + 31) / 32;
+  while (near) {
+    const int pair = __ffs(near) - 1;
+    near &= near - 1;
+#pragma unroll 1
+    for (int u = 0; u < 2; ++u) {
+      const int e = 2 * pair + u;
+      float a = __fdiv_rn(fetch(e), c.scale);
+      if (AFF) a = fminf(fmaxf(__fadd_rn(a, c.zp), 0.f), c.hi);
+      uint32_t code = (__float_as_uint(__fadd_rn(a, c.magic)) - __float_as_uint(kMagic)) & ((1u << SB) - 1u);
+      const int sh = (e % EPW) * SB;
+      code ^= (c.flip >> sh) & ((1u << SB) - 1u);
+      const uint32_t m = ((1u << SB) - 1u) << sh;
+#pragma unroll
+      for (int q = 0; q < NW; ++q)
+        if (q == e / EPW) w[q] = (w[q] & ~m) | (code << sh);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fast Walsh-Hadamard butterflies of a row spread over a warp, lane holding EPL
+// consecutive elements.  Stages run in the reference order h = 1, 2, 4, ...
+// (core.py:950-955); every output is one fp32 add or subtract of the previous
+// stage, as there.  Cross-lane stages compute o + sign * v with one fused
+// multiply-add (sign +1: v + o on the left lane, -1: o - v on the right lane).
+// ---------------------------------------------------------------------------
+template <int EPL>
+__device__ __forceinline__ void fwht_warp(float (&v)[EPL]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 1; h < EPL; h <<= 1) {
+    if constexpr (EPL >= 4) {
+      // two butterflies per packed add / subtract
+#pragma unroll
+      for (int i = 0; i < EPL; i += 2 * h) {
+#pragma unroll
+        for (int j = 0; j < h; j += 2) {
+          const int a = i + j;
+          if (h == 1) {
+            // pairs (a, a+1) and (a+2, a+3)
+            if ((a & 3) != 0) continue;
+            const uint64_t l = pk2(v[a], v[a + 2]), r = pk2(v[a + 1], v[a + 3]);
+            const uint64_t s = add2(l, r), df = sub2(l, r);
+            v[a] = lo2(s); v[a + 2] = hi2(s); v[a + 1] = lo2(df); v[a + 3] = hi2(df);
+          } else {
+            const uint64_t l = pk2(v[a], v[a + 1]), r = pk2(v[a + h], v[a + h + 1]);
+            const uint64_t s = add2(l, r), df = sub2(l, r);
+            v[a] = lo2(s); v[a + 1] = hi2(s); v[a + h] = lo2(df); v[a + h + 1] = hi2(df);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        if ((i & h) == 0) {
+          const float a = v[i], b = v[i + h];
+          v[i] = __fadd_rn(a, b);
+          v[i + h] = __fsub_rn(a, b);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const float sg = (lane & m) ? -1.f : 1.f;
+    const uint64_t sg2 = pk2(sg, sg);
+#pragma unroll
+    for (int i = 0; i < EPL; i += 2) {
+      const float o0 = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+      const float o1 = __shfl_xor_sync(0xFFFFFFFFu, v[i + 1], m);
+      const uint64_t r = fma2(sg2, pk2(v[i], v[i + 1]), pk2(o0, o1));
+      v[i] = lo2(r);
+      v[i + 1] = hi2(r);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Hadamard helpers (core.py:945-956)
 // ---------------------------------------------------------------------------
 // y / divisor rounded to T.  For bf16 a product with the reciprocal is accurate to a
@@ -240,6 +451,43 @@ __device__ __forceinline__ void store_bytes(uint8_t* dst, const uint32_t* w) {
     *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Code extraction: 2^23 + code as an fp32 bit pattern, one byte permute per code.
+// `nib[k]` holds code k of a word in the low byte of byte k' of one of the masked
+// words below; PRMT places that byte under the exponent byte 0x4B.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t with_magic(uint32_t src, int byte) {
+  return __byte_perm(src, 0x4B000000u, 0x7540u | (uint32_t)byte);
+}
+
+// 32 / SB codes of one 32-bit word, in element order, as fp32 bit patterns 2^23 + code
+template <int SB>
+__device__ __forceinline__ void word_codes(uint32_t w, uint32_t (&out)[32 / SB]) {
+  if constexpr (SB == 8) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out[k] = with_magic(w, k);
+  } else if constexpr (SB == 4) {
+    const uint32_t ev = w & 0x0F0F0F0Fu, od = (w >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      out[2 * k] = with_magic(ev, k);
+      out[2 * k + 1] = with_magic(od, k);
+    }
+  } else {
+    uint32_t m[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) m[j] = (w >> (2 * j)) & 0x03030303u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) out[4 * k + j] = with_magic(m[j], k);
+  }
+}
+
+__device__ __forceinline__ void bar_half(int half) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -9,6 +9,8 @@ namespace gkv {
 constexpr int kThreads = 256;    // threads per block of the tile kernels
 constexpr int kMaxLayers = 40;   // layers per launch (larger calls are split)
 constexpr int kRetTile = 64;     // retained rows per tile
+constexpr int kRun = 32;         // elements of one thread's run along the grouped axis (tile kernels)
+constexpr int kTokRun = 16;      // rows of one thread's run of a token-axis quantizer
 
 // Tier numbering inside the kernels: 0 retained, 1 standard, 2 cold.
 // Tensor numbering follows gkv_tensor_slot: 0 std K, 1 std V, 2 cold K, 3 cold V.

@@ -74,202 +74,228 @@ __device__ void copy_retained_tile(const QuantParams& p, const T* kb, const T* v
   }
 }
 
-// Hadamard rotation of `rows` rows held in shared memory, one warp per row.
-// Butterfly stages run in the reference order h = 1, 2, 4, ... (core.py:950-955).
+// Hadamard rotation of `rows` rows held in shared memory, one warp per row, by the
+// 4 warps of one half-block.
 template <typename T, int D>
-__device__ void rotate_rows_smem(T* sx, int rows, float div, float inv) {
+__device__ void rotate_rows_half(T* sx, int rows, float div, float inv, int hw) {
   using G = RowGeom<T, D>;
   constexpr int EPL = D / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int r = warp; r < rows; r += kThreads / 32) {
+  const int lane = threadIdx.x & 31;
+  for (int r = hw; r < rows; r += 4) {
     T* row = sx + r * G::kPitch + lane * EPL;
     float v[EPL];
 #pragma unroll
     for (int i = 0; i < EPL; ++i) v[i] = Elem<T>::to_f32(row[i]);
-#pragma unroll
-    for (int h = 1; h < EPL; h <<= 1) {
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) {
-        if ((i & h) == 0) {
-          const float a = v[i], b = v[i + h];
-          v[i] = __fadd_rn(a, b);
-          v[i + h] = __fsub_rn(a, b);
-        }
-      }
-    }
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-      const bool right = (lane & m) != 0;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) {
-        const float o = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
-        v[i] = right ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
-      }
-    }
+    fwht_warp<EPL>(v);
 #pragma unroll
     for (int i = 0; i < EPL; ++i) row[i] = hadamard_scale<T>(v[i], div, inv);
   }
 }
 
+
 // Token-axis groups (keys by default): groups of gs consecutive tier rows of one
-// channel.  Thread (word w, segment seg) holds SEG rows of 32-bit words.
+// channel.  Item = (32-bit column word w, run of 16 rows); a word holds one fp32 or
+// two 16-bit channels.  Phase 1 writes every run's extrema to shared memory (red,
+// [TT/16][D][2] floats); after the half-block barrier phase 2 combines the runs of
+// each group, re-reads the run's values and encodes them.
 template <typename T, int D, int TT, int SB, bool AFF>
-__device__ void quant_token_tile(const TensorDesc& d, const T* sx, int gslice, int j0, float* red) {
+__device__ void quant_token_half(const TensorDesc& d, const T* sx, int gslice, int j0, float* red, int half) {
   using G = RowGeom<T, D>;
   constexpr int W = G::kWords;
-  constexpr int SEG = TT / G::kSegs;
   constexpr int CPW = 4 / (int)sizeof(T);
-  const int tid = threadIdx.x;
-  const int w = tid % W, seg = tid / W;
-
-  uint32_t x[SEG];
+  constexpr int RUN = kTokRun;
+  constexpr int NRUN = TT / RUN;
+  constexpr int ITEMS = W * NRUN;
+  constexpr int ITER = (ITEMS + 127) / 128;
+  constexpr int NW = (RUN * SB + 31) / 32;  // code words per channel
+  constexpr int WSTRIDE = G::kPitch * (int)sizeof(T) / 4;  // row stride in 32-bit words
+  const int ht = threadIdx.x & 127;
+  const int rpg = d.gs / RUN;  // runs per group (host guarantees gs >= 32, a multiple of RUN)
+#pragma unroll 1
+  for (int itn = 0; itn < ITER; ++itn) {
+    const int item = ht + itn * 128;
+    if (item >= ITEMS) break;
+    const int w = item % W, run = item / W;
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (run * RUN) * G::kPitch) + w;
+    float mn[CPW], mx[CPW];
 #pragma unroll
-  for (int i = 0; i < SEG; ++i) x[i] = reinterpret_cast<const uint32_t*>(sx + (seg * SEG + i) * G::kPitch)[w];
-
-  float mn[CPW], mx[CPW];
+    for (int c = 0; c < CPW; ++c) { mn[c] = __int_as_float(0x7f800000); mx[c] = AFF ? -__int_as_float(0x7f800000) : 0.f; }
 #pragma unroll
-  for (int c = 0; c < CPW; ++c) { mn[c] = __int_as_float(0x7f800000); mx[c] = -__int_as_float(0x7f800000); }
+    for (int i = 0; i < RUN; ++i) {
+      float f[CPW];
+      unpack_word<T>(col[i * WSTRIDE], f);
 #pragma unroll
-  for (int i = 0; i < SEG; ++i) {
-    float f[CPW];
-    unpack_word<T>(x[i], f);
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      if (AFF) { mn[c] = fminf(mn[c], f[c]); mx[c] = fmaxf(mx[c], f[c]); }
-      else { mx[c] = fmaxf(mx[c], fabsf(f[c])); }
-    }
-  }
-  const int spg = d.gs / SEG;  // segments per group (host guarantees gs >= SEG, TT % gs == 0)
-  if (spg > 1) {
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      const int ch = w * CPW + c;
-      red[(seg * D + ch) * 2 + 0] = mn[c];
-      red[(seg * D + ch) * 2 + 1] = mx[c];
-    }
-    __syncthreads();
-    const int s0 = (seg / spg) * spg;
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      const int ch = w * CPW + c;
-      for (int q = 0; q < spg; ++q) {
-        if (AFF) mn[c] = fminf(mn[c], red[((s0 + q) * D + ch) * 2 + 0]);
-        mx[c] = fmaxf(mx[c], red[((s0 + q) * D + ch) * 2 + 1]);
+      for (int c = 0; c < CPW; ++c) {
+        if (AFF) { mn[c] = fminf(mn[c], f[c]); mx[c] = fmaxf(mx[c], f[c]); }
+        else mx[c] = fmaxf(mx[c], fabsf(f[c]));
       }
     }
-    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      red[(run * D + w * CPW + c) * 2 + 0] = mn[c];
+      red[(run * D + w * CPW + c) * 2 + 1] = mx[c];
+    }
   }
-  const int tok0 = j0 + (seg / spg) * d.gs;  // first tier row of this thread's group
-  if (tok0 >= d.n_pad) return;
-  const int g = tok0 >> d.log2gs;
+  bar_half(half);
+#pragma unroll 1
+  for (int itn = 0; itn < ITER; ++itn) {
+    const int item = ht + itn * 128;
+    const bool act = item < ITEMS;
+    const int w = act ? item % W : 0, run = act ? item / W : 0;
+    const int tok0 = j0 + run * RUN;  // first tier row of the run
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (run * RUN) * G::kPitch) + w;
+    float xf[CPW][RUN];
 #pragma unroll
-  for (int c = 0; c < CPW; ++c) {
-    const int ch = w * CPW + c;
-    const GroupCoder cd = AFF ? make_affine(mn[c], mx[c], d.bits) : make_symmetric(mx[c], d.bits, d.packed != 0);
-    if (seg % spg == 0) {
-      const int64_t gi = ((int64_t)gslice * D + ch) * d.groups_row + g;
-      store_scale(d.scales, gi, d.scale_dtype, cd.scale);
-      if (AFF) d.zps[gi] = (uint8_t)cd.zpi;
-    }
-    constexpr int NW = (SEG * SB + 31) / 32;
-    uint32_t out[NW];
-#pragma unroll
-    for (int q = 0; q < NW; ++q) out[q] = 0;
-#pragma unroll
-    for (int i = 0; i < SEG; ++i) {
+    for (int i = 0; i < RUN; ++i) {
       float f[CPW];
-      unpack_word<T>(x[i], f);
-      const uint32_t code = code_of(f[c], cd) & ((1u << SB) - 1u);
-      out[(i * SB) / 32] |= code << ((i * SB) % 32);
+      unpack_word<T>(col[i * WSTRIDE], f);
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) xf[c][i] = f[c];
     }
-    const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + j0 + seg * SEG;
-    store_bytes<SEG * SB / 8>(d.codes + (e0 * SB) / 8, out);
+    float mn[CPW], mx[CPW];
+    const int r0 = (run / rpg) * rpg;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      mn[c] = __int_as_float(0x7f800000);
+      mx[c] = AFF ? -__int_as_float(0x7f800000) : 0.f;
+      for (int q = 0; q < rpg; ++q) {
+        if (AFF) mn[c] = fminf(mn[c], red[((r0 + q) * D + w * CPW + c) * 2 + 0]);
+        mx[c] = fmaxf(mx[c], red[((r0 + q) * D + w * CPW + c) * 2 + 1]);
+      }
+    }
+    uint32_t out[CPW][NW];
+    FastCoder fc[CPW];
+    uint32_t near[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const GroupCoder gc = AFF ? make_affine(mn[c], mx[c], d.bits) : make_symmetric(mx[c], d.bits, d.packed != 0);
+      fc[c] = fast_coder<AFF>(gc, d.packed != 0, d.bits);
+      near[c] = encode_fast<SB, AFF, RUN>(xf[c], fc[c], out[c]);
+    }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      if (__any_sync(0xFFFFFFFFu, near[c] != 0) && near[c]) {
+        const T* colc = sx + (run * RUN) * G::kPitch + w * CPW + c;
+        encode_fixup<SB, AFF, RUN>([colc](int i) { return Elem<T>::to_f32(colc[i * G::kPitch]); }, fc[c],
+                                   out[c], near[c]);
+      }
+    }
+    if (act && tok0 < d.n_pad) {
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) {
+        const int ch = w * CPW + c;
+        if (run % rpg == 0) {
+          const int64_t gi = ((int64_t)gslice * D + ch) * d.groups_row + (tok0 >> d.log2gs);
+          store_scale(d.scales, gi, d.scale_dtype, fc[c].scale);
+          if (AFF) d.zps[gi] = (uint8_t)fc[c].zp;
+        }
+        const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + tok0;
+        store_bytes<RUN * SB / 8>(d.codes + (e0 * SB) / 8, out[c]);
+      }
+    }
   }
 }
 
 // Channel-axis groups (values by default): groups of gs consecutive channels of one
-// token.  Thread per 16-byte chunk; the gs / VEC chunks of a group are adjacent lanes.
+// token.  Item = (tier row, run of 32 channels); the runs of a row sit in adjacent
+// lanes, so group extrema combine with shuffles.
 template <typename T, int D, int TT, int SB, bool AFF>
-__device__ void quant_channel_tile(const TensorDesc& d, const T* sx, int gslice, int j0, int rows) {
+__device__ void quant_channel_half(const TensorDesc& d, const T* sx, int gslice, int j0, int rows) {
   using G = RowGeom<T, D>;
-  constexpr int VEC = G::kVec;
-  constexpr int CPR = G::kChunks;
-  constexpr int EPW = 4 / (int)sizeof(T);
-  const int cpg = d.gs / VEC;
-  for (int it = threadIdx.x; it < TT * CPR; it += kThreads) {
-    const int r = it / CPR, c = it - r * CPR;
-    const uint4 raw = *reinterpret_cast<const uint4*>(sx + r * G::kPitch + c * VEC);
-    const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-    float v[VEC];
+  constexpr int RPR = D / kRun;  // runs per row
+  constexpr int ITEMS = TT * RPR;
+  constexpr int ITER = (ITEMS + 127) / 128;
+  constexpr int NW = kRun * SB / 32;
+  constexpr int VPL = kRun * (int)sizeof(T) / 16;  // 16-byte vectors per run
+  const int ht = threadIdx.x & 127;
+  const int tpg = d.gs / kRun;  // runs (lanes) per group
+#pragma unroll 1
+  for (int itn = 0; itn < ITER; ++itn) {
+    const int item = ht + itn * 128;
+    const int r = item / RPR, run = item % RPR;
+    const bool act = item < ITEMS && r < rows;
+    float v[kRun];
+    float mn = __int_as_float(0x7f800000), mx = AFF ? -__int_as_float(0x7f800000) : 0.f;
+    if (item < ITEMS) {  // rows past the tier end hold zeros; read them to keep lanes converged
+      const uint4* src = reinterpret_cast<const uint4*>(sx + r * G::kPitch + run * kRun);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float f[EPW];
-      unpack_word<T>(wv[q], f);
+      for (int q = 0; q < VPL; ++q) {
+        const uint4 raw = src[q];
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-      for (int u = 0; u < EPW; ++u) v[q * EPW + u] = f[u];
+        for (int u = 0; u < 4; ++u) {
+          float f[4 / sizeof(T)];
+          unpack_word<T>(wv[u], f);
+#pragma unroll
+          for (int e = 0; e < (int)(4 / sizeof(T)); ++e) v[(q * 4 + u) * (4 / sizeof(T)) + e] = f[e];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRun; ++i) {
+        if (AFF) { mn = fminf(mn, v[i]); mx = fmaxf(mx, v[i]); }
+        else mx = fmaxf(mx, fabsf(v[i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kRun; ++i) v[i] = 0.f;
     }
-    float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      if (AFF) { mn = fminf(mn, v[i]); mx = fmaxf(mx, v[i]); }
-      else mx = fmaxf(mx, fabsf(v[i]));
-    }
-    for (int m = 1; m < cpg; m <<= 1) {
+    for (int m = 1; m < tpg; m <<= 1) {
       if (AFF) mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, m));
       mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, m));
     }
-    if (r < rows) {
-      const GroupCoder cd = AFF ? make_affine(mn, mx, d.bits) : make_symmetric(mx, d.bits, d.packed != 0);
+    const GroupCoder gc = AFF ? make_affine(mn, mx, d.bits) : make_symmetric(mx, d.bits, d.packed != 0);
+    const FastCoder fc = fast_coder<AFF>(gc, d.packed != 0, d.bits);
+    uint32_t out[NW];
+    const uint32_t near = encode_fast<SB, AFF, kRun>(v, fc, out);
+    if (__any_sync(0xFFFFFFFFu, near != 0) && near) {
+      const T* chunk = sx + r * G::kPitch + run * kRun;
+      encode_fixup<SB, AFF, kRun>([chunk](int i) { return Elem<T>::to_f32(chunk[i]); }, fc, out, near);
+    }
+    if (act) {
       const int64_t row = (int64_t)gslice * d.n + j0 + r;
-      if ((c & (cpg - 1)) == 0) {
-        const int64_t gi = row * d.groups_row + c / cpg;
-        store_scale(d.scales, gi, d.scale_dtype, cd.scale);
-        if (AFF) d.zps[gi] = (uint8_t)cd.zpi;
+      if (run % tpg == 0) {
+        const int64_t gi = row * d.groups_row + run / tpg;
+        store_scale(d.scales, gi, d.scale_dtype, fc.scale);
+        if (AFF) d.zps[gi] = (uint8_t)fc.zp;
       }
-      constexpr int NW = (VEC * SB + 31) / 32;
-      uint32_t out[NW];
-#pragma unroll
-      for (int q = 0; q < NW; ++q) out[q] = 0;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        const uint32_t code = code_of(v[i], cd) & ((1u << SB) - 1u);
-        out[(i * SB) / 32] |= code << ((i * SB) % 32);
-      }
-      const int64_t e0 = row * d.n_pad + c * VEC;
-      store_bytes<VEC * SB / 8>(d.codes + (e0 * SB) / 8, out);
+      const int64_t e0 = row * d.n_pad + run * kRun;
+      store_bytes<kRun * SB / 8>(d.codes + (e0 * SB) / 8, out);
     }
   }
 }
 
 template <typename T, int D, int TT, int SB>
-__device__ __forceinline__ void quant_tensor_sb(const TensorDesc& d, const T* sx, int gslice, int j0, int rows,
-                                                float* red) {
+__device__ __forceinline__ void quant_half_sb(const TensorDesc& d, const T* sx, int gslice, int j0, int rows,
+                                              float* red, int half) {
   const bool aff = d.quantizer == GKV_AFFINE;
   if (d.axis == GKV_AXIS_TOKEN) {
-    if (aff) quant_token_tile<T, D, TT, SB, true>(d, sx, gslice, j0, red);
-    else quant_token_tile<T, D, TT, SB, false>(d, sx, gslice, j0, red);
+    if (aff) quant_token_half<T, D, TT, SB, true>(d, sx, gslice, j0, red, half);
+    else quant_token_half<T, D, TT, SB, false>(d, sx, gslice, j0, red, half);
   } else {
-    if (aff) quant_channel_tile<T, D, TT, SB, true>(d, sx, gslice, j0, rows);
-    else quant_channel_tile<T, D, TT, SB, false>(d, sx, gslice, j0, rows);
+    if (aff) quant_channel_half<T, D, TT, SB, true>(d, sx, gslice, j0, rows);
+    else quant_channel_half<T, D, TT, SB, false>(d, sx, gslice, j0, rows);
   }
 }
 
 template <typename T, int D, int TT>
-__device__ __forceinline__ void quant_tensor(const TensorDesc& d, const T* sx, int gslice, int j0, int rows,
-                                             float* red) {
-  if (d.sbits == 4) quant_tensor_sb<T, D, TT, 4>(d, sx, gslice, j0, rows, red);
-  else if (d.sbits == 2) quant_tensor_sb<T, D, TT, 2>(d, sx, gslice, j0, rows, red);
-  else quant_tensor_sb<T, D, TT, 8>(d, sx, gslice, j0, rows, red);
+__device__ __forceinline__ void quant_half(const TensorDesc& d, const T* sx, int gslice, int j0, int rows, float* red,
+                                           int half) {
+  if (d.sbits == 4) quant_half_sb<T, D, TT, 4>(d, sx, gslice, j0, rows, red, half);
+  else if (d.sbits == 2) quant_half_sb<T, D, TT, 2>(d, sx, gslice, j0, rows, red, half);
+  else quant_half_sb<T, D, TT, 8>(d, sx, gslice, j0, rows, red, half);
 }
 
 template <typename T, int D, int TT>
 constexpr size_t quant_tile_smem() {
   using G = RowGeom<T, D>;
-  return 2 * (size_t)TT * G::kPitch * sizeof(T) + (size_t)G::kSegs * D * 2 * sizeof(float) + 16;
+  return 2 * (size_t)TT * G::kPitch * sizeof(T) + 2 * (size_t)(TT / kTokRun) * D * 2 * sizeof(float) + 16;
 }
 
+// One block per tile: retained-row tiles copy; standard / cold tiles gather the K and
+// V rows into shared memory (bulk copies), then warps 0-3 quantize K and warps 4-7
+// quantize V, each half on its own named barrier.
 template <typename T, int D, int TT>
-__global__ void __launch_bounds__(kThreads) quantize_tile_kernel(const __grid_constant__ QuantParams p) {
+__global__ void __launch_bounds__(kThreads, 3) quantize_tile_kernel(const __grid_constant__ QuantParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = RowGeom<T, D>;
   const int s = blockIdx.x / p.tiles_slice;
@@ -288,8 +314,6 @@ __global__ void __launch_bounds__(kThreads) quantize_tile_kernel(const __grid_co
   k -= p.tiles[0];
   int tier = 1;
   if (k >= p.tiles[1]) { k -= p.tiles[1]; tier = 2; }
-  const TensorDesc& dk = p.t[tier == 1 ? GKV_STD_K : GKV_COLD_K];
-  const TensorDesc& dv = p.t[tier == 1 ? GKV_STD_V : GKV_COLD_V];
   const int* idx = p.idx[tier];
   const int n = p.n_tier[tier];
   const int j0 = k * TT;
@@ -298,7 +322,7 @@ __global__ void __launch_bounds__(kThreads) quantize_tile_kernel(const __grid_co
   T* sk = reinterpret_cast<T*>(smem);
   T* sv = sk + TT * G::kPitch;
   float* red = reinterpret_cast<float*>(sv + TT * G::kPitch);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(red + G::kSegs * D * 2);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 2 * (TT / kTokRun) * D * 2);
 
   if (threadIdx.x == 0) mbar_init(bar, 1);
   __syncthreads();
@@ -320,12 +344,14 @@ __global__ void __launch_bounds__(kThreads) quantize_tile_kernel(const __grid_co
   }
   if (!block_wait(bar, 0)) return;
 
-  if (dk.rotation) rotate_rows_smem<T, D>(sk, rows, p.had_div, p.had_inv);
-  if (dv.rotation) rotate_rows_smem<T, D>(sv, rows, p.had_div, p.had_inv);
-  if (dk.rotation | dv.rotation) __syncthreads();
-
-  quant_tensor<T, D, TT>(dk, sk, gslice, j0, rows, red);
-  quant_tensor<T, D, TT>(dv, sv, gslice, j0, rows, red);
+  const int half = threadIdx.x >> 7;
+  const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + half];
+  T* sx = half ? sv : sk;
+  if (d.rotation) {
+    rotate_rows_half<T, D>(sx, rows, p.had_div, p.had_inv, (threadIdx.x >> 5) & 3);
+    bar_half(half);
+  }
+  quant_half<T, D, TT>(d, sx, gslice, j0, rows, red + half * (TT / kTokRun) * D * 2, half);
 }
 
 // ---------------------------------------------------------------------------
@@ -505,13 +531,7 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
 template <typename T>
 static cudaError_t launch_tile_d(const QuantParams& p, cudaStream_t st) {
   if (p.D == 64) return p.tt == 64 ? launch_tile<T, 64, 64>(p, st) : launch_tile<T, 64, 128>(p, st);
-  if (p.D == 128) {
-    if (p.tt == 64) return launch_tile<T, 128, 64>(p, st);
-    if constexpr (sizeof(T) == 2) return launch_tile<T, 128, 128>(p, st);
-  }
-  if constexpr (sizeof(T) == 2) {
-    if (p.D == 256 && p.tt == 64) return launch_tile<T, 256, 64>(p, st);
-  }
+  if (p.D == 128) return p.tt == 64 ? launch_tile<T, 128, 64>(p, st) : launch_tile<T, 128, 128>(p, st);
   return cudaErrorInvalidConfiguration;
 }
 

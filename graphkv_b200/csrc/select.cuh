@@ -17,6 +17,7 @@ namespace {
 
 constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kSelSmemTokens = 40960;  // keys (4 B) + tier (1 B) per token fit in shared memory
 enum : uint8_t { kCand = 0, kRet = 1, kCold = 2 };
 
 struct SelectParams {
@@ -24,7 +25,7 @@ struct SelectParams {
   const float* outlier;
   int T, sink, tail, keep_protect, keep_outlier, keep_cold;
   int n_ret, n_std, n_cold;
-  uint8_t* tier;
+  uint8_t* tier;  // workspace (used when T exceeds kSelSmemTokens)
   int* idx_ret;
   int* idx_std;
   int* idx_cold;
@@ -41,41 +42,56 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 
 struct SelShared {
   uint32_t hist[256];
-  uint32_t warp_tot[kSelWarps];
-  uint32_t scan[kSelWarps];
+  uint32_t warp_cnt[3][kSelWarps];
+  uint32_t warp_off[3][kSelWarps];
   uint32_t prefix, mask, remaining;
 };
 
-// exclusive block scan of one flag per thread; returns the prefix, total in *total
-__device__ __forceinline__ uint32_t block_scan_flag(bool flag, SelShared& sh, uint32_t* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t bal = __ballot_sync(0xFFFFFFFFu, flag);
-  const uint32_t in_warp = __popc(bal & ((1u << lane) - 1u));
-  if (lane == 0) sh.warp_tot[warp] = __popc(bal);
+// Tokens handled by warp w in the ordered passes: one contiguous chunk per warp.
+struct Chunk {
+  int begin, end;
+};
+__device__ __forceinline__ Chunk warp_chunk(int T, int w) {
+  const int per = ((T + kSelWarps - 1) / kSelWarps + 31) & ~31;
+  const int b = min(T, w * per);
+  return {b, min(T, b + per)};
+}
+
+// Exclusive scan of the per-warp counters (n of them) into warp_off; one barrier pair.
+__device__ __forceinline__ void scan_warp_counts(SelShared& sh, int n) {
   __syncthreads();
-  if (warp == 0) {
-    const uint32_t v = sh.warp_tot[lane];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp < n) {
+    const uint32_t v = sh.warp_cnt[warp][lane];
     uint32_t inc = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
       if (lane >= o) inc += t;
     }
-    sh.scan[lane] = inc - v;
-    __syncwarp();
-    if (lane == 31) sh.warp_tot[0] = inc;  // block total (slot 0 was read above)
+    sh.warp_off[warp][lane] = inc - v;
   }
   __syncthreads();
-  const uint32_t r = sh.scan[warp] + in_warp;
-  *total = sh.warp_tot[0];
-  __syncthreads();
-  return r;
 }
 
-// Select `k` candidates (tier == kCand) with the largest (or smallest) keys of
-// `src` and give them tier `mark`.
-__device__ void select_mark(const SelectParams& p, const float* src, int k, bool largest, uint8_t mark,
-                            SelShared& sh) {
+template <bool SMEM>
+struct SelState {
+  const uint32_t* keys;  // shared-memory keys (SMEM) of the importance scores
+  uint8_t* tier;
+};
+
+template <bool SMEM>
+__device__ __forceinline__ uint32_t key_at(const SelState<SMEM>& st, const float* src, int t) {
+  if (SMEM && src == nullptr) return st.keys[t];
+  return order_key(src[t]);
+}
+
+// Select `k` candidates (tier == kCand) with the largest (or smallest) keys and
+// give them tier `mark`.  src == nullptr: the importance scores (cached keys).
+template <bool SMEM>
+__device__ void select_mark(const SelectParams& p, const SelState<SMEM>& st, const float* src, int k, bool largest,
+                            uint8_t mark, SelShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) { sh.prefix = 0; sh.mask = 0; sh.remaining = (uint32_t)k; }
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
@@ -86,8 +102,8 @@ __device__ void select_mark(const SelectParams& p, const float* src, int k, bool
       const int t = base + threadIdx.x;
       bool act = false;
       uint32_t digit = 0;
-      if (t < p.T && p.tier[t] == kCand) {
-        const uint32_t key = order_key(src[t]);
+      if (t < p.T && st.tier[t] == kCand) {
+        const uint32_t key = key_at<SMEM>(st, src, t);
         if ((key & mask) == prefix) {
           act = true;
           digit = (key >> shift) & 0xFFu;
@@ -96,71 +112,136 @@ __device__ void select_mark(const SelectParams& p, const float* src, int k, bool
       const uint32_t am = __ballot_sync(0xFFFFFFFFu, act);
       if (act) {
         const uint32_t peers = __match_any_sync(am, digit);
-        if ((threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&sh.hist[digit], __popc(peers));
+        if (lane == (__ffs(peers) - 1)) atomicAdd(&sh.hist[digit], __popc(peers));
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t rem = sh.remaining;
-      uint32_t cum = 0;
-      int d = 0;
-      for (int step = 0; step < 256; ++step) {
-        d = largest ? 255 - step : step;
-        const uint32_t c = sh.hist[d];
-        if (cum + c >= rem) break;
-        cum += c;
+    if (warp == 0) {
+      // lane l owns 8 bins in scan order (descending digits for `largest`)
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int bin = largest ? 255 - (lane * 8 + j) : lane * 8 + j;
+        c[j] = sh.hist[bin];
+        sum += c[j];
       }
-      sh.remaining = rem - cum;
-      sh.prefix = prefix | ((uint32_t)d << shift);
-      sh.mask = mask | (0xFFu << shift);
+      uint32_t inc = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      const uint32_t rem = sh.remaining;
+      const uint32_t before = inc - sum;
+      const uint32_t hit = __ballot_sync(0xFFFFFFFFu, before < rem && inc >= rem);
+      if (hit == 0) {
+        // fewer candidates than requested: the count check at the end reports it
+        if (lane == 0) { sh.remaining = rem; sh.prefix = prefix; sh.mask = mask | (0xFFu << shift); }
+      } else if (lane == __ffs(hit) - 1) {
+        uint32_t cum = before;
+        int j = 0;
+        for (; j < 8; ++j) {
+          if (cum + c[j] >= rem) break;
+          cum += c[j];
+        }
+        const int bin = largest ? 255 - (lane * 8 + j) : lane * 8 + j;
+        sh.remaining = rem - cum;
+        sh.prefix = prefix | ((uint32_t)bin << shift);
+        sh.mask = mask | (0xFFu << shift);
+      }
     }
     __syncthreads();
   }
   const uint32_t tau = sh.prefix;
   const uint32_t take_eq = sh.remaining;
-  uint32_t running = 0;
-  for (int base = 0; base < p.T; base += kSelThreads) {
-    const int t = base + threadIdx.x;
+  const Chunk ch = warp_chunk(p.T, warp);
+  // pass 1: candidates equal to the k-th key, per warp chunk
+  uint32_t cnt = 0;
+  for (int b = ch.begin; b < ch.end; b += 32) {
+    const int t = b + lane;
+    const bool eq = t < ch.end && st.tier[t] == kCand && key_at<SMEM>(st, src, t) == tau;
+    cnt += __popc(__ballot_sync(0xFFFFFFFFu, eq));
+  }
+  if (lane == 0) sh.warp_cnt[0][warp] = cnt;
+  scan_warp_counts(sh, 1);
+  // pass 2: mark keys beyond the k-th, and the first take_eq equal ones in token order
+  uint32_t running = sh.warp_off[0][warp];
+  for (int b = ch.begin; b < ch.end; b += 32) {
+    const int t = b + lane;
     bool cand = false, beyond = false, eq = false;
-    if (t < p.T && p.tier[t] == kCand) {
+    if (t < ch.end && st.tier[t] == kCand) {
       cand = true;
-      const uint32_t key = order_key(src[t]);
+      const uint32_t key = key_at<SMEM>(st, src, t);
       beyond = largest ? key > tau : key < tau;
       eq = key == tau;
     }
-    uint32_t total;
-    const uint32_t pos = block_scan_flag(eq, sh, &total);
-    if (cand && (beyond || (eq && running + pos < take_eq))) p.tier[t] = mark;
-    running += total;
+    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, eq);
+    const uint32_t pos = running + __popc(bal & ((1u << lane) - 1u));
+    if (cand && (beyond || (eq && pos < take_eq))) st.tier[t] = mark;
+    running += __popc(bal);
   }
   __syncthreads();
 }
 
+template <bool SMEM>
+__device__ void select_body(const SelectParams& p, SelState<SMEM> st, SelShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t = threadIdx.x; t < p.T; t += kSelThreads) {
+    st.tier[t] = (t < p.sink || t >= p.T - p.tail) ? kRet : kCand;
+    if (SMEM && p.scores) const_cast<uint32_t*>(st.keys)[t] = order_key(p.scores[t]);
+  }
+  __syncthreads();
+  if (p.keep_protect > 0) select_mark<SMEM>(p, st, SMEM ? nullptr : p.scores, p.keep_protect, true, kRet, sh);
+  if (p.keep_outlier > 0) select_mark<SMEM>(p, st, p.outlier, p.keep_outlier, true, kRet, sh);
+  if (p.keep_cold > 0) select_mark<SMEM>(p, st, SMEM ? nullptr : p.scores, p.keep_cold, false, kCold, sh);
+  // ordered compaction of the three lists
+  const Chunk ch = warp_chunk(p.T, warp);
+  uint32_t n[3] = {0, 0, 0};
+  for (int b = ch.begin; b < ch.end; b += 32) {
+    const int t = b + lane;
+    const uint8_t c = t < ch.end ? st.tier[t] : 0xFF;
+    n[0] += __popc(__ballot_sync(0xFFFFFFFFu, c == kRet));
+    n[1] += __popc(__ballot_sync(0xFFFFFFFFu, c == kCand));
+    n[2] += __popc(__ballot_sync(0xFFFFFFFFu, c == kCold));
+  }
+  if (lane == 0) {
+    sh.warp_cnt[0][warp] = n[0];
+    sh.warp_cnt[1][warp] = n[1];
+    sh.warp_cnt[2][warp] = n[2];
+  }
+  scan_warp_counts(sh, 3);
+  uint32_t off[3] = {sh.warp_off[0][warp], sh.warp_off[1][warp], sh.warp_off[2][warp]};
+  int* const out[3] = {p.idx_ret, p.idx_std, p.idx_cold};
+  const uint32_t lim[3] = {(uint32_t)p.n_ret, (uint32_t)p.n_std, (uint32_t)p.n_cold};
+  const uint8_t code[3] = {kRet, kCand, kCold};
+  for (int b = ch.begin; b < ch.end; b += 32) {
+    const int t = b + lane;
+    const uint8_t c = t < ch.end ? st.tier[t] : 0xFF;
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, c == code[q]);
+      const uint32_t pos = off[q] + __popc(bal & ((1u << lane) - 1u));
+      if (c == code[q] && pos < lim[q]) out[q][pos] = t;
+      off[q] += __popc(bal);
+    }
+  }
+  if (threadIdx.x == 0) {
+    const uint32_t tot[3] = {sh.warp_off[0][31] + sh.warp_cnt[0][31], sh.warp_off[1][31] + sh.warp_cnt[1][31],
+                             sh.warp_off[2][31] + sh.warp_cnt[2][31]};
+    if (tot[0] != lim[0] || tot[1] != lim[1] || tot[2] != lim[2]) raise_error(kErrSelectCount);
+  }
+}
+
 __global__ void __launch_bounds__(kSelThreads) select_kernel(const SelectParams p) {
   __shared__ SelShared sh;
-  for (int t = threadIdx.x; t < p.T; t += kSelThreads)
-    p.tier[t] = (t < p.sink || t >= p.T - p.tail) ? kRet : kCand;
-  __syncthreads();
-  if (p.keep_protect > 0) select_mark(p, p.scores, p.keep_protect, true, kRet, sh);
-  if (p.keep_outlier > 0) select_mark(p, p.outlier, p.keep_outlier, true, kRet, sh);
-  if (p.keep_cold > 0) select_mark(p, p.scores, p.keep_cold, false, kCold, sh);
-  uint32_t nr = 0, ns = 0, nc = 0;
-  for (int base = 0; base < p.T; base += kSelThreads) {
-    const int t = base + threadIdx.x;
-    const uint8_t c = t < p.T ? p.tier[t] : 0xFF;
-    uint32_t tr, ts, tc;
-    const uint32_t pr = block_scan_flag(c == kRet, sh, &tr);
-    const uint32_t ps = block_scan_flag(c == kCand, sh, &ts);
-    const uint32_t pc = block_scan_flag(c == kCold, sh, &tc);
-    if (c == kRet && nr + pr < (uint32_t)p.n_ret) p.idx_ret[nr + pr] = t;
-    if (c == kCand && ns + ps < (uint32_t)p.n_std) p.idx_std[ns + ps] = t;
-    if (c == kCold && nc + pc < (uint32_t)p.n_cold) p.idx_cold[nc + pc] = t;
-    nr += tr;
-    ns += ts;
-    nc += tc;
+  extern __shared__ __align__(16) uint8_t sel_smem[];
+  if (p.T <= kSelSmemTokens) {
+    SelState<true> st{reinterpret_cast<const uint32_t*>(sel_smem), sel_smem + 4 * (size_t)kSelSmemTokens};
+    select_body<true>(p, st, sh);
+  } else {
+    SelState<false> st{nullptr, p.tier};
+    select_body<false>(p, st, sh);
   }
-  if (threadIdx.x == 0 && (nr != (uint32_t)p.n_ret || ns != (uint32_t)p.n_std || nc != (uint32_t)p.n_cold))
-    raise_error(kErrSelectCount);
 }
 
 // mean(K^2) + mean(V^2) per token: warp per token, fp64 accumulation
@@ -212,7 +293,10 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
   p.idx_ret = idx_ret;
   p.idx_std = idx_std;
   p.idx_cold = idx_cold;
-  select_kernel<<<1, kSelThreads, 0, st>>>(p);
+  const size_t sm = pol.seq_len <= kSelSmemTokens ? (size_t)kSelSmemTokens * 5 : 0;
+  cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  select_kernel<<<1, kSelThreads, sm, st>>>(p);
   return cudaGetLastError();
 }
 
