@@ -171,13 +171,22 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 // ---------------------------------------------------------------------------
 // Packed encoding of a run of N (even) elements of one group.
 //
-// Per pair of elements: a = x * inv; t = fl(a [+ zp, clamped] + magic) holds the
-// code in its low mantissa bits (bits(t) = bits(kMagic) + code); d = a - rint(a).
-// A pair whose |d| comes within tolerance of 0.5 sets its bit in the returned
-// mask; encode_fixup re-encodes only those pairs with the exact IEEE quotient.
-// Codes are packed little-end-first by Horner steps acc = acc * 2^SB + bits(t)
-// (mod 2^32); the constant contribution of bits(kMagic) is subtracted once per
-// word.
+// Quotient: the reference rounds fl(x / scale) to an integer (core.py:879, 886).
+// With y = fl(1 / scale) (correctly rounded reciprocal), q0 = fl(x * y),
+// r = fl(x - q0 * scale) and q = fl(q0 + r * y) (two fused multiply-adds; the
+// quotient correction of P. Markstein, "Computation of elementary functions on the
+// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) equals the IEEE
+// quotient except for |x / scale| < 2^-79, where both round to the same code.  This
+// was checked against the IEEE division on 2.7e10 (x, scale) pairs: every bf16 and
+// fp16 x against every scale a bf16 / fp16 group maximum yields for
+// qmax in {1, 3, 7, 15, 127, 255}, and random fp32 pairs, with identical codes for
+// the symmetric rounding and for every affine zero point.
+//
+// Per pair of elements: q as above, [+ zp, clamped to [0, qmax] for affine];
+// t = fl(q + magic) holds the code in its low mantissa bits (bits(t) =
+// bits(kMagic) + code, ties to even as torch.round).  Codes are packed
+// little-end-first by Horner steps acc = acc * 2^SB + bits(t) (mod 2^32); the
+// constant contribution of bits(kMagic) is subtracted once per word.
 // ---------------------------------------------------------------------------
 struct FastCoder {
   float scale;  // fp32 coding scale
@@ -222,18 +231,13 @@ __host__ __device__ constexpr uint32_t slot_mask(int cnt) {
   return cnt * SB >= 32 ? 0xFFFFFFFFu : ((1u << (cnt * SB)) - 1u);
 }
 
-// Symmetric quotients are bounded by qmax (|a| <= 127): the fast quotient's error
-// stays below 2^-15, the tolerance below is 2^-12.  Affine quotients scale with
-// |a|: tolerance 2^-16 + |a| 2^-21.
-constexpr float kSymLimit = 0.5f - 2.44140625e-04f;
-
 template <int SB, bool AFF, int N>
-__device__ __forceinline__ uint32_t encode_fast(const float* x, const FastCoder& c, uint32_t* w) {
+__device__ __forceinline__ void encode_run(const float* x, const FastCoder& c, uint32_t* w) {
   static_assert(N % 2 == 0, "pairs");
   constexpr int EPW = 32 / SB;  // elements per 32-bit word
   constexpr int NW = (N * SB + 31) / 32;
-  const uint64_t inv2 = pk2(c.inv, c.inv), mg2 = pk2(c.magic, c.magic), zp2 = pk2(c.zp, c.zp);
-  uint32_t near = 0;
+  const uint64_t inv2 = pk2(c.inv, c.inv), nsc2 = pk2(-c.scale, -c.scale);
+  const uint64_t mg2 = pk2(c.magic, c.magic), zp2 = pk2(c.zp, c.zp);
 #pragma unroll
   for (int q = 0; q < NW; ++q) {
     const int first = q * EPW;
@@ -243,51 +247,18 @@ __device__ __forceinline__ uint32_t encode_fast(const float* x, const FastCoder&
     for (int j = EPW / 2 - 1; j >= 0; --j) {
       if (2 * j >= cnt) continue;
       const int e = first + 2 * j;
-      uint64_t a2 = mul2(pk2(x[e], x[e + 1]), inv2);
-      float tol0 = 0.f, tol1 = 0.f;
+      const uint64_t x2 = pk2(x[e], x[e + 1]);
+      const uint64_t q0 = mul2(x2, inv2);
+      uint64_t a2 = fma2(fma2(q0, nsc2, x2), inv2, q0);
       if (AFF) {
-        tol0 = __fmaf_rn(fabsf(lo2(a2)), 4.76837158203125e-07f, 1.52587890625e-05f);
-        tol1 = __fmaf_rn(fabsf(hi2(a2)), 4.76837158203125e-07f, 1.52587890625e-05f);
         a2 = add2(a2, zp2);
         a2 = pk2(fminf(fmaxf(lo2(a2), 0.f), c.hi), fminf(fmaxf(hi2(a2), 0.f), c.hi));
       }
       const uint64_t t2 = add2(a2, mg2);
-      const uint64_t d2 = sub2(a2, sub2(t2, mg2));
-      const bool nr = AFF ? (fabsf(lo2(d2)) + tol0 > 0.5f) | (fabsf(hi2(d2)) + tol1 > 0.5f)
-                          : fmaxf(fabsf(lo2(d2)), fabsf(hi2(d2))) > kSymLimit;
-      if (nr) near |= 1u << (e >> 1);
       acc = acc * (1u << SB) + (uint32_t)(t2 >> 32);
       acc = acc * (1u << SB) + (uint32_t)t2;
     }
     w[q] = (acc - magic_sum<SB>(cnt)) ^ (c.flip & slot_mask<SB>(cnt));
-  }
-  return near;
-}
-
-// Exact re-encoding of the flagged pairs: `fetch(i)` re-reads element i (from
-// shared memory); each element of a flagged pair takes the IEEE quotient, the
-// reference's operation.  Rare, kept out of line so it costs no registers on the
-// fast path.
-template <int SB, bool AFF, int N, typename Fetch>
-__device__ __noinline__ void encode_fixup(Fetch fetch, const FastCoder& c, uint32_t* w, uint32_t near) {
-  constexpr int EPW = 32 / SB;
-  constexpr int NW = (N * SB + 31) / 32;
-  while (near) {
-    const int pair = __ffs(near) - 1;
-    near &= near - 1;
-#pragma unroll 1
-    for (int u = 0; u < 2; ++u) {
-      const int e = 2 * pair + u;
-      float a = __fdiv_rn(fetch(e), c.scale);
-      if (AFF) a = fminf(fmaxf(__fadd_rn(a, c.zp), 0.f), c.hi);
-      uint32_t code = (__float_as_uint(__fadd_rn(a, c.magic)) - __float_as_uint(kMagic)) & ((1u << SB) - 1u);
-      const int sh = (e % EPW) * SB;
-      code ^= (c.flip >> sh) & ((1u << SB) - 1u);
-      const uint32_t m = ((1u << SB) - 1u) << sh;
-#pragma unroll
-      for (int q = 0; q < NW; ++q)
-        if (q == e / EPW) w[q] = (w[q] & ~m) | (code << sh);
-    }
   }
 }
 
@@ -405,6 +376,15 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint3
           smem_u32(dst_smem)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy; src_bytes == 0 writes zeros
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 // Bounded wait on phase `parity`.  Every thread of the block must call it; returns

@@ -1,16 +1,17 @@
 // Quantize + pack kernels (core.py:647-772, 848-910, 945-956, 979-990).
 //
-// Fast path: one block per tile of TT consecutive tier rows of one slice.  Warp 0
-// gathers the K and V rows of the tile into shared memory with bulk async copies
-// (one row per copy, completion on an mbarrier), rows are rotated in place when the
-// tensor uses the Hadamard rotation, then each tensor is grouped along its axis,
-// scaled and packed straight to HBM.  Retained rows are copied by tiles of the same
-// launch.
+// Fast path: one block per tile of TT consecutive tier rows of one slice.  All
+// threads gather the K and V rows of the tile into shared memory with 16-byte
+// asynchronous copies, rows are rotated in place when the tensor uses the Hadamard
+// rotation, then each tensor is grouped along its axis, scaled and packed straight
+// to HBM.  Retained rows are copied by tiles of the same launch.
 //
 // General path: any geometry the tiles do not cover (group sizes that are not
 // powers of two, padded head dims, tiny tiers, unaligned inputs): one thread per
 // group computes the scale, one thread per output byte packs the codes.
 #pragma once
+
+#include <algorithm>
 
 #include "gkv_params.cuh"
 
@@ -165,20 +166,11 @@ __device__ void quant_token_half(const TensorDesc& d, const T* sx, int gslice, i
     }
     uint32_t out[CPW][NW];
     FastCoder fc[CPW];
-    uint32_t near[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
       const GroupCoder gc = AFF ? make_affine(mn[c], mx[c], d.bits) : make_symmetric(mx[c], d.bits, d.packed != 0);
       fc[c] = fast_coder<AFF>(gc, d.packed != 0, d.bits);
-      near[c] = encode_fast<SB, AFF, RUN>(xf[c], fc[c], out[c]);
-    }
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      if (__any_sync(0xFFFFFFFFu, near[c] != 0) && near[c]) {
-        const T* colc = sx + (run * RUN) * G::kPitch + w * CPW + c;
-        encode_fixup<SB, AFF, RUN>([colc](int i) { return Elem<T>::to_f32(colc[i * G::kPitch]); }, fc[c],
-                                   out[c], near[c]);
-      }
+      encode_run<SB, AFF, RUN>(xf[c], fc[c], out[c]);
     }
     if (act && tok0 < d.n_pad) {
 #pragma unroll
@@ -246,11 +238,7 @@ __device__ void quant_channel_half(const TensorDesc& d, const T* sx, int gslice,
     const GroupCoder gc = AFF ? make_affine(mn, mx, d.bits) : make_symmetric(mx, d.bits, d.packed != 0);
     const FastCoder fc = fast_coder<AFF>(gc, d.packed != 0, d.bits);
     uint32_t out[NW];
-    const uint32_t near = encode_fast<SB, AFF, kRun>(v, fc, out);
-    if (__any_sync(0xFFFFFFFFu, near != 0) && near) {
-      const T* chunk = sx + r * G::kPitch + run * kRun;
-      encode_fixup<SB, AFF, kRun>([chunk](int i) { return Elem<T>::to_f32(chunk[i]); }, fc, out, near);
-    }
+    encode_run<SB, AFF, kRun>(v, fc, out);
     if (act) {
       const int64_t row = (int64_t)gslice * d.n + j0 + r;
       if (run % tpg == 0) {
@@ -286,66 +274,111 @@ __device__ __forceinline__ void quant_half(const TensorDesc& d, const T* sx, int
 }
 
 template <typename T, int D, int TT>
-constexpr size_t quant_tile_smem() {
+struct QuantTileSmem {
   using G = RowGeom<T, D>;
-  return 2 * (size_t)TT * G::kPitch * sizeof(T) + 2 * (size_t)(TT / kTokRun) * D * 2 * sizeof(float) + 16;
+  static constexpr size_t kTensor = (size_t)TT * G::kPitch * sizeof(T);     // one staged tensor tile
+  static constexpr size_t kBuffer = 2 * kTensor;                           // K and V
+  static constexpr size_t kRed = 2 * (size_t)(TT / kTokRun) * D * 2 * sizeof(float);  // per-half run extrema
+  static constexpr size_t kTotal = kBuffer + kRed;
+};
+
+template <typename T, int D, int TT>
+constexpr size_t quant_tile_smem() {
+  return QuantTileSmem<T, D, TT>::kTotal;
 }
 
-// One block per tile: retained-row tiles copy; standard / cold tiles gather the K and
-// V rows into shared memory (bulk copies), then warps 0-3 quantize K and warps 4-7
-// quantize V, each half on its own named barrier.
-template <typename T, int D, int TT>
-__global__ void __launch_bounds__(kThreads, 3) quantize_tile_kernel(const __grid_constant__ QuantParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  using G = RowGeom<T, D>;
-  const int s = blockIdx.x / p.tiles_slice;
-  int k = blockIdx.x - s * p.tiles_slice;
+// Tile t of a launch -> (slice, tier, tile within the tier); tier 0 = retained rows.
+struct TileRef {
+  int s, tier, k;
+};
+__device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
+  TileRef r;
+  r.s = t / p.tiles_slice;
+  int k = t - r.s * p.tiles_slice;
+  r.tier = 0;
+  if (k >= p.tiles[0]) {
+    k -= p.tiles[0];
+    r.tier = 1;
+    if (k >= p.tiles[1]) { k -= p.tiles[1]; r.tier = 2; }
+  }
+  r.k = k;
+  return r;
+}
+
+template <typename T>
+struct SliceIn {
+  const T* kb;
+  const T* vb;
+  int64_t kst, vst;
+};
+template <typename T>
+__device__ __forceinline__ SliceIn<T> slice_in(const QuantParams& p, int s) {
   const LayerDesc& L = p.layers[find_layer(p, s)];
   const int local = s - L.slice_begin;
   const int b = local / L.heads, h = local - b * L.heads;
-  const T* kb = reinterpret_cast<const T*>(L.k) + b * L.ks[0] + h * L.ks[1];
-  const T* vb = reinterpret_cast<const T*>(L.v) + b * L.vs[0] + h * L.vs[1];
-  const int gslice = p.slice_offset + s;
+  return {reinterpret_cast<const T*>(L.k) + b * L.ks[0] + h * L.ks[1],
+          reinterpret_cast<const T*>(L.v) + b * L.vs[0] + h * L.vs[1], L.ks[2], L.vs[2]};
+}
 
-  if (k < p.tiles[0]) {
-    copy_retained_tile<T, D>(p, kb, vb, L.ks[2], L.vs[2], gslice, k);
-    return;
-  }
-  k -= p.tiles[0];
-  int tier = 1;
-  if (k >= p.tiles[1]) { k -= p.tiles[1]; tier = 2; }
-  const int* idx = p.idx[tier];
-  const int n = p.n_tier[tier];
-  const int j0 = k * TT;
-  const int rows = min(TT, n - j0);
-
-  T* sk = reinterpret_cast<T*>(smem);
-  T* sv = sk + TT * G::kPitch;
-  float* red = reinterpret_cast<float*>(sv + TT * G::kPitch);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(red + 2 * (TT / kTokRun) * D * 2);
-
-  if (threadIdx.x == 0) mbar_init(bar, 1);
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    if (threadIdx.x == 0) mbar_arrive_expect_tx(bar, (uint32_t)(rows * 2 * G::kRowBytes));
-    __syncwarp();
-    for (int r = threadIdx.x; r < rows; r += 32) {
-      int tok = idx[j0 + r];
-      if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
-      bulk_load(sk + r * G::kPitch, kb + tok * L.ks[2], G::kRowBytes, bar);
-      bulk_load(sv + r * G::kPitch, vb + tok * L.vs[2], G::kRowBytes, bar);
+// Issue the 16-byte asynchronous copies that gather tile t's K and V rows into a
+// staging buffer (rows past the end of the tier are zero-filled: token-axis groups
+// quantize them as padding), then commit them as one group.  Retained tiles stage
+// nothing but still commit a group so that the group count stays uniform.
+template <typename T, int D, int TT>
+__device__ __forceinline__ void stage_tile(const QuantParams& p, int t, T* sk, T* sv) {
+  using G = RowGeom<T, D>;
+  const TileRef tr = tile_ref(p, t);
+  if (tr.tier != 0) {
+    const SliceIn<T> in = slice_in<T>(p, tr.s);
+    const int* idx = p.idx[tr.tier];
+    const int j0 = tr.k * TT;
+    const int rows = min(TT, p.n_tier[tr.tier] - j0);
+    constexpr int CH = TT * G::kChunks;  // chunks per tensor
+#pragma unroll
+    for (int i = 0; i < 2 * CH / kThreads; ++i) {
+      const int e = threadIdx.x + i * kThreads;
+      const int tsr = e / CH, rem = e - tsr * CH;
+      const int r = rem / G::kChunks, c = rem - r * G::kChunks;
+      int tok = 0;
+      if (r < rows) {
+        tok = idx[j0 + r];
+        if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
+      }
+      const T* src = (tsr ? in.vb + tok * in.vst : in.kb + tok * in.kst) + c * G::kVec;
+      cp_async16((tsr ? sv : sk) + r * G::kPitch + c * G::kVec, src, r < rows ? 16u : 0u);
     }
   }
-  // rows past the end of the tier are zero: token-axis groups quantize them as padding
-  for (int e = threadIdx.x; e < (TT - rows) * G::kChunks; e += kThreads) {
-    const int r = rows + e / G::kChunks, c = e % G::kChunks;
-    *reinterpret_cast<uint4*>(sk + r * G::kPitch + c * G::kVec) = make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<uint4*>(sv + r * G::kPitch + c * G::kVec) = make_uint4(0, 0, 0, 0);
-  }
-  if (!block_wait(bar, 0)) return;
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
 
+// One block per tile: retained-row tiles copy rows; standard / cold tiles gather
+// the K and V rows into shared memory (16-byte asynchronous copies from every
+// thread), then warps 0-3 quantize K and warps 4-7 quantize V, each half on its own
+// named barrier.
+template <typename T, int D, int TT>
+__global__ void __launch_bounds__(kThreads, 3) quantize_tile_kernel(const __grid_constant__ QuantParams p,
+                                                                    int total_tiles) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  using SM = QuantTileSmem<T, D, TT>;
+  (void)total_tiles;
+  const int t = blockIdx.x;
+  const TileRef tr = tile_ref(p, t);
+  const int gslice = p.slice_offset + tr.s;
+  if (tr.tier == 0) {
+    const SliceIn<T> in = slice_in<T>(p, tr.s);
+    copy_retained_tile<T, D>(p, in.kb, in.vb, in.kst, in.vst, gslice, tr.k);
+    return;
+  }
+  T* sk = reinterpret_cast<T*>(smem);
+  T* sv = reinterpret_cast<T*>(smem + SM::kTensor);
+  float* red = reinterpret_cast<float*>(smem + SM::kBuffer);
+  stage_tile<T, D, TT>(p, t, sk, sv);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  const int j0 = tr.k * TT;
+  const int rows = min(TT, p.n_tier[tr.tier] - j0);
   const int half = threadIdx.x >> 7;
-  const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + half];
+  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + half];
   T* sx = half ? sv : sk;
   if (d.rotation) {
     rotate_rows_half<T, D>(sx, rows, p.had_div, p.had_inv, (threadIdx.x >> 5) & 3);
@@ -516,15 +549,17 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 // ---------------------------------------------------------------------------
 // host-side launchers (called from capi.cu)
 // ---------------------------------------------------------------------------
+int device_sm_count();
+
 template <typename T, int D, int TT>
 static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
   const size_t sm = quant_tile_smem<T, D, TT>();
   auto kern = quantize_tile_kernel<T, D, TT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
-  const int64_t blocks = (int64_t)p.S * p.tiles_slice;
-  if (blocks == 0) return cudaSuccess;
-  kern<<<(unsigned)blocks, kThreads, sm, st>>>(p);
+  const int64_t tiles = (int64_t)p.S * p.tiles_slice;
+  if (tiles == 0) return cudaSuccess;
+  kern<<<(unsigned)tiles, kThreads, sm, st>>>(p, (int)tiles);
   return cudaGetLastError();
 }
 
