@@ -236,7 +236,7 @@ int32_t gkv_device_error(int32_t* code) {
   return GKV_OK;
 }
 
-size_t gkv_select_workspace_bytes(int32_t seq_len) { return seq_len > 0 ? align256((size_t)seq_len) : 0; }
+size_t gkv_select_workspace_bytes(int32_t seq_len) { return seq_len > 0 ? select_workspace(seq_len) : 0; }
 
 int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const gkv_select_policy* pol,
                          int32_t* idx_retained, int32_t* idx_standard, int32_t* idx_cold, void* workspace,
@@ -255,7 +255,8 @@ int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const
   if (p.keep_outlier && !outlier_scores) return fail(GKV_ERR_INVALID, "outlier scores required");
   if ((p.n_retained && !idx_retained) || (p.n_standard && !idx_standard) || (p.n_cold && !idx_cold))
     return fail(GKV_ERR_INVALID, "missing index list output");
-  if (!workspace || workspace_bytes < (size_t)T) return fail(GKV_ERR_WORKSPACE, "selection workspace too small");
+  if (!workspace || workspace_bytes < select_workspace(T))
+    return fail(GKV_ERR_WORKSPACE, "selection workspace too small");
   cudaError_t e = launch_select(scores, outlier_scores, p, idx_retained, idx_standard, idx_cold,
                                 static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? GKV_OK : cuda_fail(e, "select kernel launch");
@@ -415,10 +416,13 @@ namespace {
 constexpr int kStaticSelectMaxTokens = GKV_STATIC_SELECT_MAX_TOKENS;
 constexpr int kMaxDevices = 64;
 
-// 1 MiB of tier bytes.  Every GPU that loads this library holds it until the
-// process exits.  In host code `g_select_scratch` only names a host-side handle
-// of the symbol; the device address comes from cudaGetSymbolAddress below.
-static __device__ __align__(256) uint8_t g_select_scratch[kStaticSelectMaxTokens];
+// Selection workspace for kStaticSelectMaxTokens tokens (13 MiB: tier bytes plus
+// the three int32 tables of the exact tie path).  Every GPU that loads this
+// library holds it until the process exits.  In host code `g_select_scratch`
+// only names a host-side handle of the symbol; the device address comes from
+// cudaGetSymbolAddress below.
+constexpr size_t kStaticSelectBytes = select_workspace(kStaticSelectMaxTokens);
+static __device__ __align__(256) uint8_t g_select_scratch[kStaticSelectBytes];
 
 std::mutex g_scratch_mutex;
 void* g_scratch_address[kMaxDevices] = {};
@@ -457,5 +461,5 @@ extern "C" int32_t gkv_select_tiers_static(const float* scores, const float* out
   // the kernel writes the tier byte of every token before reading it, so the
   // previous call's contents need no clearing
   return gkv_select_tiers(scores, outlier_scores, policy, idx_retained, idx_standard, idx_cold, scratch,
-                          (size_t)kStaticSelectMaxTokens, stream);
+                          kStaticSelectBytes, stream);
 }

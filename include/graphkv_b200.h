@@ -139,9 +139,11 @@ int32_t gkv_device_error(int32_t* code);
  * lists.  Replaces build_retention_mask (core.py:595-644),
  * _apply_score_retention (core.py:1034-1048), the cold-tier topk
  * (core.py:685-712) and the index lists (core.py:716-719).  Among equal scores
- * at a selection boundary the lower token position is taken.
+ * at a selection boundary the tokens are those torch.topk picks on the CPU
+ * (the order of libstdc++'s partial_sort / nth_element over the candidates).
  * scores / outlier_scores: fp32 [T] (outlier_scores may be NULL when
- * keep_outlier == 0).  workspace: gkv_select_workspace_bytes(T) bytes. */
+ * keep_outlier == 0).  workspace: gkv_select_workspace_bytes(T) bytes
+ * (13 bytes per token, 256-byte aligned regions). */
 size_t gkv_select_workspace_bytes(int32_t seq_len);
 int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const gkv_select_policy* policy,
                          int32_t* idx_retained, int32_t* idx_standard, int32_t* idx_cold,
@@ -156,8 +158,9 @@ int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const
  * device-wide synchronisation.
  *  - Limit: seq_len <= GKV_STATIC_SELECT_MAX_TOKENS; larger sizes return
  *    GKV_ERR_TOO_LARGE without launching anything.
- *  - The scratch is a 1 MiB device array inside the library; every GPU that
- *    loads the library keeps it until the process exits.
+ *  - The scratch is a 13 MiB device array inside the library (the selection
+ *    workspace of GKV_STATIC_SELECT_MAX_TOKENS tokens); every GPU that loads
+ *    the library keeps it until the process exits.
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
  *    before any stream capture.

@@ -174,12 +174,130 @@ def order_keys(scores: np.ndarray) -> np.ndarray:
 
 
 def topk_indices(scores: np.ndarray, k: int, largest: bool) -> np.ndarray:
-    """Positions of the k largest (or smallest) scores.  Among equal scores the
-    lower position wins; torch.topk (core.py:1047, 707) leaves that choice
-    unspecified, so the tests check for ties at the boundary separately."""
+    """Positions of the k largest (or smallest) scores, as torch.topk on CPU
+    chooses them (core.py:1047, 707).
+
+    Without a tie at the k-th score the set is unique.  With one, torch's CPU
+    topk (ATen ``TopKImpl.h``, ``topk_impl_loop``) decides by the order in which
+    libstdc++ visits the (value, position) queue: ``std::partial_sort`` when
+    ``k * 64 <= n``, else ``std::nth_element``; ``libstdc_select`` restates both."""
     keys = order_keys(scores)
     order = np.argsort(~keys if largest else keys, kind="stable")
-    return order[:k]
+    n = keys.size
+    if k <= 0:
+        return order[:0]
+    if k >= n or keys[order[k - 1]] != keys[order[k]]:
+        return order[:k]
+    return np.asarray(libstdc_select(keys.tolist(), k, largest), dtype=np.int64)
+
+
+# -- libstdc++ selection algorithms (GCC bits/stl_heap.h, bits/stl_algo.h) ---
+# The comparator of ATen's topk is "x > y" (largest) or "x < y" (smallest) on
+# the values, NaN ranked above every number; the order keys encode exactly that.
+
+def _adjust_heap(q, first, hole, length, item, kv, less):
+    """std::__adjust_heap then std::__push_heap: sift the hole at ``hole`` down
+    to a leaf along the larger child (right child on ties), then push ``item`` up."""
+    top = hole
+    child = hole
+    while child < (length - 1) // 2:
+        child = 2 * (child + 1)
+        if less(kv[q[first + child]], kv[q[first + child - 1]]):
+            child -= 1
+        q[first + hole] = q[first + child]
+        hole = child
+    if (length & 1) == 0 and child == (length - 2) // 2:
+        child = 2 * (child + 1)
+        q[first + hole] = q[first + child - 1]
+        hole = child - 1
+    parent = (hole - 1) // 2
+    while hole > top and less(kv[q[first + parent]], kv[item]):
+        q[first + hole] = q[first + parent]
+        hole = parent
+        parent = (hole - 1) // 2
+    q[first + hole] = item
+
+
+def _heap_select(q, first, middle, last, kv, less):
+    """std::__heap_select: heapify [first, middle), then every later element that
+    compares before the heap top replaces it (std::__pop_heap)."""
+    length = middle - first
+    if length >= 2:
+        parent = (length - 2) // 2
+        while True:
+            _adjust_heap(q, first, parent, length, q[first + parent], kv, less)
+            if parent == 0:
+                break
+            parent -= 1
+    for i in range(middle, last):
+        if less(kv[q[i]], kv[q[first]]):
+            item = q[i]
+            q[i] = q[first]
+            _adjust_heap(q, first, 0, length, item, kv, less)
+
+
+def _introselect(q, first, nth, last, kv, less):
+    """std::__introselect with depth limit 2*floor(log2(n)): median-of-three
+    pivot (first+1, middle, last-1) moved to ``first``, unguarded Hoare
+    partition, recurse into the side holding ``nth``; heap select when the depth
+    runs out; insertion sort of the final <= 3 elements."""
+    depth = 2 * ((last - first).bit_length() - 1)
+    while last - first > 3:
+        if depth == 0:
+            _heap_select(q, first, nth + 1, last, kv, less)
+            q[first], q[nth] = q[nth], q[first]
+            return
+        depth -= 1
+        a, b, c = first + 1, first + (last - first) // 2, last - 1
+        ka, kb, kc = kv[q[a]], kv[q[b]], kv[q[c]]
+        if less(ka, kb):
+            m = b if less(kb, kc) else (c if less(ka, kc) else a)
+        elif less(ka, kc):
+            m = a
+        elif less(kb, kc):
+            m = c
+        else:
+            m = b
+        q[first], q[m] = q[m], q[first]
+        pivot = kv[q[first]]
+        lo, hi = first + 1, last
+        while True:
+            while less(kv[q[lo]], pivot):
+                lo += 1
+            hi -= 1
+            while less(pivot, kv[q[hi]]):
+                hi -= 1
+            if not lo < hi:
+                break
+            q[lo], q[hi] = q[hi], q[lo]
+            lo += 1
+        if lo <= nth:
+            first = lo
+        else:
+            last = lo
+    for i in range(first + 1, last):
+        item = q[i]
+        if less(kv[item], kv[q[first]]):
+            q[first + 1:i + 1] = q[first:i]
+            q[first] = item
+        else:
+            j = i
+            while less(kv[item], kv[q[j - 1]]):
+                q[j] = q[j - 1]
+                j -= 1
+            q[j] = item
+
+
+def libstdc_select(keys: list, k: int, largest: bool) -> list:
+    """Positions that end in the first k slots of torch's CPU topk queue."""
+    n = len(keys)
+    q = list(range(n))
+    less = (lambda x, y: x > y) if largest else (lambda x, y: x < y)
+    if k * 64 <= n:
+        _heap_select(q, 0, k, n, keys, less)
+    else:
+        _introselect(q, 0, k - 1, n, keys, less)
+    return sorted(q[:k])
 
 
 def boundary_tie(scores: np.ndarray, k: int, largest: bool) -> bool:

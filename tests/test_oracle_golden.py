@@ -7,7 +7,7 @@ from oracle import graphkv_oracle as orc
 from tests.golden.cases import CASES, case_layers, case_scores, tensor_digest
 from tests.oracle_bridge import compare_arrays, load_golden, oracle_arrays, oracle_layers, scores_np
 
-SMALL = [c for c in CASES if not c.workload and c.name != "scores_ties"]
+SMALL = [c for c in CASES if not c.workload]
 
 
 @pytest.mark.parametrize("case", SMALL, ids=lambda c: c.name)
@@ -30,21 +30,11 @@ def test_oracle_matches_reference(case):
     assert not problems, problems
 
 
-def test_ties_case_differs_only_inside_the_tie_class():
-    """torch.topk's choice among equal scores is unspecified; the oracle takes
-    the lower positions.  Both must pick the same number of tokens and agree on
-    every token whose score is strictly beyond the boundary."""
-    case = next(c for c in CASES if c.name == "scores_ties")
-    rec, arrays = load_golden(case.name)
+def test_ties_case_has_boundary_ties():
+    """The scores_ties golden exercises the tie rule: the k-th score also occurs
+    outside the selected set, so torch's CPU topk order decides."""
+    rec, _ = load_golden("scores_ties")
     assert rec["ties"]["protect"] is True
-    (k, v), = case_layers(case)
-    s = case_scores(case).numpy()
-    ql, = oracle_layers(case, [(k, v)], scores_np(case_scores(case)))
-    ref_cold, my_cold = arrays["l0.idx_cold"], ql.idx_cold
-    assert ref_cold.size == my_cold.size
-    boundary = max(s[ref_cold].max(), s[my_cold].max())
-    assert set(ref_cold[s[ref_cold] < boundary]) == set(my_cold[s[my_cold] < boundary])
-    assert rec["stats"] == orc.cache_stats([ql])
 
 
 def test_pack_lowbit_known_answer():

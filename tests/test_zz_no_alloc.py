@@ -4,8 +4,8 @@ Some callers cannot allocate device memory at the moment they select tiers --
 an engine that has already given all free device memory to its own pool, or a
 latency-critical path that cannot pay for cudaMalloc's implicit device-wide
 synchronisation.  For them the library offers this entry point, which takes no
-workspace and allocates nothing; it keeps one byte of tier state per token in a
-fixed 1 MiB device array (up to GKV_STATIC_SELECT_MAX_TOKENS tokens).
+workspace and allocates nothing; it keeps the selection workspace (13 bytes per
+token) in a fixed 13 MiB device array (up to GKV_STATIC_SELECT_MAX_TOKENS tokens).
 
 These tests call it through the C ABI and check, on two calls in a row, that
 its index lists equal those of gkv_select_tiers with a caller-supplied
