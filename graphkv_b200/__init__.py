@@ -17,24 +17,74 @@ from .core import (
     hf_cache_to_tuple,
     quantize_kv_layer,
 )
-from .integrations import quantize_hf_cache
+from .graph_model import (
+    GraphFactBank,
+    GraphMemory17L,
+    GraphMemoryConfig,
+    GraphMemoryRequest,
+    GraphMnemeRequest,
+    GraphQueryBank,
+    GraphRetentionChunk,
+    build_candidate_bank,
+    build_fact_bank,
+    build_graph_mneme_token_scores,
+    build_query_bank,
+    bundled_graph_model_dir,
+    bundled_graph_model_metadata,
+    graph_mneme_chunk_scores,
+    graph_mneme_request_token_scores,
+    graph_mneme_token_scores,
+    load_bundled_graph_model,
+    normalize_graph_scores,
+)
+from .integrations import (
+    llama_cpp_args,
+    llama_cpp_command,
+    llama_cpp_env,
+    quantize_hf_cache,
+    vllm_cli_args,
+    vllm_kwargs,
+)
 from .profiles import GraphKVProfile, get_profile, list_profiles
 
 __version__ = "0.1.0"
 
 __all__ = [
+    "GraphFactBank",
     "GraphKVProfile",
+    "GraphMemory17L",
+    "GraphMemoryConfig",
+    "GraphMemoryRequest",
+    "GraphMnemeRequest",
+    "GraphQueryBank",
+    "GraphRetentionChunk",
     "KvQuantConfig",
     "QuantizedKvCache",
     "QuantizedKvLayer",
     "QuantizedTensor",
     "attention_from_kv",
     "attention_report",
+    "build_candidate_bank",
+    "build_fact_bank",
+    "build_graph_mneme_token_scores",
+    "build_query_bank",
     "build_retention_mask",
+    "bundled_graph_model_dir",
+    "bundled_graph_model_metadata",
     "chunk_scores_to_token_scores",
     "get_profile",
+    "graph_mneme_chunk_scores",
+    "graph_mneme_request_token_scores",
+    "graph_mneme_token_scores",
     "hf_cache_to_tuple",
     "list_profiles",
+    "llama_cpp_args",
+    "llama_cpp_command",
+    "llama_cpp_env",
+    "load_bundled_graph_model",
+    "normalize_graph_scores",
     "quantize_hf_cache",
     "quantize_kv_layer",
+    "vllm_cli_args",
+    "vllm_kwargs",
 ]

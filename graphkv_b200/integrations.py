@@ -3,6 +3,9 @@
 same output formats."""
 from __future__ import annotations
 
+import shlex
+from typing import Iterable
+
 from .core import QuantizedKvCache, hf_cache_to_tuple
 from .profiles import GraphKVProfile, get_profile
 
@@ -47,3 +50,46 @@ def _hf_cache_seq_len(past_key_values: object) -> int:
     if not layers:
         raise ValueError("past_key_values must contain at least one non-empty KV layer.")
     return int(layers[0][0].shape[2])
+
+
+# ---------------------------------------------------------------------------
+# engine-native recipes (integrations.py:65-124): the settings a vLLM or
+# llama.cpp profile stands for, as keyword arguments, CLI flags or environment
+# ---------------------------------------------------------------------------
+
+def _engine_profile(profile, engine: str, label: str) -> GraphKVProfile:
+    selected = get_profile(profile)
+    if selected.engine != engine:
+        raise ValueError(f"Profile {selected.name!r} is not a {label} profile.")
+    return selected
+
+
+def vllm_kwargs(profile: str | GraphKVProfile = "vllm-fp8-calibrated", **overrides) -> dict[str, object]:
+    """Keyword arguments for ``vllm.LLM(...)``: vLLM's native KV cache dtype and
+    scale calibration (low-bit GraphKV caches would need a vLLM backend patch)."""
+    selected = _engine_profile(profile, "vllm", "vLLM")
+    return {"kv_cache_dtype": selected.vllm_kv_cache_dtype,
+            "calculate_kv_scales": selected.vllm_calculate_kv_scales, **overrides}
+
+
+def vllm_cli_args(profile: str | GraphKVProfile = "vllm-fp8-calibrated") -> list[str]:
+    kw = vllm_kwargs(get_profile(profile))
+    return ["--kv-cache-dtype", str(kw["kv_cache_dtype"])] + (["--calculate-kv-scales"]
+                                                              if kw.get("calculate_kv_scales") else [])
+
+
+def llama_cpp_args(profile: str | GraphKVProfile = "llamacpp-q8") -> list[str]:
+    selected = _engine_profile(profile, "llama.cpp", "llama.cpp")
+    return ["--cache-type-k", str(selected.llama_cache_type_k), "--cache-type-v", str(selected.llama_cache_type_v)]
+
+
+def llama_cpp_env(profile: str | GraphKVProfile = "llamacpp-q8") -> dict[str, str]:
+    selected = _engine_profile(profile, "llama.cpp", "llama.cpp")
+    return {"LLAMA_ARG_CACHE_TYPE_K": str(selected.llama_cache_type_k),
+            "LLAMA_ARG_CACHE_TYPE_V": str(selected.llama_cache_type_v)}
+
+
+def llama_cpp_command(model_path: str, *, profile: str | GraphKVProfile = "llamacpp-q8", binary: str = "llama-cli",
+                      extra_args: Iterable[str] = ()) -> str:
+    """Shell-quoted llama.cpp command line with the profile's cache types."""
+    return shlex.join([binary, "-m", model_path, *llama_cpp_args(profile), *extra_args])
