@@ -92,6 +92,11 @@ int resolve_tensor(const gkv_plan& p, int i, int n, TensorDesc& d) {
   d.packed = sp.packed ? 1 : 0;
   d.sbits = d.packed ? d.bits : 8;
   d.scale_dtype = sp.scale_dtype;
+  {
+    const int qmax = sp.quantizer == GKV_AFFINE ? (1 << sp.bits) - 1 : (1 << (sp.bits - 1)) - 1;
+    d.qmax = (float)qmax;
+    d.rqmax = 1.0f / (float)qmax;  // IEEE single division: the correctly rounded reciprocal
+  }
   d.n = n;
   const int len = axis_len;
   d.n_pad = (int)(ceil_div(len, d.gs) * d.gs);
@@ -112,14 +117,17 @@ int resolve_tensor(const gkv_plan& p, int i, int n, TensorDesc& d) {
 }
 
 // Can tensor d run in the tile kernels with tile height TT?
-// Tile kernels work on runs of 32 elements along the grouped axis: groups of
+// Quantize tiles (64 rows) hold whole token-axis groups of 32 or 64 rows per
+// thread; channel-axis groups are powers of two >= 32 dividing head_dim.  The
+// dequantize tiles work on runs of 32 elements along the grouped axis: groups of
 // 32, 64 or 128 (powers of two dividing the tile height or head_dim).
 bool tensor_fast(const TensorDesc& d, int esize, int D, int TT, bool quantize) {
   (void)esize;
   if (d.log2gs < 0 || d.gs < 32 || !aligned16(d.codes)) return false;
   if (d.axis == GKV_AXIS_TOKEN) {
+    if (quantize) return d.gs == 32 || d.gs == 64;
     if (d.gs > TT || TT % d.gs) return false;
-    if (!quantize && d.rotation) return false;  // rotated token-axis dequant: general path
+    if (d.rotation) return false;  // rotated token-axis dequant: general path
     return true;
   }
   return D % d.gs == 0;
@@ -174,7 +182,7 @@ int resolve_plan(const gkv_plan* pp, int64_t S, bool quantize, const gkv_layer_i
   for (int tier = 1; tier <= 2; ++tier) {
     if (!geom_ok || r.n[tier] == 0) continue;
     int need = 64;
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 4 && !quantize; ++i)  // quantize tiles are always 64 rows
       if (kTierOf[i] == tier && r.t[i].axis == GKV_AXIS_TOKEN) need = need > r.t[i].gs ? need : r.t[i].gs;
     if (need > 128 || !tile_instantiated(esize, D, need)) continue;
     want[tier] = true;
@@ -310,6 +318,10 @@ int32_t gkv_quantize(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n
   q.ret_v = p.retained_v;
   q.had_div = p.hadamard_divisor;
   q.had_inv = p.hadamard_divisor > 0.f ? 1.0f / p.hadamard_divisor : 0.f;
+  // the fused quotient y * (1 / div) + correction is proven exact (|quotient| >=
+  // 2^-100) for fp32(sqrt(D)) at the tile head dims 64 (a power of two) and 128
+  q.had_fused = (p.head_dim == 64 || p.head_dim == 128) &&
+                p.hadamard_divisor == (float)std::sqrt((double)p.head_dim);
   q.tt = r.tt;
   q.tiles[0] = r.fast[0] ? (int)ceil_div(r.n[0], kRetTile) : 0;
   for (int k = 1; k <= 2; ++k) q.tiles[k] = r.fast[k] ? (int)ceil_div(r.n[k], r.tt) : 0;

@@ -263,6 +263,125 @@ __device__ __forceinline__ void encode_run(const float* x, const FastCoder& c, u
 }
 
 // ---------------------------------------------------------------------------
+// Correctly rounded quotient x / c from rc = RN(1 / c): one product and one
+// fused-multiply-add correction (Markstein).  For the divisors used here -- the
+// code ranges qmax in {3, 7, 15, 127, 255} and fp32(sqrt(D)) for D in
+// {32, 128, 512} -- this equals the IEEE quotient for every fp32 x whose
+// quotient is at least 2^-100 in magnitude (checked exhaustively over all 2^32
+// bit patterns against __fdiv_rn); qmax = 1 and powers of two are exact trivially.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float quot(float x, float c, float rc) {
+  const float q0 = __fmul_rn(x, rc);
+  return __fmaf_rn(__fmaf_rn(-q0, c, x), rc, q0);
+}
+__device__ __forceinline__ uint64_t quot2(uint64_t x2, uint64_t nc2, uint64_t rc2) {
+  const uint64_t q0 = mul2(x2, rc2);
+  return fma2(fma2(q0, nc2, x2), rc2, q0);
+}
+
+// Group coders built from a group's statistics (core.py:863-887); the scale
+// division by qmax uses quot() (exact for every scale >= 1e-8).
+__device__ __forceinline__ FastCoder sym_coder(float absmax, float qmax, float rqmax, int bits, bool packed) {
+  FastCoder c;
+  c.scale = quot(fmaxf(absmax, kEps), qmax, rqmax);
+  c.inv = __frcp_rn(c.scale);
+  c.zp = 0.f;
+  c.hi = qmax;
+  if (packed) {
+    c.magic = kMagic + (float)(1 << (bits - 1));
+    c.flip = 0u;
+  } else {
+    c.magic = kMagic + 128.f;
+    c.flip = 0x80808080u;
+  }
+  return c;
+}
+
+__device__ __forceinline__ FastCoder aff_coder(float mn, float mx, float qmax, float rqmax) {
+  FastCoder c;
+  const float range = __fsub_rn(mx, mn);
+  const bool degenerate = range < kEps;
+  const float absmax = fmaxf(fabsf(mn), fabsf(mx));
+  c.scale = quot(fmaxf(degenerate ? absmax : range, kEps), qmax, rqmax);
+  c.inv = __frcp_rn(c.scale);
+  float z;
+  if (degenerate) {
+    z = mn < 0.f ? qmax : 0.f;
+  } else {
+    // round(-min / scale): the quotient from the reciprocal, corrected once,
+    // rounds like the IEEE quotient (the same argument as for the codes)
+    z = fminf(fmaxf(rintf(quot(-mn, c.scale, c.inv)), 0.f), qmax);
+  }
+  c.zp = z;
+  c.hi = qmax;
+  c.magic = kMagic;
+  c.flip = 0u;
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// Packed statistics of 32-bit words holding two 16-bit elements.
+// max.xorsign.abs returns max(|a|, |b|) with the XOR of the signs: the
+// magnitude accumulates the absolute maximum of both halves independently.
+// ---------------------------------------------------------------------------
+template <typename T> struct Word16;
+template <> struct Word16<__nv_bfloat16> {
+  __device__ __forceinline__ static uint32_t amax(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  __device__ __forceinline__ static uint32_t vmax(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  __device__ __forceinline__ static uint32_t vmin(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static constexpr uint32_t kNegInf = 0xFF80FF80u, kPosInf = 0x7F807F80u;
+  __device__ __forceinline__ static float lo(uint32_t w) { return __uint_as_float(w << 16); }
+  __device__ __forceinline__ static float hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+  __device__ __forceinline__ static uint64_t pair(uint32_t w) { return pk2(lo(w), hi(w)); }
+  __device__ __forceinline__ static uint32_t round2(float a, float b) {  // (a low, b high), RNE
+    const __nv_bfloat162 r = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+};
+template <> struct Word16<__half> {
+  __device__ __forceinline__ static uint32_t amax(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  __device__ __forceinline__ static uint32_t vmax(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  __device__ __forceinline__ static uint32_t vmin(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static constexpr uint32_t kNegInf = 0xFC00FC00u, kPosInf = 0x7C007C00u;
+  __device__ __forceinline__ static float lo(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
+  }
+  __device__ __forceinline__ static float hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+  __device__ __forceinline__ static uint64_t pair(uint32_t w) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    return pk2(f.x, f.y);
+  }
+  __device__ __forceinline__ static uint32_t round2(float a, float b) {
+    const __half2 r = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+};
+
+// ---------------------------------------------------------------------------
 // Fast Walsh-Hadamard butterflies of a row spread over a warp, lane holding EPL
 // consecutive elements.  Stages run in the reference order h = 1, 2, 4, ...
 // (core.py:950-955); every output is one fp32 add or subtract of the previous
@@ -468,6 +587,10 @@ __device__ __forceinline__ void word_codes(uint32_t w, uint32_t (&out)[32 / SB])
 
 __device__ __forceinline__ void bar_half(int half) {
   asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
+}
+// named barrier of the 64 threads of one half of a 128-thread block
+__device__ __forceinline__ void bar_half64(int half) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + half) : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -25,6 +25,8 @@ struct TensorDesc {
   int packed;       // 1: sub-byte packing
   int sbits;        // stored bits per code (bits when packed, else 8)
   int scale_dtype;  // GKV_F16 / GKV_BF16 / GKV_F32
+  float qmax;       // largest code: 2^(bits-1) - 1 (symmetric) or 2^bits - 1 (affine)
+  float rqmax;      // 1 / qmax rounded to nearest
   int n;            // tier length
   int n_pad;        // token axis: padded tier length; channel axis: padded head_dim
   int groups_row;   // token axis: groups per channel (n_pad / gs); channel: groups per token
@@ -54,6 +56,7 @@ struct QuantParams {
   void* ret_k;
   void* ret_v;
   float had_div, had_inv;
+  int had_fused;     // 1: had_div is fp32(sqrt(D)) with the fused quotient proven exact for it
   int tt;            // tile rows of the fast path (64 or 128)
   int tiles[3];      // fast-path tiles per slice per tier (0 when the tier is not in this launch)
   int tiles_slice;

@@ -1,14 +1,25 @@
 // Quantize + pack kernels (core.py:647-772, 848-910, 945-956, 979-990).
 //
-// Fast path: one block per tile of TT consecutive tier rows of one slice.  All
-// threads gather the K and V rows of the tile into shared memory with 16-byte
-// asynchronous copies, rows are rotated in place when the tensor uses the Hadamard
-// rotation, then each tensor is grouped along its axis, scaled and packed straight
-// to HBM.  Retained rows are copied by tiles of the same launch.
+// Fast path: two launches, one over K and one over V; one block of 64 threads per
+// tile of 64 consecutive tier rows of one slice.  The threads gather the tile's
+// rows into shared memory with 16-byte asynchronous copies, then quantize them,
+// each thread holding whole quantization groups in registers:
+//  - token-axis groups (K): a thread owns one 32-bit column word (two 16-bit
+//    channels, or one fp32 channel) over the group's gs rows; lanes of a warp own
+//    consecutive words of the same rows, so the column reads are conflict-free;
+//  - channel-axis groups (V): a thread owns a run of 128 bytes of one row (a whole
+//    group, or 1/2 or 1/4 of one, combined with the lanes 8 or 16 apart); the 8
+//    lanes of a quarter-warp read 8 different rows, so the 16-byte reads are
+//    conflict-free (row pitch = 4 words mod 32 banks).
+// Rotated V rows (cold tier) are transformed in registers: butterflies inside the
+// thread, then across the lanes that hold the rest of the row.  Group statistics
+// use packed 16-bit min/max, the scale one fused quotient, the codes the packed
+// quotient of gkv_common.cuh.  Retained rows are copied by tiles of the same launch.
 //
 // General path: any geometry the tiles do not cover (group sizes that are not
-// powers of two, padded head dims, tiny tiers, unaligned inputs): one thread per
-// group computes the scale, one thread per output byte packs the codes.
+// 32 or 64 along tokens, group sizes that are not powers of two, padded head
+// dims, tiny tiers, unaligned inputs): one thread per group computes the scale,
+// one thread per output byte packs the codes.
 #pragma once
 
 #include <algorithm>
@@ -17,22 +28,9 @@
 
 namespace gkv {
 
-// ---------------------------------------------------------------------------
-// element access
-// ---------------------------------------------------------------------------
-template <typename T>
-__device__ __forceinline__ void unpack_word(uint32_t w, float (&f)[4 / sizeof(T)]) {
-  if constexpr (sizeof(T) == 4) {
-    f[0] = __uint_as_float(w);
-  } else if constexpr (Elem<T>::kTag == GKV_BF16) {
-    f[0] = __uint_as_float(w << 16);
-    f[1] = __uint_as_float(w & 0xFFFF0000u);
-  } else {
-    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w));
-    f[0] = t.x;
-    f[1] = t.y;
-  }
-}
+constexpr int kQThreads = 64;   // threads of a quantize tile block
+constexpr int kQTile = 64;      // tier rows of a quantize tile
+constexpr unsigned kFull = 0xFFFFFFFFu;
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 r;
@@ -43,47 +41,45 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 }
 
 template <typename T, int D>
-struct RowGeom {
+struct QGeom {
   static constexpr int kRowBytes = D * (int)sizeof(T);
-  static constexpr int kPitch = D + 16 / (int)sizeof(T);  // +16 B per row spreads rows over banks
-  static constexpr int kVec = 16 / (int)sizeof(T);
-  static constexpr int kChunks = D / kVec;
-  static constexpr int kWords = kRowBytes / 4;
-  static constexpr int kSegs = kThreads / kWords;         // token-axis segments per tile
+  static constexpr int kPitchB = kRowBytes + 16;  // +16 B per row: consecutive rows start 4 banks apart
+  static constexpr int kPitchW = kPitchB / 4;
+  static constexpr int kWords = kRowBytes / 4;     // 32-bit words per row
+  static constexpr int kChunks = kRowBytes / 16;   // 16-byte chunks per row
+  static constexpr int kEPW = 4 / (int)sizeof(T);  // elements per word
+  static constexpr int kRun = 128 / (int)sizeof(T);  // elements of a channel-axis run (128 bytes)
+  static constexpr size_t kSmem = (size_t)kQTile * kPitchB;  // one tensor's tile
 };
 
 // ---------------------------------------------------------------------------
-// fast path pieces
+// retained rows
 // ---------------------------------------------------------------------------
 template <typename T, int D>
-__device__ void copy_retained_tile(const QuantParams& p, const T* kb, const T* vb, int64_t kst, int64_t vst,
-                                   int gslice, int tile) {
-  using G = RowGeom<T, D>;
+__device__ void copy_retained_tile(const QuantParams& p, const T* src, int64_t st, void* ret, int gslice, int tile) {
+  constexpr int kVec = 16 / (int)sizeof(T);
+  constexpr int kChunks = D / kVec;
   const int R = p.n_tier[0];
   const int j0 = tile * kRetTile;
   const int rows = min(kRetTile, R - j0);
-  T* rk = reinterpret_cast<T*>(p.ret_k) + ((int64_t)gslice * R + j0) * D;
-  T* rv = reinterpret_cast<T*>(p.ret_v) + ((int64_t)gslice * R + j0) * D;
-  for (int e = threadIdx.x; e < rows * G::kChunks; e += kThreads) {
-    const int r = e / G::kChunks, c = e - r * G::kChunks;
+  T* dst = reinterpret_cast<T*>(ret) + ((int64_t)gslice * R + j0) * D;
+  for (int e = threadIdx.x; e < rows * kChunks; e += kQThreads) {
+    const int r = e / kChunks, c = e - r * kChunks;
     int tok = p.idx[0][j0 + r];
     if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
-    const uint4 a = ldg_stream(kb + tok * kst + c * G::kVec);
-    const uint4 b = ldg_stream(vb + tok * vst + c * G::kVec);
-    *reinterpret_cast<uint4*>(rk + r * D + c * G::kVec) = a;
-    *reinterpret_cast<uint4*>(rv + r * D + c * G::kVec) = b;
+    *reinterpret_cast<uint4*>(dst + r * D + c * kVec) = ldg_stream(src + tok * st + c * kVec);
   }
 }
 
-// Hadamard rotation of `rows` rows held in shared memory, one warp per row, by the
-// 4 warps of one half-block.
+// Hadamard rotation of the tile's rows in shared memory (token-axis tensors with
+// the rotation), one warp per row, by the two warps of a half-block.
 template <typename T, int D>
-__device__ void rotate_rows_half(T* sx, int rows, float div, float inv, int hw) {
-  using G = RowGeom<T, D>;
+__device__ void rotate_rows_smem(T* sx, float div, float inv, int hw) {
+  using G = QGeom<T, D>;
   constexpr int EPL = D / 32;
   const int lane = threadIdx.x & 31;
-  for (int r = hw; r < rows; r += 4) {
-    T* row = sx + r * G::kPitch + lane * EPL;
+  for (int r = hw; r < kQTile; r += 2) {
+    T* row = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(sx) + r * G::kPitchB) + lane * EPL;
     float v[EPL];
 #pragma unroll
     for (int i = 0; i < EPL; ++i) v[i] = Elem<T>::to_f32(row[i]);
@@ -93,198 +89,350 @@ __device__ void rotate_rows_half(T* sx, int rows, float div, float inv, int hw) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// encoding from data words
+// ---------------------------------------------------------------------------
+// Two consecutive elements (e, e + 1) of a run held as 32-bit data words.
+template <typename T, int NW>
+__device__ __forceinline__ uint64_t pair_at(const uint32_t (&w)[NW], int e) {
+  if constexpr (sizeof(T) == 4) return pk2(__uint_as_float(w[e]), __uint_as_float(w[e + 1]));
+  else return Word16<T>::pair(w[e >> 1]);
+}
 
-// Token-axis groups (keys by default): groups of gs consecutive tier rows of one
-// channel.  Item = (32-bit column word w, run of 16 rows); a word holds one fp32 or
-// two 16-bit channels.  Phase 1 writes every run's extrema to shared memory (red,
-// [TT/16][D][2] floats); after the half-block barrier phase 2 combines the runs of
-// each group, re-reads the run's values and encodes them.
-template <typename T, int D, int TT, int SB, bool AFF>
-__device__ void quant_token_half(const TensorDesc& d, const T* sx, int gslice, int j0, float* red, int half) {
-  using G = RowGeom<T, D>;
-  constexpr int W = G::kWords;
-  constexpr int CPW = 4 / (int)sizeof(T);
-  constexpr int RUN = kTokRun;
-  constexpr int NRUN = TT / RUN;
-  constexpr int ITEMS = W * NRUN;
-  constexpr int ITER = (ITEMS + 127) / 128;
-  constexpr int NW = (RUN * SB + 31) / 32;  // code words per channel
-  constexpr int WSTRIDE = G::kPitch * (int)sizeof(T) / 4;  // row stride in 32-bit words
-  const int ht = threadIdx.x & 127;
-  const int rpg = d.gs / RUN;  // runs per group (host guarantees gs >= 32, a multiple of RUN)
-#pragma unroll 1
-  for (int itn = 0; itn < ITER; ++itn) {
-    const int item = ht + itn * 128;
-    if (item >= ITEMS) break;
-    const int w = item % W, run = item / W;
-    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (run * RUN) * G::kPitch) + w;
-    float mn[CPW], mx[CPW];
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) { mn[c] = __int_as_float(0x7f800000); mx[c] = AFF ? -__int_as_float(0x7f800000) : 0.f; }
-#pragma unroll
-    for (int i = 0; i < RUN; ++i) {
-      float f[CPW];
-      unpack_word<T>(col[i * WSTRIDE], f);
-#pragma unroll
-      for (int c = 0; c < CPW; ++c) {
-        if (AFF) { mn[c] = fminf(mn[c], f[c]); mx[c] = fmaxf(mx[c], f[c]); }
-        else mx[c] = fmaxf(mx[c], fabsf(f[c]));
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      red[(run * D + w * CPW + c) * 2 + 0] = mn[c];
-      red[(run * D + w * CPW + c) * 2 + 1] = mx[c];
-    }
+// Quotient, [zero point and clamp], magic add of a pair of elements.
+template <bool AFF>
+__device__ __forceinline__ uint64_t code_pair(uint64_t x2, uint64_t inv2, uint64_t nsc2, uint64_t zp2, uint64_t mg2,
+                                              float hi) {
+  uint64_t a2 = quot2(x2, nsc2, inv2);
+  if (AFF) {
+    a2 = add2(a2, zp2);
+    a2 = pk2(fminf(fmaxf(lo2(a2), 0.f), hi), fminf(fmaxf(hi2(a2), 0.f), hi));
   }
-  bar_half(half);
-#pragma unroll 1
-  for (int itn = 0; itn < ITER; ++itn) {
-    const int item = ht + itn * 128;
-    const bool act = item < ITEMS;
-    const int w = act ? item % W : 0, run = act ? item / W : 0;
-    const int tok0 = j0 + run * RUN;  // first tier row of the run
-    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (run * RUN) * G::kPitch) + w;
-    float xf[CPW][RUN];
+  return add2(a2, mg2);
+}
+
+// Encode a run and store its codes in pieces of at most 16 bytes as they complete
+// (keeps few code words live).  `store` false: encode only (lanes that hold
+// padding rows still take part in the warp's shuffles but write nothing).
+template <typename T, int SB, bool AFF, int NW>
+__device__ __forceinline__ void encode_store_run(const uint32_t (&w)[NW], const FastCoder& c, uint8_t* dst,
+                                                 bool store) {
+  constexpr int N = NW * (4 / (int)sizeof(T));
+  constexpr int EPC = 32 / SB;
+  constexpr int NC = N / EPC;                 // code words of the run
+  constexpr int PIECE = NC < 4 ? NC : 4;      // code words per store
+  static_assert(N % EPC == 0 && NC % PIECE == 0, "whole code words");
+  const uint64_t inv2 = pk2(c.inv, c.inv), nsc2 = pk2(-c.scale, -c.scale);
+  const uint64_t mg2 = pk2(c.magic, c.magic), zp2 = pk2(c.zp, c.zp);
 #pragma unroll
-    for (int i = 0; i < RUN; ++i) {
-      float f[CPW];
-      unpack_word<T>(col[i * WSTRIDE], f);
+  for (int q0 = 0; q0 < NC; q0 += PIECE) {
+    uint32_t out[PIECE];
 #pragma unroll
-      for (int c = 0; c < CPW; ++c) xf[c][i] = f[c];
-    }
-    float mn[CPW], mx[CPW];
-    const int r0 = (run / rpg) * rpg;
+    for (int q = 0; q < PIECE; ++q) {
+      uint32_t acc = 0;
 #pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      mn[c] = __int_as_float(0x7f800000);
-      mx[c] = AFF ? -__int_as_float(0x7f800000) : 0.f;
-      for (int q = 0; q < rpg; ++q) {
-        if (AFF) mn[c] = fminf(mn[c], red[((r0 + q) * D + w * CPW + c) * 2 + 0]);
-        mx[c] = fmaxf(mx[c], red[((r0 + q) * D + w * CPW + c) * 2 + 1]);
+      for (int j = EPC / 2 - 1; j >= 0; --j) {
+        const uint64_t t2 = code_pair<AFF>(pair_at<T>(w, (q0 + q) * EPC + 2 * j), inv2, nsc2, zp2, mg2, c.hi);
+        acc = acc * (1u << SB) + (uint32_t)(t2 >> 32);
+        acc = acc * (1u << SB) + (uint32_t)t2;
       }
+      out[q] = (acc - magic_sum<SB>(EPC)) ^ (c.flip & slot_mask<SB>(EPC));
     }
-    uint32_t out[CPW][NW];
-    FastCoder fc[CPW];
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      const GroupCoder gc = AFF ? make_affine(mn[c], mx[c], d.bits) : make_symmetric(mx[c], d.bits, d.packed != 0);
-      fc[c] = fast_coder<AFF>(gc, d.packed != 0, d.bits);
-      encode_run<SB, AFF, RUN>(xf[c], fc[c], out[c]);
-    }
-    if (act && tok0 < d.n_pad) {
-#pragma unroll
-      for (int c = 0; c < CPW; ++c) {
-        const int ch = w * CPW + c;
-        if (run % rpg == 0) {
-          const int64_t gi = ((int64_t)gslice * D + ch) * d.groups_row + (tok0 >> d.log2gs);
-          store_scale(d.scales, gi, d.scale_dtype, fc[c].scale);
-          if (AFF) d.zps[gi] = (uint8_t)fc[c].zp;
-        }
-        const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + tok0;
-        store_bytes<RUN * SB / 8>(d.codes + (e0 * SB) / 8, out[c]);
-      }
-    }
+    if (store) store_bytes<PIECE * 4>(dst + q0 * 4, out);
   }
 }
 
-// Channel-axis groups (values by default): groups of gs consecutive channels of one
-// token.  Item = (tier row, run of 32 channels); the runs of a row sit in adjacent
-// lanes, so group extrema combine with shuffles.
-template <typename T, int D, int TT, int SB, bool AFF>
-__device__ void quant_channel_half(const TensorDesc& d, const T* sx, int gslice, int j0, int rows) {
-  using G = RowGeom<T, D>;
-  constexpr int RPR = D / kRun;  // runs per row
-  constexpr int ITEMS = TT * RPR;
-  constexpr int ITER = (ITEMS + 127) / 128;
-  constexpr int NW = kRun * SB / 32;
-  constexpr int VPL = kRun * (int)sizeof(T) / 16;  // 16-byte vectors per run
-  const int ht = threadIdx.x & 127;
-  const int tpg = d.gs / kRun;  // runs (lanes) per group
-#pragma unroll 1
-  for (int itn = 0; itn < ITER; ++itn) {
-    const int item = ht + itn * 128;
-    const int r = item / RPR, run = item % RPR;
-    const bool act = item < ITEMS && r < rows;
-    float v[kRun];
-    float mn = __int_as_float(0x7f800000), mx = AFF ? -__int_as_float(0x7f800000) : 0.f;
-    if (item < ITEMS) {  // rows past the tier end hold zeros; read them to keep lanes converged
-      const uint4* src = reinterpret_cast<const uint4*>(sx + r * G::kPitch + run * kRun);
+// Same for two channels held in the halves of 16-bit column words.
+template <typename T, int SB, bool AFF, int GS>
+__device__ __forceinline__ void encode_store_columns(const uint32_t (&x)[GS], const FastCoder& c0,
+                                                     const FastCoder& c1, uint8_t* dst0, uint8_t* dst1) {
+  constexpr int EPC = 32 / SB;
+  constexpr int NC = GS / EPC;
+  constexpr int PIECE = NC < 4 ? NC : 4;
+  const uint64_t inv2 = pk2(c0.inv, c1.inv), nsc2 = pk2(-c0.scale, -c1.scale);
+  const uint64_t mg2 = pk2(c0.magic, c1.magic), zp2 = pk2(c0.zp, c1.zp);
 #pragma unroll
-      for (int q = 0; q < VPL; ++q) {
-        const uint4 raw = src[q];
-        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+  for (int q0 = 0; q0 < NC; q0 += PIECE) {
+    uint32_t o0[PIECE], o1[PIECE];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float f[4 / sizeof(T)];
-          unpack_word<T>(wv[u], f);
+    for (int q = 0; q < PIECE; ++q) {
+      uint32_t a0 = 0, a1 = 0;
 #pragma unroll
-          for (int e = 0; e < (int)(4 / sizeof(T)); ++e) v[(q * 4 + u) * (4 / sizeof(T)) + e] = f[e];
-        }
+      for (int i = EPC - 1; i >= 0; --i) {
+        const uint64_t t2 = code_pair<AFF>(Word16<T>::pair(x[(q0 + q) * EPC + i]), inv2, nsc2, zp2, mg2, c0.hi);
+        a0 = a0 * (1u << SB) + (uint32_t)t2;
+        a1 = a1 * (1u << SB) + (uint32_t)(t2 >> 32);
       }
-#pragma unroll
-      for (int i = 0; i < kRun; ++i) {
-        if (AFF) { mn = fminf(mn, v[i]); mx = fmaxf(mx, v[i]); }
-        else mx = fmaxf(mx, fabsf(v[i]));
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < kRun; ++i) v[i] = 0.f;
+      o0[q] = (a0 - magic_sum<SB>(EPC)) ^ (c0.flip & slot_mask<SB>(EPC));
+      o1[q] = (a1 - magic_sum<SB>(EPC)) ^ (c1.flip & slot_mask<SB>(EPC));
     }
-    for (int m = 1; m < tpg; m <<= 1) {
-      if (AFF) mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, m));
-      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, m));
-    }
-    const GroupCoder gc = AFF ? make_affine(mn, mx, d.bits) : make_symmetric(mx, d.bits, d.packed != 0);
-    const FastCoder fc = fast_coder<AFF>(gc, d.packed != 0, d.bits);
-    uint32_t out[NW];
-    encode_run<SB, AFF, kRun>(v, fc, out);
-    if (act) {
-      const int64_t row = (int64_t)gslice * d.n + j0 + r;
-      if (run % tpg == 0) {
-        const int64_t gi = row * d.groups_row + run / tpg;
-        store_scale(d.scales, gi, d.scale_dtype, fc.scale);
-        if (AFF) d.zps[gi] = (uint8_t)fc.zp;
-      }
-      const int64_t e0 = row * d.n_pad + run * kRun;
-      store_bytes<kRun * SB / 8>(d.codes + (e0 * SB) / 8, out);
-    }
+    store_bytes<PIECE * 4>(dst0 + q0 * 4, o0);
+    store_bytes<PIECE * 4>(dst1 + q0 * 4, o1);
   }
 }
 
-template <typename T, int D, int TT, int SB>
-__device__ __forceinline__ void quant_half_sb(const TensorDesc& d, const T* sx, int gslice, int j0, int rows,
-                                              float* red, int half) {
-  const bool aff = d.quantizer == GKV_AFFINE;
-  if (d.axis == GKV_AXIS_TOKEN) {
-    if (aff) quant_token_half<T, D, TT, SB, true>(d, sx, gslice, j0, red, half);
-    else quant_token_half<T, D, TT, SB, false>(d, sx, gslice, j0, red, half);
+// Statistics of a run of data words: absmax (symmetric) or min/max (affine),
+// per element half for 16-bit types.
+template <typename T, bool AFF, int NW>
+__device__ __forceinline__ void run_stats(const uint32_t (&w)[NW], float& mn, float& mx) {
+  if constexpr (sizeof(T) == 4) {
+    mn = __int_as_float(0x7f800000);
+    mx = AFF ? -__int_as_float(0x7f800000) : 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const float f = __uint_as_float(w[i]);
+      if (AFF) { mn = fminf(mn, f); mx = fmaxf(mx, f); }
+      else mx = fmaxf(mx, fabsf(f));
+    }
   } else {
-    if (aff) quant_channel_half<T, D, TT, SB, true>(d, sx, gslice, j0, rows);
-    else quant_channel_half<T, D, TT, SB, false>(d, sx, gslice, j0, rows);
+    using W = Word16<T>;
+    if (AFF) {
+      uint32_t a = W::kPosInf, b = W::kNegInf;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) { a = W::vmin(a, w[i]); b = W::vmax(b, w[i]); }
+      mn = fminf(W::lo(a), W::hi(a));
+      mx = fmaxf(W::lo(b), W::hi(b));
+    } else {
+      uint32_t a = 0u;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) a = W::amax(a, w[i]);
+      a &= 0x7FFF7FFFu;
+      mn = 0.f;
+      mx = fmaxf(W::lo(a), W::hi(a));
+    }
   }
 }
 
-template <typename T, int D, int TT>
-__device__ __forceinline__ void quant_half(const TensorDesc& d, const T* sx, int gslice, int j0, int rows, float* red,
-                                           int half) {
-  if (d.sbits == 4) quant_half_sb<T, D, TT, 4>(d, sx, gslice, j0, rows, red, half);
-  else if (d.sbits == 2) quant_half_sb<T, D, TT, 2>(d, sx, gslice, j0, rows, red, half);
-  else quant_half_sb<T, D, TT, 8>(d, sx, gslice, j0, rows, red, half);
+// ---------------------------------------------------------------------------
+// token-axis groups (K): thread = (column word, group)
+// ---------------------------------------------------------------------------
+template <typename T, int D, int GS, int SB, bool AFF>
+__device__ void quant_tokens(const TensorDesc& d, const uint8_t* sx, int gslice, int j0, int ht) {
+  using G = QGeom<T, D>;
+  constexpr int NG = kQTile / GS;          // groups per tile
+  constexpr int ITEMS = G::kWords * NG;
+#pragma unroll 1
+  for (int item = ht; item < ITEMS; item += kQThreads) {
+    const int g = item / G::kWords, w = item - g * G::kWords;
+    const int tok0 = j0 + g * GS;
+    if (tok0 >= d.n_pad) continue;  // a whole group of padding past the padded tier
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (g * GS) * G::kPitchB) + w;
+    uint32_t x[GS];
+#pragma unroll
+    for (int i = 0; i < GS; ++i) x[i] = col[i * G::kPitchW];
+    if constexpr (sizeof(T) == 4) {
+      float mn, mx;
+      run_stats<T, AFF, GS>(x, mn, mx);
+      const FastCoder c = AFF ? aff_coder(mn, mx, d.qmax, d.rqmax)
+                              : sym_coder(mx, d.qmax, d.rqmax, d.bits, d.packed != 0);
+      const int ch = w;
+      const int64_t gi = ((int64_t)gslice * D + ch) * d.groups_row + (tok0 >> d.log2gs);
+      store_scale(d.scales, gi, d.scale_dtype, c.scale);
+      if (AFF) d.zps[gi] = (uint8_t)c.zp;
+      const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + tok0;
+      encode_store_run<T, SB, AFF, GS>(x, c, d.codes + (e0 * SB) / 8, true);
+    } else {
+      using W = Word16<T>;
+      FastCoder c0, c1;
+      if (AFF) {
+        uint32_t a = W::kPosInf, b = W::kNegInf;
+#pragma unroll
+        for (int i = 0; i < GS; ++i) { a = W::vmin(a, x[i]); b = W::vmax(b, x[i]); }
+        c0 = aff_coder(W::lo(a), W::lo(b), d.qmax, d.rqmax);
+        c1 = aff_coder(W::hi(a), W::hi(b), d.qmax, d.rqmax);
+      } else {
+        uint32_t a = 0u;
+#pragma unroll
+        for (int i = 0; i < GS; ++i) a = W::amax(a, x[i]);
+        a &= 0x7FFF7FFFu;
+        c0 = sym_coder(W::lo(a), d.qmax, d.rqmax, d.bits, d.packed != 0);
+        c1 = sym_coder(W::hi(a), d.qmax, d.rqmax, d.bits, d.packed != 0);
+      }
+      const int ch = 2 * w;
+      const int64_t gi0 = ((int64_t)gslice * D + ch) * d.groups_row + (tok0 >> d.log2gs);
+      store_scale(d.scales, gi0, d.scale_dtype, c0.scale);
+      store_scale(d.scales, gi0 + d.groups_row, d.scale_dtype, c1.scale);
+      if (AFF) {
+        d.zps[gi0] = (uint8_t)c0.zp;
+        d.zps[gi0 + d.groups_row] = (uint8_t)c1.zp;
+      }
+      const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + tok0;
+      encode_store_columns<T, SB, AFF, GS>(x, c0, c1, d.codes + (e0 * SB) / 8, d.codes + ((e0 + d.n_pad) * SB) / 8);
+    }
+  }
 }
 
-template <typename T, int D, int TT>
-struct QuantTileSmem {
-  using G = RowGeom<T, D>;
-  static constexpr size_t kTensor = (size_t)TT * G::kPitch * sizeof(T);     // one staged tensor tile
-  static constexpr size_t kBuffer = 2 * kTensor;                           // K and V
-  static constexpr size_t kRed = 2 * (size_t)(TT / kTokRun) * D * 2 * sizeof(float);  // per-half run extrema
-  static constexpr size_t kTotal = kBuffer + kRed;
-};
+// ---------------------------------------------------------------------------
+// channel-axis groups (V): thread = (row, run of 128 bytes)
+// ---------------------------------------------------------------------------
+// In-register Hadamard transform of one row split into RPR runs of RUN elements
+// held by the lanes 8 apart (run u in lane bits 3-4).  Butterflies h = 1 .. RUN/2
+// inside the thread, h >= RUN across lanes, in the reference order; then y / div:
+// the fused quotient when `fused` (proven exact for quotients >= 2^-100) and no
+// |y| of this thread is below 2^-90 (zeros included: the fused form turns -0
+// into +0), else IEEE division.
+template <int RUN, int RPR>
+__device__ __forceinline__ void rotate_run(uint64_t (&v)[RUN / 2], int u, float div, float rdiv, bool fused) {
+  // h = 1: inside each pair
+#pragma unroll
+  for (int k = 0; k < RUN / 2; ++k) {
+    const float a = lo2(v[k]), b = hi2(v[k]);
+    v[k] = pk2(__fadd_rn(a, b), __fsub_rn(a, b));
+  }
+  // h = 2 .. RUN/2: pairs k and k + h/2
+#pragma unroll
+  for (int h = 2; h < RUN; h <<= 1) {
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) {
+      if ((2 * k) & h) continue;
+      const uint64_t a = v[k], b = v[k + h / 2];
+      v[k] = add2(a, b);
+      v[k + h / 2] = sub2(a, b);
+    }
+  }
+  // h = RUN .. (RPR * RUN) / 2: across lanes
+#pragma unroll
+  for (int m = 1; m < RPR; m <<= 1) {
+    const bool right = (u & m) != 0;
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) {
+      const float o0 = __shfl_xor_sync(kFull, lo2(v[k]), 8 * m);
+      const float o1 = __shfl_xor_sync(kFull, hi2(v[k]), 8 * m);
+      const uint64_t o = pk2(o0, o1);
+      v[k] = right ? sub2(o, v[k]) : add2(v[k], o);
+    }
+  }
+  float least = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int k = 0; k < RUN / 2; ++k) least = fminf(least, fminf(fabsf(lo2(v[k])), fabsf(hi2(v[k]))));
+  if (fused && !(least < 8.077935669463161e-28f /* 2^-90 */)) {
+    const uint64_t nd2 = pk2(-div, -div), rd2 = pk2(rdiv, rdiv);
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) v[k] = quot2(v[k], nd2, rd2);
+  } else {
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) v[k] = pk2(__fdiv_rn(lo2(v[k]), div), __fdiv_rn(hi2(v[k]), div));
+  }
+}
 
-template <typename T, int D, int TT>
-constexpr size_t quant_tile_smem() {
-  return QuantTileSmem<T, D, TT>::kTotal;
+template <typename T, int NW>
+__device__ __forceinline__ void load_run(const uint8_t* src, uint32_t (&w)[NW]) {
+#pragma unroll
+  for (int q = 0; q < NW / 4; ++q) {
+    const uint4 r = reinterpret_cast<const uint4*>(src)[q];
+    w[4 * q] = r.x; w[4 * q + 1] = r.y; w[4 * q + 2] = r.z; w[4 * q + 3] = r.w;
+  }
+}
+
+template <typename T, int RUN, int NW>
+__device__ __forceinline__ void words_to_pairs(const uint32_t (&w)[NW], uint64_t (&v)[RUN / 2]) {
+#pragma unroll
+  for (int k = 0; k < RUN / 2; ++k) v[k] = pair_at<T>(w, 2 * k);
+}
+
+template <typename T, int RUN, int NW>
+__device__ __forceinline__ void pairs_to_words(const uint64_t (&v)[RUN / 2], uint32_t (&w)[NW]) {
+#pragma unroll
+  for (int k = 0; k < RUN / 2; ++k) {
+    if constexpr (sizeof(T) == 4) {
+      w[2 * k] = (uint32_t)v[k];
+      w[2 * k + 1] = (uint32_t)(v[k] >> 32);
+    } else {
+      w[k] = Word16<T>::round2(lo2(v[k]), hi2(v[k]));
+    }
+  }
+}
+
+template <typename T, int D, int RUN, int SB, bool AFF, bool ROT>
+__device__ void quant_channels(const TensorDesc& d, const uint8_t* sx, int gslice, int j0, int rows, int ht,
+                               float div, float rdiv, bool fused) {
+  using G = QGeom<T, D>;
+  constexpr int RPR = D / RUN;             // runs per row (1, 2 or 4)
+  constexpr int NW = RUN * (int)sizeof(T) / 4;
+  constexpr int ROWS_STEP = 32 / RPR;      // rows per warp step (lane = row j + 8 * (run + RPR * row block))
+  constexpr int STEPS = kQTile / ROWS_STEP;
+  static_assert(RPR == 1 || RPR == 2 || RPR == 4, "runs per row");
+  const int lane = threadIdx.x & 31, hw = ht >> 5;
+  const int j = lane & 7, k = lane >> 3;
+  const int u = k % RPR, rb = k / RPR;
+  const int rpg = d.gs / RUN;              // runs per group: 1, 2 or 4 (gs >= RUN)
+#pragma unroll 1
+  for (int step = hw; step < STEPS; step += 2) {
+    const int r = step * ROWS_STEP + rb * 8 + j;
+    const uint8_t* src = sx + r * G::kPitchB + u * (RUN * (int)sizeof(T));
+    uint32_t w[NW];
+    load_run<T, NW>(src, w);
+    if constexpr (ROT) {
+      uint64_t v[RUN / 2];
+      words_to_pairs<T, RUN, NW>(w, v);
+      rotate_run<RUN, RPR>(v, u, div, rdiv, fused);
+      pairs_to_words<T, RUN, NW>(v, w);
+    }
+    float mn, mx;
+    run_stats<T, AFF, NW>(w, mn, mx);
+    for (int m = 1; m < rpg; m <<= 1) {
+      if (AFF) mn = fminf(mn, __shfl_xor_sync(kFull, mn, 8 * m));
+      mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 8 * m));
+    }
+    const FastCoder c = AFF ? aff_coder(mn, mx, d.qmax, d.rqmax) : sym_coder(mx, d.qmax, d.rqmax, d.bits, d.packed != 0);
+    const bool act = r < rows;
+    const int64_t row = (int64_t)gslice * d.n + j0 + r;
+    if (act && u % rpg == 0) {
+      const int64_t gi = row * d.groups_row + u / rpg;
+      store_scale(d.scales, gi, d.scale_dtype, c.scale);
+      if (AFF) d.zps[gi] = (uint8_t)c.zp;
+    }
+    const int64_t e0 = row * d.n_pad + u * RUN;
+    encode_store_run<T, SB, AFF, NW>(w, c, d.codes + (e0 * SB) / 8, act);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dispatch on the tensor's runtime parameters
+// ---------------------------------------------------------------------------
+template <typename T, int D, int SB>
+__device__ __forceinline__ void quant_tile_tokens_sb(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
+                                                     int ht) {
+  const bool aff = d.quantizer == GKV_AFFINE;
+  if (d.gs == 64) {
+    if (aff) quant_tokens<T, D, 64, SB, true>(d, sx, gslice, j0, ht);
+    else quant_tokens<T, D, 64, SB, false>(d, sx, gslice, j0, ht);
+  } else {
+    if (aff) quant_tokens<T, D, 32, SB, true>(d, sx, gslice, j0, ht);
+    else quant_tokens<T, D, 32, SB, false>(d, sx, gslice, j0, ht);
+  }
+}
+
+template <typename T, int D, int RUN, int SB>
+__device__ __forceinline__ void quant_tile_channels_sb(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
+                                                       int rows, int ht, float div, float rdiv, bool fused) {
+  const bool aff = d.quantizer == GKV_AFFINE;
+  if (d.rotation) {
+    if (aff) quant_channels<T, D, RUN, SB, true, true>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    else quant_channels<T, D, RUN, SB, false, true>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+  } else {
+    if (aff) quant_channels<T, D, RUN, SB, true, false>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    else quant_channels<T, D, RUN, SB, false, false>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+  }
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void quant_tile_channels(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
+                                                    int rows, int ht, float div, float rdiv, bool fused) {
+  // run = 128 bytes, or half of that when the group is smaller or the rows are
+  // rotated (64 fp32 values of a run in registers leave too few for the rest)
+  constexpr int RUN = QGeom<T, D>::kRun;
+  if (d.gs < RUN || (d.rotation && RUN / 2 >= 32)) {
+    if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) {
+      if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN / 2, 4>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+      else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN / 2, 2>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+      else quant_tile_channels_sb<T, D, RUN / 2, 8>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    }
+  } else {
+    if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN, 4>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN, 2>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    else quant_tile_channels_sb<T, D, RUN, 8>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+  }
 }
 
 // Tile t of a launch -> (slice, tier, tile within the tier); tier 0 = retained rows.
@@ -305,86 +453,72 @@ __device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
   return r;
 }
 
-template <typename T>
-struct SliceIn {
-  const T* kb;
-  const T* vb;
-  int64_t kst, vst;
-};
-template <typename T>
-__device__ __forceinline__ SliceIn<T> slice_in(const QuantParams& p, int s) {
-  const LayerDesc& L = p.layers[find_layer(p, s)];
-  const int local = s - L.slice_begin;
-  const int b = local / L.heads, h = local - b * L.heads;
-  return {reinterpret_cast<const T*>(L.k) + b * L.ks[0] + h * L.ks[1],
-          reinterpret_cast<const T*>(L.v) + b * L.vs[0] + h * L.vs[1], L.ks[2], L.vs[2]};
-}
-
-// Issue the 16-byte asynchronous copies that gather tile t's K and V rows into a
-// staging buffer (rows past the end of the tier are zero-filled: token-axis groups
-// quantize them as padding), then commit them as one group.  Retained tiles stage
-// nothing but still commit a group so that the group count stays uniform.
-template <typename T, int D, int TT>
-__device__ __forceinline__ void stage_tile(const QuantParams& p, int t, T* sk, T* sv) {
-  using G = RowGeom<T, D>;
-  const TileRef tr = tile_ref(p, t);
-  if (tr.tier != 0) {
-    const SliceIn<T> in = slice_in<T>(p, tr.s);
-    const int* idx = p.idx[tr.tier];
-    const int j0 = tr.k * TT;
-    const int rows = min(TT, p.n_tier[tr.tier] - j0);
-    constexpr int CH = TT * G::kChunks;  // chunks per tensor
+// Gather the tile's rows of one tensor into shared memory: thread = (16-byte
+// chunk, rows r0, r0 + step, ...); the lanes of a warp cover whole rows
+// (coalesced).  Rows past the end of the tier are zero-filled (token-axis groups
+// quantize them as padding).
+template <typename T, int D>
+__device__ __forceinline__ void stage_tile(const QuantParams& p, const TileRef& tr, const T* base, int64_t st,
+                                           uint8_t* sx) {
+  using G = QGeom<T, D>;
+  constexpr int STEP = kQThreads / G::kChunks;  // rows per pass
+  const int* idx = p.idx[tr.tier];
+  const int j0 = tr.k * kQTile;
+  const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+  const int c = threadIdx.x % G::kChunks, r0 = threadIdx.x / G::kChunks;
 #pragma unroll
-    for (int i = 0; i < 2 * CH / kThreads; ++i) {
-      const int e = threadIdx.x + i * kThreads;
-      const int tsr = e / CH, rem = e - tsr * CH;
-      const int r = rem / G::kChunks, c = rem - r * G::kChunks;
-      int tok = 0;
-      if (r < rows) {
-        tok = idx[j0 + r];
-        if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
-      }
-      const T* src = (tsr ? in.vb + tok * in.vst : in.kb + tok * in.kst) + c * G::kVec;
-      cp_async16((tsr ? sv : sk) + r * G::kPitch + c * G::kVec, src, r < rows ? 16u : 0u);
+  for (int i = 0; i < kQTile / STEP; ++i) {
+    const int r = r0 + i * STEP;
+    int tok = 0;
+    if (r < rows) {
+      tok = idx[j0 + r];
+      if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
     }
+    cp_async16(sx + r * G::kPitchB + c * 16, base + tok * st + c * (16 / (int)sizeof(T)), r < rows ? 16u : 0u);
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// One block per tile: retained-row tiles copy rows; standard / cold tiles gather
-// the K and V rows into shared memory (16-byte asynchronous copies from every
-// thread), then warps 0-3 quantize K and warps 4-7 quantize V, each half on its own
-// named barrier.
-template <typename T, int D, int TT>
-__global__ void __launch_bounds__(kThreads, 3) quantize_tile_kernel(const __grid_constant__ QuantParams p,
-                                                                    int total_tiles) {
+// One block per tile of one tensor (`tensor` 1: values, 0: keys).  The kernel is
+// compiled per grouping axis (AXIS = GKV_AXIS_TOKEN / GKV_AXIS_CHANNEL): tiles
+// of a tier whose tensor is grouped along the other axis are left to the other
+// kernel.  Retained-row tiles copy rows when `copy_retained`; standard / cold
+// tiles gather the rows into shared memory, then quantize them.
+template <typename T, int D, int AXIS>
+__global__ void __launch_bounds__(kQThreads, 8) quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor,
+                                                                     int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
-  using SM = QuantTileSmem<T, D, TT>;
-  (void)total_tiles;
-  const int t = blockIdx.x;
-  const TileRef tr = tile_ref(p, t);
+  const TileRef tr = tile_ref(p, blockIdx.x);
+  if (tr.tier == 0 && !copy_retained) return;
+  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+  if (tr.tier != 0 && d.axis != AXIS) return;
   const int gslice = p.slice_offset + tr.s;
+  const LayerDesc& L = p.layers[find_layer(p, tr.s)];
+  const int local = tr.s - L.slice_begin;
+  const int b = local / L.heads, h = local - b * L.heads;
+  const T* base = tensor ? reinterpret_cast<const T*>(L.v) + b * L.vs[0] + h * L.vs[1]
+                         : reinterpret_cast<const T*>(L.k) + b * L.ks[0] + h * L.ks[1];
+  const int64_t st = tensor ? L.vs[2] : L.ks[2];
   if (tr.tier == 0) {
-    const SliceIn<T> in = slice_in<T>(p, tr.s);
-    copy_retained_tile<T, D>(p, in.kb, in.vb, in.kst, in.vst, gslice, tr.k);
+    copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
     return;
   }
-  T* sk = reinterpret_cast<T*>(smem);
-  T* sv = reinterpret_cast<T*>(smem + SM::kTensor);
-  float* red = reinterpret_cast<float*>(smem + SM::kBuffer);
-  stage_tile<T, D, TT>(p, t, sk, sv);
+  stage_tile<T, D>(p, tr, base, st, smem);
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  const int j0 = tr.k * TT;
-  const int rows = min(TT, p.n_tier[tr.tier] - j0);
-  const int half = threadIdx.x >> 7;
-  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + half];
-  T* sx = half ? sv : sk;
-  if (d.rotation) {
-    rotate_rows_half<T, D>(sx, rows, p.had_div, p.had_inv, (threadIdx.x >> 5) & 3);
-    bar_half(half);
+  const int j0 = tr.k * kQTile;
+  const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+  if constexpr (AXIS == GKV_AXIS_TOKEN) {
+    if (d.rotation) {
+      rotate_rows_smem<T, D>(reinterpret_cast<T*>(smem), p.had_div, p.had_inv, threadIdx.x >> 5);
+      __syncthreads();
+    }
+    if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, smem, gslice, j0, threadIdx.x);
+    else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, smem, gslice, j0, threadIdx.x);
+    else quant_tile_tokens_sb<T, D, 8>(d, smem, gslice, j0, threadIdx.x);
+  } else {
+    quant_tile_channels<T, D>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
   }
-  quant_half<T, D, TT>(d, sx, gslice, j0, rows, red + half * (TT / kTokRun) * D * 2, half);
 }
 
 // ---------------------------------------------------------------------------
@@ -551,22 +685,40 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 // ---------------------------------------------------------------------------
 int device_sm_count();
 
-template <typename T, int D, int TT>
+// Per tensor (keys, values): one launch per grouping axis its tiers use; the
+// first of them also copies the tensor's retained rows.
+template <typename T, int D>
 static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
-  const size_t sm = quant_tile_smem<T, D, TT>();
-  auto kern = quantize_tile_kernel<T, D, TT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  if (e != cudaSuccess) return e;
+  const size_t sm = QGeom<T, D>::kSmem;
   const int64_t tiles = (int64_t)p.S * p.tiles_slice;
   if (tiles == 0) return cudaSuccess;
-  kern<<<(unsigned)tiles, kThreads, sm, st>>>(p, (int)tiles);
-  return cudaGetLastError();
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(quantize_tile_kernel<T, D, GKV_AXIS_TOKEN>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess)
+    return e;
+  if ((e = cudaFuncSetAttribute(quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess)
+    return e;
+  for (int tensor = 0; tensor < 2; ++tensor) {
+    bool token = false, channel = false;
+    for (int tier = 1; tier <= 2; ++tier) {
+      if (p.tiles[tier] == 0) continue;
+      const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+      (d.axis == GKV_AXIS_TOKEN ? token : channel) = true;
+    }
+    if (!token && !channel) channel = true;  // retained rows only
+    if (token) quantize_tile_kernel<T, D, GKV_AXIS_TOKEN><<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, 1);
+    if (channel)
+      quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL><<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, token ? 0 : 1);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 template <typename T>
 static cudaError_t launch_tile_d(const QuantParams& p, cudaStream_t st) {
-  if (p.D == 64) return p.tt == 64 ? launch_tile<T, 64, 64>(p, st) : launch_tile<T, 64, 128>(p, st);
-  if (p.D == 128) return p.tt == 64 ? launch_tile<T, 128, 64>(p, st) : launch_tile<T, 128, 128>(p, st);
+  if (p.D == 64) return launch_tile<T, 64>(p, st);
+  if (p.D == 128) return launch_tile<T, 128>(p, st);
   return cudaErrorInvalidConfiguration;
 }
 

@@ -3,8 +3,9 @@
 ``CompressionEngine(pairs, config, scores)`` resolves the policy, allocates the
 device arena of every stored tensor and the dequantized outputs, and builds the
 C plans once.  Each ``quantize()`` then issues, per run of same-shaped layers,
-one selection launch and one quantize launch; ``dequantize()`` issues one
-dequantize launch -- no allocation, no Python object construction.  The
+one selection launch and two quantize launches (keys, values) per 40 layers;
+``dequantize()`` issues one dequantize launch -- no allocation, no Python object
+construction.  The
 inputs are read at their current addresses on every call, so callers refill
 them in place (e.g. a serving loop that compresses caches of one shape).
 
@@ -48,7 +49,8 @@ class CompressionEngine:
             if it[0] != "run":
                 continue
             run = it[1]
-            n += (1 if it[3] else 0) + (1 if run.outlier is not None else 0) + 2
+            chunks = -(-len(run.pairs) // 40)  # gkv_quantize splits calls into 40-layer launches
+            n += (1 if it[3] else 0) + (1 if run.outlier is not None else 0) + 2 * chunks + 1
         return n
 
     def quantize(self) -> None:
