@@ -326,6 +326,7 @@ int32_t gkv_quantize(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n
   q.tiles[0] = r.fast[0] ? (int)ceil_div(r.n[0], kRetTile) : 0;
   for (int k = 1; k <= 2; ++k) q.tiles[k] = r.fast[k] ? (int)ceil_div(r.n[k], r.tt) : 0;
   q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
+  q.tile_div = make_fastdiv((uint32_t)(q.tiles_slice > 0 ? q.tiles_slice : 1));
   int64_t slice0 = 0;
   for (int l0 = 0; l0 < n_layers; l0 += kMaxLayers) {
     const int nl = n_layers - l0 < kMaxLayers ? n_layers - l0 : kMaxLayers;
@@ -343,6 +344,10 @@ int32_t gkv_quantize(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n
     q.n_layers = nl;
     q.S = S;
     q.slice_offset = (int)slice0;
+    bool uniform = true;
+    for (int l = 1; l < nl; ++l) uniform &= q.layers[l].heads == q.layers[0].heads;
+    q.layer_div = uniform ? make_fastdiv((uint32_t)(p.batch * q.layers[0].heads)) : FastDiv{0u, 0u, 0, 0};
+    q.head_div = make_fastdiv((uint32_t)q.layers[0].heads);
     cudaError_t e = cudaSuccess;
     if (q.tiles_slice > 0 && (e = launch_quantize_tiles(q, p.dtype, s)) != cudaSuccess)
       return cuda_fail(e, "quantize tile kernel");

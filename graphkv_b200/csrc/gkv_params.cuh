@@ -15,6 +15,29 @@ constexpr int kTokRun = 16;      // rows of one thread's run of a token-axis qua
 // Tier numbering inside the kernels: 0 retained, 1 standard, 2 cold.
 // Tensor numbering follows gkv_tensor_slot: 0 std K, 1 std V, 2 cold K, 3 cold V.
 
+// Division of 32-bit unsigned integers by a divisor fixed per launch: the
+// round-up multiply-high method of T. Granlund and P. Montgomery ("Division by
+// invariant integers using multiplication", PLDI 1994, figure 4.1), exact for
+// every n < 2^32 and 1 <= d <= 2^31.
+struct FastDiv {
+  uint32_t d, m;
+  int s1, s2;
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    const uint32_t t = __umulhi(m, n);
+    return (t + ((n - t) >> s1)) >> s2;
+  }
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  int l = 0;
+  while ((1ull << l) < d) ++l;
+  FastDiv f;
+  f.d = d;
+  f.m = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+  f.s1 = l > 0 ? 1 : 0;
+  f.s2 = l > 0 ? l - 1 : 0;
+  return f;
+}
+
 struct TensorDesc {
   int bits;         // 2, 4, 8
   int quantizer;    // GKV_SYMMETRIC / GKV_AFFINE
@@ -61,6 +84,9 @@ struct QuantParams {
   int tiles[3];      // fast-path tiles per slice per tier (0 when the tier is not in this launch)
   int tiles_slice;
   int slice_offset;  // global index of slice 0 of this launch (retained / codes addressing)
+  FastDiv tile_div;  // by tiles_slice
+  FastDiv layer_div; // by the slices of one layer when every layer has as many (d == 0: they differ)
+  FastDiv head_div;  // by the heads of a layer (valid when layer_div is)
   LayerDesc layers[kMaxLayers];
 };
 
@@ -81,6 +107,7 @@ struct DequantParams {
 
 // Slice -> layer lookup (layers sorted by slice_begin).
 __device__ __forceinline__ int find_layer(const QuantParams& p, int s) {
+  if (p.layer_div.d) return (int)p.layer_div.div((uint32_t)s);
   int l = 0;
   while (l + 1 < p.n_layers && s >= p.layers[l + 1].slice_begin) ++l;
   return l;

@@ -291,15 +291,16 @@ __device__ __forceinline__ void rotate_run(uint64_t (&v)[RUN / 2], int u, float 
     }
   }
   // h = RUN .. (RPR * RUN) / 2: across lanes
+  // (left lane: v + o; right lane: o - v, as fma(-1, v, o): one rounding, as the subtraction)
 #pragma unroll
   for (int m = 1; m < RPR; m <<= 1) {
-    const bool right = (u & m) != 0;
+    const float sg = (u & m) ? -1.f : 1.f;
+    const uint64_t sg2 = pk2(sg, sg);
 #pragma unroll
     for (int k = 0; k < RUN / 2; ++k) {
       const float o0 = __shfl_xor_sync(kFull, lo2(v[k]), 8 * m);
       const float o1 = __shfl_xor_sync(kFull, hi2(v[k]), 8 * m);
-      const uint64_t o = pk2(o0, o1);
-      v[k] = right ? sub2(o, v[k]) : add2(v[k], o);
+      v[k] = fma2(sg2, v[k], pk2(o0, o1));
     }
   }
   float least = __int_as_float(0x7f800000);
@@ -419,10 +420,9 @@ __device__ __forceinline__ void quant_tile_channels_sb(const TensorDesc& d, cons
 template <typename T, int D>
 __device__ __forceinline__ void quant_tile_channels(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
                                                     int rows, int ht, float div, float rdiv, bool fused) {
-  // run = 128 bytes, or half of that when the group is smaller or the rows are
-  // rotated (64 fp32 values of a run in registers leave too few for the rest)
+  // run = 128 bytes, or half of that when the group is smaller
   constexpr int RUN = QGeom<T, D>::kRun;
-  if (d.gs < RUN || (d.rotation && RUN / 2 >= 32)) {
+  if (d.gs < RUN) {
     if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) {
       if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN / 2, 4>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
       else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN / 2, 2>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
@@ -441,7 +441,7 @@ struct TileRef {
 };
 __device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
   TileRef r;
-  r.s = t / p.tiles_slice;
+  r.s = (int)p.tile_div.div((uint32_t)t);
   int k = t - r.s * p.tiles_slice;
   r.tier = 0;
   if (k >= p.tiles[0]) {
@@ -453,71 +453,130 @@ __device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
   return r;
 }
 
-// Gather the tile's rows of one tensor into shared memory: thread = (16-byte
-// chunk, rows r0, r0 + step, ...); the lanes of a warp cover whole rows
-// (coalesced).  Rows past the end of the tier are zero-filled (token-axis groups
-// quantize them as padding).
+// Issue the loads of tile `tr` of one tensor into a staging buffer: thread r
+// copies row r with one bulk copy (TMA, 16-byte aligned rows) that completes on
+// `bar`; rows past the end of the tier are zero-filled in place (token-axis
+// groups quantize them as padding).  Thread 0 arms the barrier with the bytes.
 template <typename T, int D>
 __device__ __forceinline__ void stage_tile(const QuantParams& p, const TileRef& tr, const T* base, int64_t st,
-                                           uint8_t* sx) {
+                                           uint8_t* sx, uint64_t* bar) {
   using G = QGeom<T, D>;
-  constexpr int STEP = kQThreads / G::kChunks;  // rows per pass
-  const int* idx = p.idx[tr.tier];
+  static_assert(kQThreads == kQTile, "one row per thread");
   const int j0 = tr.k * kQTile;
   const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-  const int c = threadIdx.x % G::kChunks, r0 = threadIdx.x / G::kChunks;
+  const int r = threadIdx.x;
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(bar, (uint32_t)(rows * G::kRowBytes));
+  uint8_t* dst = sx + r * G::kPitchB;
+  if (r < rows) {
+    int tok = p.idx[tr.tier][j0 + r];
+    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
+    bulk_load(dst, base + tok * st, (uint32_t)G::kRowBytes, bar);
+  } else {
 #pragma unroll
-  for (int i = 0; i < kQTile / STEP; ++i) {
-    const int r = r0 + i * STEP;
-    int tok = 0;
-    if (r < rows) {
-      tok = idx[j0 + r];
-      if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
-    }
-    cp_async16(sx + r * G::kPitchB + c * 16, base + tok * st + c * (16 / (int)sizeof(T)), r < rows ? 16u : 0u);
+    for (int c = 0; c < G::kChunks; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0u, 0u, 0u, 0u);
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// One block per tile of one tensor (`tensor` 1: values, 0: keys).  The kernel is
-// compiled per grouping axis (AXIS = GKV_AXIS_TOKEN / GKV_AXIS_CHANNEL): tiles
-// of a tier whose tensor is grouped along the other axis are left to the other
-// kernel.  Retained-row tiles copy rows when `copy_retained`; standard / cold
-// tiles gather the rows into shared memory, then quantize them.
-template <typename T, int D, int AXIS>
-__global__ void __launch_bounds__(kQThreads, 8) quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor,
-                                                                     int copy_retained) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const TileRef tr = tile_ref(p, blockIdx.x);
-  if (tr.tier == 0 && !copy_retained) return;
+// Slice base pointer and token stride of one tensor.
+template <typename T>
+__device__ __forceinline__ const T* tensor_base(const QuantParams& p, int s, int tensor, int64_t& st) {
+  const LayerDesc& L = p.layers[find_layer(p, s)];
+  const int local = s - L.slice_begin;
+  const int b = p.layer_div.d ? (int)p.head_div.div((uint32_t)local) : local / L.heads;
+  const int h = local - b * L.heads;
+  st = tensor ? L.vs[2] : L.ks[2];
+  return tensor ? reinterpret_cast<const T*>(L.v) + b * L.vs[0] + h * L.vs[1]
+                : reinterpret_cast<const T*>(L.k) + b * L.ks[0] + h * L.ks[1];
+}
+
+// Does this launch handle tile t, and does it stage rows for it?
+template <int AXIS>
+__device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr, int tensor, int copy_retained) {
+  if (tr.tier == 0) return copy_retained ? 1 : 0;  // 1: retained copy
   const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-  if (tr.tier != 0 && d.axis != AXIS) return;
-  const int gslice = p.slice_offset + tr.s;
-  const LayerDesc& L = p.layers[find_layer(p, tr.s)];
-  const int local = tr.s - L.slice_begin;
-  const int b = local / L.heads, h = local - b * L.heads;
-  const T* base = tensor ? reinterpret_cast<const T*>(L.v) + b * L.vs[0] + h * L.vs[1]
-                         : reinterpret_cast<const T*>(L.k) + b * L.ks[0] + h * L.ks[1];
-  const int64_t st = tensor ? L.vs[2] : L.ks[2];
-  if (tr.tier == 0) {
-    copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
-    return;
+  return d.axis == AXIS ? 2 : 0;                     // 2: quantize
+}
+
+// Persistent blocks over the tiles of one tensor (`tensor` 1: values, 0: keys),
+// compiled per grouping axis (AXIS): tiles of a tier grouped along the other
+// axis are left to the other kernel; retained-row tiles are copied when
+// `copy_retained`.  Two staging buffers: while a tile is quantized, the rows of
+// the block's next tile are in flight.
+template <typename T, int D, int AXIS>
+__global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor,
+                                                                     int copy_retained, int total_tiles) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  using G = QGeom<T, D>;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * G::kSmem);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
   }
-  stage_tile<T, D>(p, tr, base, st, smem);
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  const int j0 = tr.k * kQTile;
-  const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-  if constexpr (AXIS == GKV_AXIS_TOKEN) {
-    if (d.rotation) {
-      rotate_rows_smem<T, D>(reinterpret_cast<T*>(smem), p.had_div, p.had_inv, threadIdx.x >> 5);
-      __syncthreads();
+  // first tile of this block that the launch handles
+  int cur = blockIdx.x;
+  int role = 0;
+  for (; cur < total_tiles; cur += gridDim.x)
+    if ((role = tile_role<AXIS>(p, tile_ref(p, cur), tensor, copy_retained)) != 0) break;
+  uint32_t phase = 0u;    // bit b: parity of buffer b's next phase
+  uint32_t pending = 0u;  // bit b: buffer b has copies in flight
+  int buf = 0;
+  if (cur < total_tiles && role == 2) {
+    const TileRef tr = tile_ref(p, cur);
+    int64_t st;
+    const T* base = tensor_base<T>(p, tr.s, tensor, st);
+    stage_tile<T, D>(p, tr, base, st, smem, &bar[0]);
+    pending = 1u;
+  }
+  while (cur < total_tiles) {
+    // find and stage the next tile
+    int nxt = cur + gridDim.x, nrole = 0;
+    for (; nxt < total_tiles; nxt += gridDim.x)
+      if ((nrole = tile_role<AXIS>(p, tile_ref(p, nxt), tensor, copy_retained)) != 0) break;
+    if (nxt < total_tiles && nrole == 2) {
+      const TileRef tn = tile_ref(p, nxt);
+      int64_t st;
+      const T* base = tensor_base<T>(p, tn.s, tensor, st);
+      stage_tile<T, D>(p, tn, base, st, smem + (buf ^ 1) * G::kSmem, &bar[buf ^ 1]);
+      pending |= 1u << (buf ^ 1);
     }
-    if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, smem, gslice, j0, threadIdx.x);
-    else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, smem, gslice, j0, threadIdx.x);
-    else quant_tile_tokens_sb<T, D, 8>(d, smem, gslice, j0, threadIdx.x);
-  } else {
-    quant_tile_channels<T, D>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
+    const TileRef tr = tile_ref(p, cur);
+    const int gslice = p.slice_offset + tr.s;
+    int64_t st;
+    const T* base = tensor_base<T>(p, tr.s, tensor, st);
+    if (role == 1) {
+      copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
+    } else {
+      const bool ok = block_wait(&bar[buf], (phase >> buf) & 1u);
+      phase ^= 1u << buf;
+      pending &= ~(1u << buf);
+      if (!ok) {
+        // error recorded; let the other buffer's copies land (bounded) before exiting
+        if (pending & (1u << (buf ^ 1))) block_wait(&bar[buf ^ 1], (phase >> (buf ^ 1)) & 1u);
+        return;
+      }
+      uint8_t* sx = smem + buf * G::kSmem;
+      const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+      const int j0 = tr.k * kQTile;
+      const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+      if constexpr (AXIS == GKV_AXIS_TOKEN) {
+        if (d.rotation) {
+          rotate_rows_smem<T, D>(reinterpret_cast<T*>(sx), p.had_div, p.had_inv, threadIdx.x >> 5);
+          __syncthreads();
+        }
+        if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, sx, gslice, j0, threadIdx.x);
+        else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, sx, gslice, j0, threadIdx.x);
+        else quant_tile_tokens_sb<T, D, 8>(d, sx, gslice, j0, threadIdx.x);
+      } else {
+        quant_tile_channels<T, D>(d, sx, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
+      }
+    }
+    // this buffer's generic-proxy reads / writes precede the next bulk copies into it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    cur = nxt;
+    role = nrole;
+    buf ^= 1;
   }
 }
 
@@ -686,19 +745,24 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 int device_sm_count();
 
 // Per tensor (keys, values): one launch per grouping axis its tiers use; the
-// first of them also copies the tensor's retained rows.
+// first of them also copies the tensor's retained rows.  Persistent grid: as
+// many blocks as fit on the device at once, at most one per tile.
 template <typename T, int D>
 static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
-  const size_t sm = QGeom<T, D>::kSmem;
+  const size_t sm = 2 * QGeom<T, D>::kSmem + 2 * sizeof(uint64_t);
   const int64_t tiles = (int64_t)p.S * p.tiles_slice;
   if (tiles == 0) return cudaSuccess;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(quantize_tile_kernel<T, D, GKV_AXIS_TOKEN>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess)
-    return e;
-  if ((e = cudaFuncSetAttribute(quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess)
-    return e;
+  auto ktok = quantize_tile_kernel<T, D, GKV_AXIS_TOKEN>;
+  auto kch = quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>;
+  if ((e = cudaFuncSetAttribute(ktok, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(kch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess) return e;
+  int occ_tok = 0, occ_ch = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_tok, ktok, kQThreads, sm)) != cudaSuccess) return e;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_ch, kch, kQThreads, sm)) != cudaSuccess) return e;
+  const int sms = device_sm_count();
+  const unsigned g_tok = (unsigned)std::min<int64_t>(tiles, (int64_t)sms * std::max(occ_tok, 1));
+  const unsigned g_ch = (unsigned)std::min<int64_t>(tiles, (int64_t)sms * std::max(occ_ch, 1));
   for (int tensor = 0; tensor < 2; ++tensor) {
     bool token = false, channel = false;
     for (int tier = 1; tier <= 2; ++tier) {
@@ -707,9 +771,8 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
       (d.axis == GKV_AXIS_TOKEN ? token : channel) = true;
     }
     if (!token && !channel) channel = true;  // retained rows only
-    if (token) quantize_tile_kernel<T, D, GKV_AXIS_TOKEN><<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, 1);
-    if (channel)
-      quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL><<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, token ? 0 : 1);
+    if (token) ktok<<<g_tok, kQThreads, sm, st>>>(p, tensor, 1, (int)tiles);
+    if (channel) kch<<<g_ch, kQThreads, sm, st>>>(p, tensor, token ? 0 : 1, (int)tiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -63,3 +63,24 @@ def test_no_cpu_fallback():
     cfg = get_profile("graphkv-int4-balanced").config
     with pytest.raises(RuntimeError, match="CUDA device"):
         g.quantize_kv_layer(torch.randn(1, 1, 256, 64), torch.randn(1, 1, 256, 64), cfg)
+
+
+def _fastdiv(d):
+    """Host constants of the tile kernels' invariant-divisor division (Granlund and
+    Montgomery, PLDI 1994, figure 4.1), restated: m = floor(2^32 (2^l - d) / d) + 1."""
+    l = (d - 1).bit_length()
+    return ((1 << 32) * ((1 << l) - d)) // d + 1, (1 if l > 0 else 0), (l - 1 if l > 0 else 0)
+
+
+def test_invariant_divisor_division_is_exact():
+    import random
+    rng = random.Random(5)
+    divisors = [1, 2, 3, 5, 7, 64, 112, 253, 1000, 4096, 65535, 2 ** 31 - 1, 2 ** 31]
+    divisors += [rng.randrange(1, 2 ** 31) for _ in range(200)]
+    for d in divisors:
+        m, s1, s2 = _fastdiv(d)
+        assert 0 <= m < 2 ** 32
+        nums = [0, 1, d - 1, d, d + 1, 2 ** 32 - 1, 2 ** 32 - 2, 2 ** 31] + [rng.randrange(2 ** 32) for _ in range(300)]
+        for n in nums:
+            t = (m * n) >> 32
+            assert (t + ((n - t) >> s1)) >> s2 == n // d, (d, n)
