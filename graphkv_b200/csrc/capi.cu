@@ -116,20 +116,15 @@ int resolve_tensor(const gkv_plan& p, int i, int n, TensorDesc& d) {
   return GKV_OK;
 }
 
-// Can tensor d run in the tile kernels with tile height TT?
-// Quantize tiles (64 rows) hold whole token-axis groups of 32 or 64 rows per
-// thread; channel-axis groups are powers of two >= 32 dividing head_dim.  The
-// dequantize tiles work on runs of 32 elements along the grouped axis: groups of
-// 32, 64 or 128 (powers of two dividing the tile height or head_dim).
+// Can tensor d run in the tile kernels (tiles of 64 tier rows)?  Token-axis
+// groups of 32 or 64 rows (a thread holds a column over a whole group);
+// channel-axis groups are powers of two >= 32 dividing head_dim.  Rotated
+// token-axis tensors dequantize on the general path.
 bool tensor_fast(const TensorDesc& d, int esize, int D, int TT, bool quantize) {
   (void)esize;
+  (void)TT;
   if (d.log2gs < 0 || d.gs < 32 || !aligned16(d.codes)) return false;
-  if (d.axis == GKV_AXIS_TOKEN) {
-    if (quantize) return d.gs == 32 || d.gs == 64;
-    if (d.gs > TT || TT % d.gs) return false;
-    if (d.rotation) return false;  // rotated token-axis dequant: general path
-    return true;
-  }
+  if (d.axis == GKV_AXIS_TOKEN) return (d.gs == 32 || d.gs == 64) && (quantize || !d.rotation);
   return D % d.gs == 0;
 }
 
@@ -181,12 +176,7 @@ int resolve_plan(const gkv_plan* pp, int64_t S, bool quantize, const gkv_layer_i
   bool want[3] = {false, false, false};
   for (int tier = 1; tier <= 2; ++tier) {
     if (!geom_ok || r.n[tier] == 0) continue;
-    int need = 64;
-    for (int i = 0; i < 4 && !quantize; ++i)  // quantize tiles are always 64 rows
-      if (kTierOf[i] == tier && r.t[i].axis == GKV_AXIS_TOKEN) need = need > r.t[i].gs ? need : r.t[i].gs;
-    if (need > 128 || !tile_instantiated(esize, D, need)) continue;
     want[tier] = true;
-    tt = tt > need ? tt : need;
   }
   r.tt = tt;
   for (int tier = 1; tier <= 2; ++tier) {
@@ -400,6 +390,9 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
   q.tiles[0] = r.fast[0] ? (int)ceil_div(r.n[0], kRetTile) : 0;
   for (int k = 1; k <= 2; ++k) q.tiles[k] = r.fast[k] ? (int)ceil_div(r.n[k], r.tt) : 0;
   q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
+  q.tile_div = make_fastdiv((uint32_t)(q.tiles_slice > 0 ? q.tiles_slice : 1));
+  q.had_fused = (p.head_dim == 64 || p.head_dim == 128) &&
+                p.hadamard_divisor == (float)std::sqrt((double)p.head_dim);
   cudaError_t e;
   if (q.tiles_slice > 0 && (e = launch_dequantize_tiles(q, p.dtype, s)) != cudaSuccess)
     return cuda_fail(e, "dequantize tile kernel");

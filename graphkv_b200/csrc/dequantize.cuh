@@ -12,6 +12,8 @@
 // (warp per row); both leave through warp-per-row stores of whole output rows.
 #pragma once
 
+#include <algorithm>
+
 #include "gkv_params.cuh"
 
 namespace gkv {
@@ -58,301 +60,428 @@ __device__ __forceinline__ int load_zp(const TensorDesc& d, int64_t gi) {
   return d.quantizer == GKV_AFFINE ? (int)d.zps[gi] : 0;
 }
 
-// Output of one decoded row (lane holds D/32 consecutive channels): optional
-// inverse rotation across the warp, cast to T, one vector store per lane.
-// Cross-lane butterfly stages compute o + sign * v with one fused multiply-add:
-// sign = +1 gives v + o, sign = -1 gives o - v, each rounded once as the
-// reference's add / subtract.
-template <typename T, int D, bool ROT>
-__device__ __forceinline__ void emit_row(float (&v)[D / 32], float div, float inv, T* dst) {
-  constexpr int EPL = D / 32;
-  const int lane = threadIdx.x & 31;
-  if constexpr (ROT) fwht_warp<EPL>(v);
-  constexpr int NB = EPL * (int)sizeof(T);
-  constexpr int NW = NB / 4;
-  uint32_t w[NW];
-  if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) w[i] = __float_as_uint(ROT ? __fdiv_rn(v[i], div) : v[i]);
+// ---------------------------------------------------------------------------
+// Fast path: persistent blocks of 64 threads over tiles of 64 tier rows of one
+// tensor, one kernel per grouping axis.  Every thread stages the packed codes of
+// its items of the block's NEXT tile with asynchronous copies, and their scales,
+// zero points and output rows, while it decodes the current tile -- the loads of
+// a tile are in flight during the previous tile's work.  Staged codes are
+// interleaved by 16-byte chunks across the block's threads (chunk q of thread t
+// at (q * 64 + t) * 16), so a warp's 16-byte reads are conflict-free.
+//  - channel-axis groups (V): item = (row, run of 128 bytes of output), lanes
+//    mapped as in the quantizer (runs of a row 8 lanes apart); decoded, optionally
+//    rotated in registers, and stored as 16-byte vectors at the output row;
+//  - token-axis groups (K): item = (column word, group); decoded column-wise into
+//    a shared [64][D] tile, whose rows then leave as 16-byte vectors.
+// ---------------------------------------------------------------------------
+constexpr int kDThreads = 64;
+constexpr int kDTile = 64;
+constexpr int kDItems = 4;       // items (channel axis) or item channels (token axis) per thread, at most
+constexpr int kDSlot = 128;      // staged code bytes per thread and tile, at most (int8 codes)
+
+template <typename T, int D>
+struct DGeom {
+  static constexpr int kRowBytes = D * (int)sizeof(T);
+  static constexpr int kPitchB = kRowBytes + 16;
+  static constexpr int kPitchW = kPitchB / 4;
+  static constexpr int kRun = 128 / (int)sizeof(T);
+  static constexpr size_t kStage = (size_t)kDThreads * kDSlot;  // codes of one tile
+  static constexpr size_t kMeta = (size_t)kDThreads * (2 * kDItems + 1) * 4;  // scales, zero points, output rows
+  static constexpr size_t kBuf = kStage + kMeta;
+  static constexpr size_t kTile = (size_t)kDTile * kPitchB;      // token-axis output tile
+};
+
+// Staging buffer of one tile: codes, then per-thread scales / zero points and
+// the output row of tile row t.
+struct DStage {
+  uint8_t* codes;
+  float* scale;  // [kDItems][64]
+  int* zp;       // [kDItems][64]
+  int* tok;      // [64]
+  __device__ __forceinline__ static DStage at(uint8_t* base, size_t stage_bytes) {
+    DStage s;
+    s.codes = base;
+    s.scale = reinterpret_cast<float*>(base + stage_bytes);
+    s.zp = reinterpret_cast<int*>(base + stage_bytes + kDItems * kDThreads * 4);
+    s.tok = reinterpret_cast<int*>(base + stage_bytes + 2 * kDItems * kDThreads * 4);
+    return s;
+  }
+  // byte b of this thread's code slot
+  __device__ __forceinline__ uint8_t* code_at(int b) const {
+    return codes + ((b >> 4) * kDThreads + (int)threadIdx.x) * 16 + (b & 15);
+  }
+};
+
+template <int NB>
+__device__ __forceinline__ void copy_codes(const DStage& st, int b0, const uint8_t* src) {
+  if constexpr (NB == 8) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(st.code_at(b0))), "l"(src) : "memory");
   } else {
 #pragma unroll
-    for (int i = 0; i < EPL; i += 2) {
-      uint32_t lo, hi;
-      if constexpr (ROT) {
-        lo = tbits(hadamard_scale<T>(v[i], div, inv));
-        hi = tbits(hadamard_scale<T>(v[i + 1], div, inv));
-        w[i / 2] = lo | (hi << 16);
-      } else if constexpr (Elem<T>::kTag == GKV_BF16) {
-        const __nv_bfloat162 p = __floats2bfloat162_rn(v[i], v[i + 1]);
-        w[i / 2] = *reinterpret_cast<const uint32_t*>(&p);
-      } else {
-        const __half2 p = __floats2half2_rn(v[i], v[i + 1]);
-        w[i / 2] = *reinterpret_cast<const uint32_t*>(&p);
-      }
+    for (int i = 0; i < NB / 16; ++i) cp_async16(st.code_at(b0 + 16 * i), src + 16 * i, 16u);
+  }
+}
+
+// NB (8 .. 64) staged bytes from byte b0 of this thread's slot, as words
+template <int NB>
+__device__ __forceinline__ void read_codes(const DStage& st, int b0, uint32_t (&w)[NB / 4]) {
+  if constexpr (NB == 8) {
+    const uint2 t = *reinterpret_cast<const uint2*>(st.code_at(b0));
+    w[0] = t.x; w[1] = t.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < NB / 16; ++i) {
+      const uint4 t = *reinterpret_cast<const uint4*>(st.code_at(b0 + 16 * i));
+      w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
     }
   }
-  store_bytes<NB>(reinterpret_cast<uint8_t*>(dst + lane * EPL), w);
 }
 
-
-// 32 codes of a run (SB bits each) as fp32 bit patterns 2^23 + code
-template <int SB>
-__device__ __forceinline__ void run_codes(const uint32_t (&w)[SB], uint32_t (&c)[kRun]) {
-#pragma unroll
-  for (int q = 0; q < SB; ++q) {
-    uint32_t t[32 / SB];
-    word_codes<SB>(w[q], t);
-#pragma unroll
-    for (int i = 0; i < 32 / SB; ++i) c[q * (32 / SB) + i] = t[i];
-  }
+__device__ __forceinline__ uint64_t decode_pair(uint32_t c0, uint32_t c1, uint32_t x0, uint32_t x1, uint64_t base2,
+                                                uint64_t sc2) {
+  return mul2(sub2(pk2(__uint_as_float(c0 ^ x0), __uint_as_float(c1 ^ x1)), base2), sc2);
 }
 
-template <int SB>
-__device__ __forceinline__ void load_run(const uint8_t* p, uint32_t (&w)[SB]) {
-  if constexpr (SB == 2) {
-    const uint2 t = *reinterpret_cast<const uint2*>(p);
-    w[0] = t.x; w[1] = t.y;
-  } else if constexpr (SB == 4) {
-    const uint4 t = *reinterpret_cast<const uint4*>(p);
-    w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
-  } else {
-    const uint4 t0 = reinterpret_cast<const uint4*>(p)[0], t1 = reinterpret_cast<const uint4*>(p)[1];
-    w[0] = t0.x; w[1] = t0.y; w[2] = t0.z; w[3] = t0.w; w[4] = t1.x; w[5] = t1.y; w[6] = t1.z; w[7] = t1.w;
-  }
-}
-
-// decoded values of a run: ((2^23 + code) ^ xor) - base, times the scale, in packed pairs
-__device__ __forceinline__ void decode_run(const uint32_t (&c)[kRun], const Decoder& dc, float (&v)[kRun]) {
-  const uint64_t base2 = pk2(dc.base, dc.base), sc2 = pk2(dc.scale, dc.scale);
-#pragma unroll
-  for (int i = 0; i < kRun; i += 2) {
-    const uint64_t q = sub2(pk2(__uint_as_float(c[i] ^ dc.xor_mask), __uint_as_float(c[i + 1] ^ dc.xor_mask)), base2);
-    const uint64_t r = mul2(q, sc2);
-    v[i] = lo2(r);
-    v[i + 1] = hi2(r);
-  }
-}
-
-// pack two fp32 values into one 32-bit word of T (round to nearest even)
 template <typename T>
-__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
-  if constexpr (Elem<T>::kTag == GKV_BF16) {
-    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&p);
-  } else {
-    const __half2 p = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&p);
-  }
+__device__ __forceinline__ uint32_t out_word(uint64_t v2) {
+  return Word16<T>::round2(lo2(v2), hi2(v2));
 }
 
-// Channel-axis tensor (values by default): item = (tier row, run of 32 channels),
-// the runs of a row in adjacent lanes (the Hadamard rotation crosses them with
-// shuffles).  Codes, scale and zero point are loaded once per run, decoded in
-// registers and stored with 16-byte vector stores at the row's output position.
-template <typename T, int D, int TT, int SB, bool ROT>
-__device__ void dequant_channel_half(const DequantParams& p, const TensorDesc& d, T* out, const int* tok, int s,
-                                     int j0, int rows) {
-  constexpr int RPR = D / kRun;
-  constexpr int ITEMS = TT * RPR;
-  constexpr int ITER = (ITEMS + 127) / 128;
-  const int ht = threadIdx.x & 127;
-  const int lane = threadIdx.x & 31;
-#pragma unroll 1
-  for (int itn = 0; itn < ITER; ++itn) {
-    const int item = ht + itn * 128;
-    const int r = item / RPR, run = item % RPR;
-    const bool act = item < ITEMS && r < rows;
-    uint32_t w[SB];
+struct DTileRef {
+  int s, tier, k;
+};
+__device__ __forceinline__ DTileRef dtile_ref(const DequantParams& p, int t) {
+  DTileRef r;
+  r.s = (int)p.tile_div.div((uint32_t)t);
+  int k = t - r.s * p.tiles_slice;
+  r.tier = 0;
+  if (k >= p.tiles[0]) {
+    k -= p.tiles[0];
+    r.tier = 1;
+    if (k >= p.tiles[1]) { k -= p.tiles[1]; r.tier = 2; }
+  }
+  r.k = k;
+  return r;
+}
+
+template <int AXIS>
+__device__ __forceinline__ int dtile_role(const DequantParams& p, const DTileRef& tr, int tensor, int copy_retained) {
+  if (tr.tier == 0) return copy_retained ? 1 : 0;
+  return p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor].axis == AXIS ? 2 : 0;
+}
+
+// ---- channel axis ---------------------------------------------------------
+template <int D, int RUN>
+struct ChanMap {
+  static constexpr int RPR = D / RUN;
+  static constexpr int ROWS_STEP = 32 / RPR;
+  static constexpr int ITEMS = (kDTile / ROWS_STEP) / 2;  // items per thread (two warps)
+  __device__ __forceinline__ static void item(int i, int& r, int& u) {
+    const int lane = threadIdx.x & 31, hw = threadIdx.x >> 5;
+    const int j = lane & 7, k = lane >> 3;
+    u = k % RPR;
+    r = (hw + 2 * i) * ROWS_STEP + (k / RPR) * 8 + j;
+  }
+};
+
+template <int D, int RUN, int SB>
+__device__ __forceinline__ void chan_issue(const TensorDesc& d, int s, int j0, int rows, const DStage& st) {
+  using M = ChanMap<D, RUN>;
+  constexpr int NB = RUN * SB / 8;
 #pragma unroll
-    for (int q = 0; q < SB; ++q) w[q] = 0;
-    float scale = 0.f;
+  for (int i = 0; i < M::ITEMS; ++i) {
+    int r, u;
+    M::item(i, r, u);
+    float sc = 0.f;
     int zp = 0;
-    if (act) {
+    if (r < rows) {
       const int64_t row = (int64_t)s * d.n + j0 + r;
-      load_run<SB>(d.codes + ((row * d.n_pad + run * kRun) * SB) / 8, w);
-      const int64_t gi = row * d.groups_row + ((run * kRun) >> d.log2gs);
-      scale = load_scale(d.scales, gi, d.scale_dtype);
+      copy_codes<NB>(st, i * NB, d.codes + ((row * d.n_pad + u * RUN) * SB) / 8);
+      const int64_t gi = row * d.groups_row + ((u * RUN) >> d.log2gs);
+      sc = load_scale(d.scales, gi, d.scale_dtype);
       zp = load_zp(d, gi);
     }
-    uint32_t c[kRun];
-    run_codes<SB>(w, c);
-    float v[kRun];
-    decode_run(c, make_decoder(d, scale, zp), v);
-    if constexpr (ROT) {
-      // in-thread stages h = 1 .. 16, then across the RPR lanes of the row
+    st.scale[i * kDThreads + threadIdx.x] = sc;
+    st.zp[i * kDThreads + threadIdx.x] = zp;
+  }
+}
+
+template <typename T, int D, int RUN, int SB, bool ROT>
+__device__ void chan_decode(const DequantParams& p, const TensorDesc& d, const DStage& st, int rows, T* out) {
+  using M = ChanMap<D, RUN>;
+  constexpr int NB = RUN * SB / 8;
+  constexpr int NC = NB / 4;
+  constexpr int EPC = 32 / SB;
+#pragma unroll 1
+  for (int i = 0; i < M::ITEMS; ++i) {
+    int r, u;
+    M::item(i, r, u);
+    const bool act = r < rows;
+    uint32_t cw[NC];
+    read_codes<NB>(st, i * NB, cw);
+    const Decoder dc = make_decoder(d, st.scale[i * kDThreads + threadIdx.x], st.zp[i * kDThreads + threadIdx.x]);
+    const uint64_t base2 = pk2(dc.base, dc.base), sc2 = pk2(dc.scale, dc.scale);
+    const uint32_t xm = SB == 8 ? dc.xor_mask : 0u;  // only unpacked symmetric codes flip
+    uint64_t v[RUN / 2];
 #pragma unroll
-      for (int h = 1; h < kRun; h <<= 1) {
+    for (int q = 0; q < NC; ++q) {
+      uint32_t c[EPC];
+      word_codes<SB>(cw[q], c);
 #pragma unroll
-        for (int i = 0; i < kRun; i += 2 * h) {
-#pragma unroll
-          for (int j = 0; j < h; ++j) {
-            const float a = v[i + j], bb = v[i + j + h];
-            v[i + j] = __fadd_rn(a, bb);
-            v[i + j + h] = __fsub_rn(a, bb);
-          }
-        }
-      }
-#pragma unroll
-      for (int m = 1; m < RPR; m <<= 1) {
-        const float sg = (lane & m) ? -1.f : 1.f;
-        const uint64_t sg2 = pk2(sg, sg);
-#pragma unroll
-        for (int i = 0; i < kRun; i += 2) {
-          const float o0 = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
-          const float o1 = __shfl_xor_sync(0xFFFFFFFFu, v[i + 1], m);
-          const uint64_t rr = fma2(sg2, pk2(v[i], v[i + 1]), pk2(o0, o1));
-          v[i] = lo2(rr);
-          v[i + 1] = hi2(rr);
-        }
-      }
+      for (int e = 0; e < EPC; e += 2) v[(q * EPC + e) / 2] = decode_pair(c[e], c[e + 1], xm, xm, base2, sc2);
     }
-    if (act && tok[r] >= 0) {
-      T* dst = out + (int64_t)tok[r] * D + run * kRun;
+    if constexpr (ROT) {
+      // Decoded values are integer multiples of a stored scale (>= 2^-24 when
+      // nonzero), so every nonzero butterfly output is far above the fused
+      // quotient's 2^-100 bound.  -0 needs a zero scale (a group that underflowed
+      // its scale dtype) and infinities an overflowed one: then the warp divides
+      // exactly.
+      const bool fused = (p.had_fused != 0) && __all_sync(kFull, dc.scale != 0.f && isfinite(dc.scale));
+      rotate_run<RUN, M::RPR, false>(v, u, p.had_div, p.had_inv, fused);
+    }
+    const int tok = act ? st.tok[r] : -1;
+    if (tok >= 0) {
+      uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)tok * D + u * RUN);
       if constexpr (sizeof(T) == 4) {
 #pragma unroll
-        for (int q = 0; q < kRun / 4; ++q) {
-          float o[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) o[u] = ROT ? __fdiv_rn(v[4 * q + u], p.had_div) : v[4 * q + u];
-          reinterpret_cast<uint4*>(dst)[q] =
-              make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
-        }
+        for (int k = 0; k < RUN / 2; k += 2)
+          dst[k / 2] = make_uint4((uint32_t)v[k], (uint32_t)(v[k] >> 32), (uint32_t)v[k + 1], (uint32_t)(v[k + 1] >> 32));
       } else {
 #pragma unroll
-        for (int q = 0; q < kRun / 8; ++q) {
-          uint32_t o[4];
+        for (int k = 0; k < RUN / 2; k += 4)
+          dst[k / 4] = make_uint4(out_word<T>(v[k]), out_word<T>(v[k + 1]), out_word<T>(v[k + 2]), out_word<T>(v[k + 3]));
+      }
+    }
+  }
+}
+
+// ---- token axis -----------------------------------------------------------
+template <typename T, int D, int GS>
+struct TokMap {
+  static constexpr int W = D * (int)sizeof(T) / 4;       // column words
+  static constexpr int CPW = 4 / (int)sizeof(T);         // channels per word
+  static constexpr int ITEMS_TILE = W * (kDTile / GS);
+  static constexpr int ITEMS = (ITEMS_TILE + kDThreads - 1) / kDThreads;
+};
+
+template <typename T, int D, int GS, int SB>
+__device__ __forceinline__ void tok_issue(const TensorDesc& d, int s, int j0, const DStage& st) {
+  using M = TokMap<T, D, GS>;
+  constexpr int NB = GS * SB / 8;  // code bytes per channel and group
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float a = v[8 * q + 2 * u], bb = v[8 * q + 2 * u + 1];
-            if constexpr (ROT)
-              o[u] = tbits(hadamard_scale<T>(a, p.had_div, p.had_inv)) |
-                     (tbits(hadamard_scale<T>(bb, p.had_div, p.had_inv)) << 16);
-            else
-              o[u] = pack_pair<T>(a, bb);
-          }
-          reinterpret_cast<uint4*>(dst)[q] = make_uint4(o[0], o[1], o[2], o[3]);
+  for (int i = 0; i < M::ITEMS; ++i) {
+    const int item = threadIdx.x + i * kDThreads;
+    const int g = item / M::W, w = item - g * M::W;
+    const int tok0 = j0 + g * GS;
+#pragma unroll
+    for (int c = 0; c < M::CPW; ++c) {
+      float sc = 0.f;
+      int zp = 0;
+      if (item < M::ITEMS_TILE && tok0 < d.n_pad) {
+        const int64_t crow = (int64_t)s * D + w * M::CPW + c;
+        copy_codes<NB>(st, (i * M::CPW + c) * NB, d.codes + ((crow * d.n_pad + tok0) * SB) / 8);
+        const int64_t gi = crow * d.groups_row + (tok0 >> d.log2gs);
+        sc = load_scale(d.scales, gi, d.scale_dtype);
+        zp = load_zp(d, gi);
+      }
+      st.scale[(i * M::CPW + c) * kDThreads + threadIdx.x] = sc;
+      st.zp[(i * M::CPW + c) * kDThreads + threadIdx.x] = zp;
+    }
+  }
+}
+
+template <typename T, int D, int GS, int SB>
+__device__ void tok_decode(const TensorDesc& d, const DStage& st, int j0, uint8_t* tile) {
+  using M = TokMap<T, D, GS>;
+  using G = DGeom<T, D>;
+  constexpr int NB = GS * SB / 8;
+  constexpr int NC = NB / 4;
+  constexpr int EPC = 32 / SB;
+#pragma unroll 1
+  for (int i = 0; i < M::ITEMS; ++i) {
+    const int item = threadIdx.x + i * kDThreads;
+    if (item >= M::ITEMS_TILE) break;
+    const int g = item / M::W, w = item - g * M::W;
+    if (j0 + g * GS >= d.n_pad) continue;
+    uint32_t* col = reinterpret_cast<uint32_t*>(tile + (g * GS) * G::kPitchB) + w;
+    if constexpr (M::CPW == 2) {
+      const int k0 = (2 * i) * kDThreads + threadIdx.x, k1 = k0 + kDThreads;
+      const Decoder d0 = make_decoder(d, st.scale[k0], st.zp[k0]);
+      const Decoder d1 = make_decoder(d, st.scale[k1], st.zp[k1]);
+      const uint64_t base2 = pk2(d0.base, d1.base), sc2 = pk2(d0.scale, d1.scale);
+      const uint32_t x0 = SB == 8 ? d0.xor_mask : 0u, x1 = SB == 8 ? d1.xor_mask : 0u;
+      uint32_t c0w[NC], c1w[NC];
+      read_codes<NB>(st, (2 * i) * NB, c0w);
+      read_codes<NB>(st, (2 * i + 1) * NB, c1w);
+#pragma unroll
+      for (int q = 0; q < NC; ++q) {
+        uint32_t a[EPC], b[EPC];
+        word_codes<SB>(c0w[q], a);
+        word_codes<SB>(c1w[q], b);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e)
+          col[(q * EPC + e) * G::kPitchW] = out_word<T>(decode_pair(a[e], b[e], x0, x1, base2, sc2));
+      }
+    } else {
+      const int k0 = i * kDThreads + threadIdx.x;
+      const Decoder d0 = make_decoder(d, st.scale[k0], st.zp[k0]);
+      const uint64_t base2 = pk2(d0.base, d0.base), sc2 = pk2(d0.scale, d0.scale);
+      const uint32_t x0 = SB == 8 ? d0.xor_mask : 0u;
+      uint32_t cw[NC];
+      read_codes<NB>(st, i * NB, cw);
+#pragma unroll
+      for (int q = 0; q < NC; ++q) {
+        uint32_t a[EPC];
+        word_codes<SB>(cw[q], a);
+#pragma unroll
+        for (int e = 0; e < EPC; e += 2) {
+          const uint64_t v2 = decode_pair(a[e], a[e + 1], x0, x0, base2, sc2);
+          col[(q * EPC + e) * G::kPitchW] = (uint32_t)v2;
+          col[(q * EPC + e + 1) * G::kPitchW] = (uint32_t)(v2 >> 32);
         }
       }
     }
   }
 }
 
-// Token-axis tensor (keys by default): item = (32-bit column word, run of 32 rows);
-// the decoded values are written into the half's shared tile [TT][D + pad] of T,
-// then whole rows leave with 16-byte vector stores.  (Rotated token-axis tensors
-// take the general path.)
-template <typename T, int D, int TT, int SB>
-__device__ void dequant_token_half(const DequantParams& p, const TensorDesc& d, T* out, const int* tok, int s, int j0,
-                                   int rows, T* tile, int half) {
-  constexpr int CPW = 4 / (int)sizeof(T);
-  constexpr int W = D / CPW;
-  constexpr int NRUN = TT / kRun;
-  constexpr int ITEMS = W * NRUN;
-  constexpr int ITER = (ITEMS + 127) / 128;
-  constexpr int TP = D + 16 / (int)sizeof(T);  // tile pitch (elements)
-  const int ht = threadIdx.x & 127;
-#pragma unroll 1
-  for (int itn = 0; itn < ITER; ++itn) {
-    const int item = ht + itn * 128;
-    if (item >= ITEMS) break;
-    const int w = item % W, run = item / W;
-    const int tk = j0 + run * kRun;
-    if (tk >= d.n_pad) continue;
-    float v[CPW][kRun];
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      const int64_t crow = (int64_t)s * D + w * CPW + c;
-      uint32_t cw[SB];
-      load_run<SB>(d.codes + ((crow * d.n_pad + tk) * SB) / 8, cw);
-      const int64_t gi = crow * d.groups_row + (tk >> d.log2gs);
-      uint32_t codes[kRun];
-      run_codes<SB>(cw, codes);
-      decode_run(codes, make_decoder(d, load_scale(d.scales, gi, d.scale_dtype), load_zp(d, gi)), v[c]);
-    }
-    uint32_t* col = reinterpret_cast<uint32_t*>(tile + (run * kRun) * TP) + w;
-#pragma unroll
-    for (int i = 0; i < kRun; ++i) {
-      if constexpr (CPW == 2) col[i * (TP / 2)] = pack_pair<T>(v[0][i], v[1][i]);
-      else col[i * TP] = __float_as_uint(v[0][i]);
-    }
-  }
-  bar_half(half);
-  constexpr int CPR = D * (int)sizeof(T) / 16;  // 16-byte chunks per row
-  for (int e = ht; e < rows * CPR; e += 128) {
-    const int r = e / CPR, c = e - r * CPR;
-    if (tok[r] < 0) continue;
-    reinterpret_cast<uint4*>(out + (int64_t)tok[r] * D)[c] = reinterpret_cast<const uint4*>(tile + r * TP)[c];
-  }
-}
-
-template <typename T, int D, int TT, bool ROT>
-__device__ __forceinline__ void dequant_half_rot(const DequantParams& p, const TensorDesc& d, T* out, const int* tok,
-                                                 int s, int j0, int rows, T* tile, int half) {
-  if (d.axis == GKV_AXIS_TOKEN) {
-    if constexpr (!ROT) {
-      if (d.sbits == 4) dequant_token_half<T, D, TT, 4>(p, d, out, tok, s, j0, rows, tile, half);
-      else if (d.sbits == 2) dequant_token_half<T, D, TT, 2>(p, d, out, tok, s, j0, rows, tile, half);
-      else dequant_token_half<T, D, TT, 8>(p, d, out, tok, s, j0, rows, tile, half);
+// ---- dispatch -------------------------------------------------------------
+template <typename T, int D, int AXIS>
+__device__ __forceinline__ void dq_issue(const TensorDesc& d, int s, int j0, int rows, const DStage& st) {
+  if constexpr (AXIS == GKV_AXIS_TOKEN) {
+    (void)rows;
+    if (d.gs == 64) {
+      if (d.sbits == 4) tok_issue<T, D, 64, 4>(d, s, j0, st);
+      else if (d.sbits == 2) tok_issue<T, D, 64, 2>(d, s, j0, st);
+      else tok_issue<T, D, 64, 8>(d, s, j0, st);
+    } else {
+      if (d.sbits == 4) tok_issue<T, D, 32, 4>(d, s, j0, st);
+      else if (d.sbits == 2) tok_issue<T, D, 32, 2>(d, s, j0, st);
+      else tok_issue<T, D, 32, 8>(d, s, j0, st);
     }
   } else {
-    if (d.sbits == 4) dequant_channel_half<T, D, TT, 4, ROT>(p, d, out, tok, s, j0, rows);
-    else if (d.sbits == 2) dequant_channel_half<T, D, TT, 2, ROT>(p, d, out, tok, s, j0, rows);
-    else dequant_channel_half<T, D, TT, 8, ROT>(p, d, out, tok, s, j0, rows);
+    constexpr int RUN = DGeom<T, D>::kRun;
+    if (d.gs < RUN) {
+      if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) {
+        if (d.sbits == 4) chan_issue<D, RUN / 2, 4>(d, s, j0, rows, st);
+        else if (d.sbits == 2) chan_issue<D, RUN / 2, 2>(d, s, j0, rows, st);
+        else chan_issue<D, RUN / 2, 8>(d, s, j0, rows, st);
+      }
+    } else {
+      if (d.sbits == 4) chan_issue<D, RUN, 4>(d, s, j0, rows, st);
+      else if (d.sbits == 2) chan_issue<D, RUN, 2>(d, s, j0, rows, st);
+      else chan_issue<D, RUN, 8>(d, s, j0, rows, st);
+    }
   }
 }
 
-template <typename T, int D, int TT>
-constexpr size_t dequant_tile_smem() {
-  return 2 * (size_t)TT * (D + 16 / sizeof(T)) * sizeof(T) + (size_t)TT * sizeof(int);
+template <typename T, int D, int RUN>
+__device__ __forceinline__ void chan_decode_any(const DequantParams& p, const TensorDesc& d, const DStage& st, int rows,
+                                                T* out) {
+  if (d.rotation) {
+    if (d.sbits == 4) chan_decode<T, D, RUN, 4, true>(p, d, st, rows, out);
+    else if (d.sbits == 2) chan_decode<T, D, RUN, 2, true>(p, d, st, rows, out);
+    else chan_decode<T, D, RUN, 8, true>(p, d, st, rows, out);
+  } else {
+    if (d.sbits == 4) chan_decode<T, D, RUN, 4, false>(p, d, st, rows, out);
+    else if (d.sbits == 2) chan_decode<T, D, RUN, 2, false>(p, d, st, rows, out);
+    else chan_decode<T, D, RUN, 8, false>(p, d, st, rows, out);
+  }
 }
 
-// One block per tile: retained tiles scatter their rows; standard / cold tiles load
-// the tile's output positions once, then warps 0-3 decode K and warps 4-7 decode V.
-template <typename T, int D, int TT>
-__global__ void __launch_bounds__(kThreads, 3) dequantize_tile_kernel(const __grid_constant__ DequantParams p) {
+// Persistent blocks over the tiles of one tensor (`tensor` 1: values, 0: keys),
+// compiled per grouping axis; retained-row tiles are copied when `copy_retained`.
+template <typename T, int D, int AXIS>
+__global__ void __launch_bounds__(kDThreads, 8) dequantize_tile_kernel(const __grid_constant__ DequantParams p,
+                                                                       int tensor, int copy_retained,
+                                                                       int total_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int s = blockIdx.x / p.tiles_slice;
-  int k = blockIdx.x - s * p.tiles_slice;
-  T* ok = reinterpret_cast<T*>(p.out_k) + (int64_t)s * p.T * D;
-  T* ov = reinterpret_cast<T*>(p.out_v) + (int64_t)s * p.T * D;
-  if (k < p.tiles[0]) {
-    constexpr int VEC = 16 / (int)sizeof(T), CPR = D / VEC;
-    const int R = p.n_tier[0];
-    const int j0 = k * kRetTile, rows = min(kRetTile, R - j0);
-    const T* rk = reinterpret_cast<const T*>(p.ret_k) + ((int64_t)s * R + j0) * D;
-    const T* rv = reinterpret_cast<const T*>(p.ret_v) + ((int64_t)s * R + j0) * D;
-    for (int e = threadIdx.x; e < rows * CPR; e += kThreads) {
-      const int r = e / CPR, c = e - r * CPR;
-      const int tok = p.idx[0][j0 + r];
-      if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); continue; }
-      *reinterpret_cast<uint4*>(ok + (int64_t)tok * D + c * VEC) = *reinterpret_cast<const uint4*>(rk + r * D + c * VEC);
-      *reinterpret_cast<uint4*>(ov + (int64_t)tok * D + c * VEC) = *reinterpret_cast<const uint4*>(rv + r * D + c * VEC);
+  using G = DGeom<T, D>;
+  uint8_t* tile = smem + 2 * G::kBuf;  // token axis: [64][pitch]
+  T* const out_base = reinterpret_cast<T*>(tensor ? p.out_v : p.out_k);
+  int cur = blockIdx.x, role = 0;
+  for (; cur < total_tiles; cur += gridDim.x)
+    if ((role = dtile_role<AXIS>(p, dtile_ref(p, cur), tensor, copy_retained)) != 0) break;
+  int buf = 0;
+  auto issue = [&](int t, int b) {
+    const DTileRef tr = dtile_ref(p, t);
+    const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+    const int j0 = tr.k * kDTile;
+    const int rows = min(kDTile, p.n_tier[tr.tier] - j0);
+    const DStage st = DStage::at(smem + b * G::kBuf, G::kStage);
+    dq_issue<T, D, AXIS>(d, tr.s, j0, rows, st);
+    int t_out = -1;
+    if ((int)threadIdx.x < rows) {
+      t_out = p.idx[tr.tier][j0 + threadIdx.x];
+      if ((unsigned)t_out >= (unsigned)p.T) { raise_error(kErrBadIndex); t_out = -1; }
     }
-    return;
-  }
-  k -= p.tiles[0];
-  int tier = 1;
-  if (k >= p.tiles[1]) { k -= p.tiles[1]; tier = 2; }
-  const int* idx = p.idx[tier];
-  const int j0 = k * TT;
-  const int rows = min(TT, p.n_tier[tier] - j0);
-  constexpr int TP = D + 16 / (int)sizeof(T);
-  T* tiles = reinterpret_cast<T*>(smem);
-  int* tok = reinterpret_cast<int*>(smem + 2 * (size_t)TT * TP * sizeof(T));
-  for (int r = threadIdx.x; r < TT; r += kThreads) {
-    int t = -1;
-    if (r < rows) {
-      t = idx[j0 + r];
-      if ((unsigned)t >= (unsigned)p.T) { raise_error(kErrBadIndex); t = -1; }
+    st.tok[threadIdx.x] = t_out;
+  };
+  if (cur < total_tiles && role == 2) issue(cur, 0);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  while (cur < total_tiles) {
+    int nxt = cur + gridDim.x, nrole = 0;
+    for (; nxt < total_tiles; nxt += gridDim.x)
+      if ((nrole = dtile_role<AXIS>(p, dtile_ref(p, nxt), tensor, copy_retained)) != 0) break;
+    if (nxt < total_tiles && nrole == 2) issue(nxt, buf ^ 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const DTileRef tr = dtile_ref(p, cur);
+    T* out = out_base + (int64_t)tr.s * p.T * D;
+    if (role == 1) {
+      constexpr int VEC = 16 / (int)sizeof(T), CPR = D / VEC;
+      const int R = p.n_tier[0];
+      const int j0 = tr.k * kRetTile, rows = min(kRetTile, R - j0);
+      const T* src = reinterpret_cast<const T*>(tensor ? p.ret_v : p.ret_k) + ((int64_t)tr.s * R + j0) * D;
+      for (int e = threadIdx.x; e < rows * CPR; e += kDThreads) {
+        const int r = e / CPR, c = e - r * CPR;
+        const int t_out = p.idx[0][j0 + r];
+        if ((unsigned)t_out >= (unsigned)p.T) { raise_error(kErrBadIndex); continue; }
+        *reinterpret_cast<uint4*>(out + (int64_t)t_out * D + c * VEC) =
+            *reinterpret_cast<const uint4*>(src + r * D + c * VEC);
+      }
+    } else {
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+      __syncthreads();  // every thread's staged rows / metadata of this tile are visible
+      const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+      const int j0 = tr.k * kDTile;
+      const int rows = min(kDTile, p.n_tier[tr.tier] - j0);
+      const DStage st = DStage::at(smem + buf * G::kBuf, G::kStage);
+      if constexpr (AXIS == GKV_AXIS_TOKEN) {
+        if (d.gs == 64) {
+          if (d.sbits == 4) tok_decode<T, D, 64, 4>(d, st, j0, tile);
+          else if (d.sbits == 2) tok_decode<T, D, 64, 2>(d, st, j0, tile);
+          else tok_decode<T, D, 64, 8>(d, st, j0, tile);
+        } else {
+          if (d.sbits == 4) tok_decode<T, D, 32, 4>(d, st, j0, tile);
+          else if (d.sbits == 2) tok_decode<T, D, 32, 2>(d, st, j0, tile);
+          else tok_decode<T, D, 32, 8>(d, st, j0, tile);
+        }
+        // the tile's rows leave as 16-byte vectors: thread = (chunk, rows r0, r0 + step, ...)
+        __syncthreads();
+        constexpr int CH = G::kRowBytes / 16, STEP = kDThreads / CH;
+        const int c = threadIdx.x % CH, r0 = threadIdx.x / CH;
+#pragma unroll 4
+        for (int i = 0; i < kDTile / STEP; ++i) {
+          const int r = r0 + i * STEP;
+          const int t_out = r < rows ? st.tok[r] : -1;
+          if (t_out >= 0)
+            reinterpret_cast<uint4*>(out + (int64_t)t_out * D)[c] =
+                *reinterpret_cast<const uint4*>(tile + r * G::kPitchB + c * 16);
+        }
+      } else {
+        constexpr int RUN = G::kRun;
+        if (d.gs < RUN) {
+          if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) chan_decode_any<T, D, RUN / 2>(p, d, st, rows, out);
+        } else {
+          chan_decode_any<T, D, RUN>(p, d, st, rows, out);
+        }
+      }
     }
-    tok[r] = t;
+    __syncthreads();  // this buffer and the tile are rewritten from the next iteration on
+    cur = nxt;
+    role = nrole;
+    buf ^= 1;
   }
-  __syncthreads();
-  const int half = threadIdx.x >> 7;
-  const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + half];
-  T* out = half ? ov : ok;
-  if (d.rotation) dequant_half_rot<T, D, TT, true>(p, d, out, tok, s, j0, rows, tiles + half * TT * TP, half);
-  else dequant_half_rot<T, D, TT, false>(p, d, out, tok, s, j0, rows, tiles + half * TT * TP, half);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -427,22 +556,45 @@ __global__ void general_dequant_retained_kernel(const __grid_constant__ DequantP
 // ---------------------------------------------------------------------------
 // host-side launchers
 // ---------------------------------------------------------------------------
-template <typename T, int D, int TT>
+template <typename T, int D>
 static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st) {
-  const size_t sm = dequant_tile_smem<T, D, TT>();
-  auto kern = dequantize_tile_kernel<T, D, TT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  if (e != cudaSuccess) return e;
-  const int64_t blocks = (int64_t)p.S * p.tiles_slice;
-  if (blocks == 0) return cudaSuccess;
-  kern<<<(unsigned)blocks, kThreads, sm, st>>>(p);
-  return cudaGetLastError();
+  using G = DGeom<T, D>;
+  const int64_t tiles = (int64_t)p.S * p.tiles_slice;
+  if (tiles == 0) return cudaSuccess;
+  const size_t sm_ch = 2 * G::kBuf;
+  const size_t sm_tok = sm_ch + G::kTile;
+  auto ktok = dequantize_tile_kernel<T, D, GKV_AXIS_TOKEN>;
+  auto kch = dequantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(ktok, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_tok)) != cudaSuccess)
+    return e;
+  if ((e = cudaFuncSetAttribute(kch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_ch)) != cudaSuccess)
+    return e;
+  int occ_tok = 0, occ_ch = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_tok, ktok, kDThreads, sm_tok)) != cudaSuccess) return e;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_ch, kch, kDThreads, sm_ch)) != cudaSuccess) return e;
+  const int sms = device_sm_count();
+  const unsigned g_tok = (unsigned)std::min<int64_t>(tiles, (int64_t)sms * std::max(occ_tok, 1));
+  const unsigned g_ch = (unsigned)std::min<int64_t>(tiles, (int64_t)sms * std::max(occ_ch, 1));
+  for (int tensor = 0; tensor < 2; ++tensor) {
+    bool token = false, channel = false;
+    for (int tier = 1; tier <= 2; ++tier) {
+      if (p.tiles[tier] == 0) continue;
+      const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+      (d.axis == GKV_AXIS_TOKEN ? token : channel) = true;
+    }
+    if (!token && !channel) channel = true;  // retained rows only
+    if (token) ktok<<<g_tok, kDThreads, sm_tok, st>>>(p, tensor, 1, (int)tiles);
+    if (channel) kch<<<g_ch, kDThreads, sm_ch, st>>>(p, tensor, token ? 0 : 1, (int)tiles);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 template <typename T>
 static cudaError_t launch_dq_tile_d(const DequantParams& p, cudaStream_t st) {
-  if (p.D == 64) return p.tt == 64 ? launch_dq_tile<T, 64, 64>(p, st) : launch_dq_tile<T, 64, 128>(p, st);
-  if (p.D == 128) return p.tt == 64 ? launch_dq_tile<T, 128, 64>(p, st) : launch_dq_tile<T, 128, 128>(p, st);
+  if (p.D == 64) return launch_dq_tile<T, 64>(p, st);
+  if (p.D == 128) return launch_dq_tile<T, 128>(p, st);
   return cudaErrorInvalidConfiguration;
 }
 

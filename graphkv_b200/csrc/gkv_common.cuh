@@ -439,6 +439,63 @@ __device__ __forceinline__ void fwht_warp(float (&v)[EPL]) {
   }
 }
 
+constexpr unsigned kFull = 0xFFFFFFFFu;
+
+// In-register Hadamard transform of one row split into RPR runs of RUN elements
+// held by the lanes 8 apart (run u in lane bits 3-4).  Butterflies h = 1 .. RUN/2
+// inside the thread, h >= RUN across lanes, in the reference order; then y / div.
+// CHECK: the fused quotient when `fused` (proven exact for quotients >= 2^-100)
+// and no |y| of this thread is below 2^-90 (zeros included: the fused form turns
+// -0 into +0), else IEEE division.  Without CHECK the caller guarantees that
+// every nonzero y is far above 2^-90 and that no y is -0, and `fused` selects.
+template <int RUN, int RPR, bool CHECK = true>
+__device__ __forceinline__ void rotate_run(uint64_t (&v)[RUN / 2], int u, float div, float rdiv, bool fused) {
+  // h = 1: inside each pair
+#pragma unroll
+  for (int k = 0; k < RUN / 2; ++k) {
+    const float a = lo2(v[k]), b = hi2(v[k]);
+    v[k] = pk2(__fadd_rn(a, b), __fsub_rn(a, b));
+  }
+  // h = 2 .. RUN/2: pairs k and k + h/2
+#pragma unroll
+  for (int h = 2; h < RUN; h <<= 1) {
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) {
+      if ((2 * k) & h) continue;
+      const uint64_t a = v[k], b = v[k + h / 2];
+      v[k] = add2(a, b);
+      v[k + h / 2] = sub2(a, b);
+    }
+  }
+  // h = RUN .. (RPR * RUN) / 2: across lanes
+  // (left lane: v + o; right lane: o - v, as fma(-1, v, o): one rounding, as the subtraction)
+#pragma unroll
+  for (int m = 1; m < RPR; m <<= 1) {
+    const float sg = (u & m) ? -1.f : 1.f;
+    const uint64_t sg2 = pk2(sg, sg);
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) {
+      const float o0 = __shfl_xor_sync(kFull, lo2(v[k]), 8 * m);
+      const float o1 = __shfl_xor_sync(kFull, hi2(v[k]), 8 * m);
+      v[k] = fma2(sg2, v[k], pk2(o0, o1));
+    }
+  }
+  if constexpr (CHECK) {
+    float least = __int_as_float(0x7f800000);
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) least = fminf(least, fminf(fabsf(lo2(v[k])), fabsf(hi2(v[k]))));
+    fused = fused && !(least < 8.077935669463161e-28f /* 2^-90 */);
+  }
+  if (fused) {
+    const uint64_t nd2 = pk2(-div, -div), rd2 = pk2(rdiv, rdiv);
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) v[k] = quot2(v[k], nd2, rd2);
+  } else {
+#pragma unroll
+    for (int k = 0; k < RUN / 2; ++k) v[k] = pk2(__fdiv_rn(lo2(v[k]), div), __fdiv_rn(hi2(v[k]), div));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Hadamard helpers (core.py:945-956)
 // ---------------------------------------------------------------------------

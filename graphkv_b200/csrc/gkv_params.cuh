@@ -90,6 +90,8 @@ struct QuantParams {
   LayerDesc layers[kMaxLayers];
 };
 
+int device_sm_count();  // host: SMs of the current device
+
 struct DequantParams {
   int T, D, S;
   const int* idx[3];
@@ -100,9 +102,11 @@ struct DequantParams {
   void* out_k;       // [S, T, D]
   void* out_v;
   float had_div, had_inv;
+  int had_fused;     // as in QuantParams
   int tt;
   int tiles[3];
   int tiles_slice;
+  FastDiv tile_div;  // by tiles_slice
 };
 
 // Slice -> layer lookup (layers sorted by slice_begin).

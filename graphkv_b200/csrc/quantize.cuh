@@ -30,7 +30,6 @@ namespace gkv {
 
 constexpr int kQThreads = 64;   // threads of a quantize tile block
 constexpr int kQTile = 64;      // tier rows of a quantize tile
-constexpr unsigned kFull = 0xFFFFFFFFu;
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 r;
@@ -265,57 +264,6 @@ __device__ void quant_tokens(const TensorDesc& d, const uint8_t* sx, int gslice,
 // ---------------------------------------------------------------------------
 // channel-axis groups (V): thread = (row, run of 128 bytes)
 // ---------------------------------------------------------------------------
-// In-register Hadamard transform of one row split into RPR runs of RUN elements
-// held by the lanes 8 apart (run u in lane bits 3-4).  Butterflies h = 1 .. RUN/2
-// inside the thread, h >= RUN across lanes, in the reference order; then y / div:
-// the fused quotient when `fused` (proven exact for quotients >= 2^-100) and no
-// |y| of this thread is below 2^-90 (zeros included: the fused form turns -0
-// into +0), else IEEE division.
-template <int RUN, int RPR>
-__device__ __forceinline__ void rotate_run(uint64_t (&v)[RUN / 2], int u, float div, float rdiv, bool fused) {
-  // h = 1: inside each pair
-#pragma unroll
-  for (int k = 0; k < RUN / 2; ++k) {
-    const float a = lo2(v[k]), b = hi2(v[k]);
-    v[k] = pk2(__fadd_rn(a, b), __fsub_rn(a, b));
-  }
-  // h = 2 .. RUN/2: pairs k and k + h/2
-#pragma unroll
-  for (int h = 2; h < RUN; h <<= 1) {
-#pragma unroll
-    for (int k = 0; k < RUN / 2; ++k) {
-      if ((2 * k) & h) continue;
-      const uint64_t a = v[k], b = v[k + h / 2];
-      v[k] = add2(a, b);
-      v[k + h / 2] = sub2(a, b);
-    }
-  }
-  // h = RUN .. (RPR * RUN) / 2: across lanes
-  // (left lane: v + o; right lane: o - v, as fma(-1, v, o): one rounding, as the subtraction)
-#pragma unroll
-  for (int m = 1; m < RPR; m <<= 1) {
-    const float sg = (u & m) ? -1.f : 1.f;
-    const uint64_t sg2 = pk2(sg, sg);
-#pragma unroll
-    for (int k = 0; k < RUN / 2; ++k) {
-      const float o0 = __shfl_xor_sync(kFull, lo2(v[k]), 8 * m);
-      const float o1 = __shfl_xor_sync(kFull, hi2(v[k]), 8 * m);
-      v[k] = fma2(sg2, v[k], pk2(o0, o1));
-    }
-  }
-  float least = __int_as_float(0x7f800000);
-#pragma unroll
-  for (int k = 0; k < RUN / 2; ++k) least = fminf(least, fminf(fabsf(lo2(v[k])), fabsf(hi2(v[k]))));
-  if (fused && !(least < 8.077935669463161e-28f /* 2^-90 */)) {
-    const uint64_t nd2 = pk2(-div, -div), rd2 = pk2(rdiv, rdiv);
-#pragma unroll
-    for (int k = 0; k < RUN / 2; ++k) v[k] = quot2(v[k], nd2, rd2);
-  } else {
-#pragma unroll
-    for (int k = 0; k < RUN / 2; ++k) v[k] = pk2(__fdiv_rn(lo2(v[k]), div), __fdiv_rn(hi2(v[k]), div));
-  }
-}
-
 template <typename T, int NW>
 __device__ __forceinline__ void load_run(const uint8_t* src, uint32_t (&w)[NW]) {
 #pragma unroll
@@ -453,27 +401,41 @@ __device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
   return r;
 }
 
-// Issue the loads of tile `tr` of one tensor into a staging buffer: thread r
-// copies row r with one bulk copy (TMA, 16-byte aligned rows) that completes on
-// `bar`; rows past the end of the tier are zero-filled in place (token-axis
-// groups quantize them as padding).  Thread 0 arms the barrier with the bytes.
+// Issue the loads of tile `tr` of one tensor into a staging buffer with 16-byte
+// asynchronous copies: thread = (chunk c, rows r0, r0 + STEP, ...), so the lanes
+// of a warp cover whole rows (coalesced).  The rows' token indices are loaded
+// once per warp (one per lane) and handed out with shuffles, so a thread waits
+// for one load before its copies go out.  Rows past the end of the tier are
+// zero-filled (token-axis groups quantize them as padding).  The caller commits.
 template <typename T, int D>
 __device__ __forceinline__ void stage_tile(const QuantParams& p, const TileRef& tr, const T* base, int64_t st,
-                                           uint8_t* sx, uint64_t* bar) {
+                                           uint8_t* sx) {
   using G = QGeom<T, D>;
-  static_assert(kQThreads == kQTile, "one row per thread");
+  constexpr int STEP = kQThreads / G::kChunks;  // rows per pass of the block (4 for 16 chunks per row)
+  constexpr int LPR = G::kChunks;               // lanes per row within a pass
+  static_assert(LPR <= 32 && 32 % LPR == 0, "rows of a pass start inside one warp");
+  constexpr int RPW = 32 / LPR;                 // rows of one pass held by a warp
+  constexpr int NPASS = kQTile / STEP;          // passes
+  static_assert(NPASS * RPW <= 32, "one index per lane");
+  const int* idx = p.idx[tr.tier];
   const int j0 = tr.k * kQTile;
   const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-  const int r = threadIdx.x;
-  if (threadIdx.x == 0) mbar_arrive_expect_tx(bar, (uint32_t)(rows * G::kRowBytes));
-  uint8_t* dst = sx + r * G::kPitchB;
-  if (r < rows) {
-    int tok = p.idx[tr.tier][j0 + r];
-    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
-    bulk_load(dst, base + tok * st, (uint32_t)G::kRowBytes, bar);
-  } else {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // lane l holds the index of row (l / RPW) * STEP + warp * RPW + l % RPW
+  const int lrow = (lane / RPW) * STEP + warp * RPW + lane % RPW;
+  int ltok = 0;
+  if (lane < NPASS * RPW && lrow < rows) {
+    ltok = idx[j0 + lrow];
+    if ((unsigned)ltok >= (unsigned)p.T) { raise_error(kErrBadIndex); ltok = 0; }
+  }
+  const int c = threadIdx.x % LPR, b = lane / LPR;  // this thread's row in a pass: pass * STEP + warp * RPW + b
+  const uint8_t* src0 = reinterpret_cast<const uint8_t*>(base) + c * 16;
+  uint8_t* dst0 = sx + (warp * RPW + b) * G::kPitchB + c * 16;
 #pragma unroll
-    for (int c = 0; c < G::kChunks; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = 0; i < NPASS; ++i) {
+    const int r = i * STEP + warp * RPW + b;
+    const int tok = __shfl_sync(kFull, ltok, i * RPW + b);
+    cp_async16(dst0 + i * STEP * G::kPitchB, src0 + (int64_t)tok * st * (int64_t)sizeof(T), r < rows ? 16u : 0u);
   }
 }
 
@@ -501,33 +463,25 @@ __device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr
 // compiled per grouping axis (AXIS): tiles of a tier grouped along the other
 // axis are left to the other kernel; retained-row tiles are copied when
 // `copy_retained`.  Two staging buffers: while a tile is quantized, the rows of
-// the block's next tile are in flight.
+// the block's next tile are in flight (one asynchronous-copy group per tile).
 template <typename T, int D, int AXIS>
 __global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor,
                                                                      int copy_retained, int total_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * G::kSmem);
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-  }
-  __syncthreads();
   // first tile of this block that the launch handles
   int cur = blockIdx.x;
   int role = 0;
   for (; cur < total_tiles; cur += gridDim.x)
     if ((role = tile_role<AXIS>(p, tile_ref(p, cur), tensor, copy_retained)) != 0) break;
-  uint32_t phase = 0u;    // bit b: parity of buffer b's next phase
-  uint32_t pending = 0u;  // bit b: buffer b has copies in flight
   int buf = 0;
   if (cur < total_tiles && role == 2) {
     const TileRef tr = tile_ref(p, cur);
     int64_t st;
     const T* base = tensor_base<T>(p, tr.s, tensor, st);
-    stage_tile<T, D>(p, tr, base, st, smem, &bar[0]);
-    pending = 1u;
+    stage_tile<T, D>(p, tr, base, st, smem);
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
   while (cur < total_tiles) {
     // find and stage the next tile
     int nxt = cur + gridDim.x, nrole = 0;
@@ -537,9 +491,9 @@ __global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __gri
       const TileRef tn = tile_ref(p, nxt);
       int64_t st;
       const T* base = tensor_base<T>(p, tn.s, tensor, st);
-      stage_tile<T, D>(p, tn, base, st, smem + (buf ^ 1) * G::kSmem, &bar[buf ^ 1]);
-      pending |= 1u << (buf ^ 1);
+      stage_tile<T, D>(p, tn, base, st, smem + (buf ^ 1) * G::kSmem);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     const TileRef tr = tile_ref(p, cur);
     const int gslice = p.slice_offset + tr.s;
     int64_t st;
@@ -547,14 +501,8 @@ __global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __gri
     if (role == 1) {
       copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
     } else {
-      const bool ok = block_wait(&bar[buf], (phase >> buf) & 1u);
-      phase ^= 1u << buf;
-      pending &= ~(1u << buf);
-      if (!ok) {
-        // error recorded; let the other buffer's copies land (bounded) before exiting
-        if (pending & (1u << (buf ^ 1))) block_wait(&bar[buf ^ 1], (phase >> (buf ^ 1)) & 1u);
-        return;
-      }
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+      __syncthreads();  // every thread's rows of this tile have landed
       uint8_t* sx = smem + buf * G::kSmem;
       const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
       const int j0 = tr.k * kQTile;
@@ -571,13 +519,12 @@ __global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __gri
         quant_tile_channels<T, D>(d, sx, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
       }
     }
-    // this buffer's generic-proxy reads / writes precede the next bulk copies into it
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
+    __syncthreads();  // this buffer is refilled from the next iteration on
     cur = nxt;
     role = nrole;
     buf ^= 1;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -742,14 +689,13 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 // ---------------------------------------------------------------------------
 // host-side launchers (called from capi.cu)
 // ---------------------------------------------------------------------------
-int device_sm_count();
 
 // Per tensor (keys, values): one launch per grouping axis its tiers use; the
 // first of them also copies the tensor's retained rows.  Persistent grid: as
 // many blocks as fit on the device at once, at most one per tile.
 template <typename T, int D>
 static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
-  const size_t sm = 2 * QGeom<T, D>::kSmem + 2 * sizeof(uint64_t);
+  const size_t sm = 2 * QGeom<T, D>::kSmem;
   const int64_t tiles = (int64_t)p.S * p.tiles_slice;
   if (tiles == 0) return cudaSuccess;
   cudaError_t e;
