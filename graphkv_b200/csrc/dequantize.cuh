@@ -112,6 +112,23 @@ struct DStage {
   }
 };
 
+// Scales, zero points and the output row of a tile, loaded into registers when
+// the tile's copies are issued and written to its staging buffer one tile of
+// work later (so no store waits for a load).
+struct DMeta {
+  float scale[kDItems];
+  int zp[kDItems];
+  int tok;
+  __device__ __forceinline__ void put(const DStage& st) const {
+#pragma unroll
+    for (int i = 0; i < kDItems; ++i) {
+      st.scale[i * kDThreads + threadIdx.x] = scale[i];
+      st.zp[i * kDThreads + threadIdx.x] = zp[i];
+    }
+    st.tok[threadIdx.x] = tok;
+  }
+};
+
 template <int NB>
 __device__ __forceinline__ void copy_codes(const DStage& st, int b0, const uint8_t* src) {
   if constexpr (NB == 8) {
@@ -185,7 +202,7 @@ struct ChanMap {
 };
 
 template <int D, int RUN, int SB>
-__device__ __forceinline__ void chan_issue(const TensorDesc& d, int s, int j0, int rows, const DStage& st) {
+__device__ __forceinline__ void chan_issue(const TensorDesc& d, int s, int j0, int rows, const DStage& st, DMeta& m) {
   using M = ChanMap<D, RUN>;
   constexpr int NB = RUN * SB / 8;
 #pragma unroll
@@ -201,8 +218,8 @@ __device__ __forceinline__ void chan_issue(const TensorDesc& d, int s, int j0, i
       sc = load_scale(d.scales, gi, d.scale_dtype);
       zp = load_zp(d, gi);
     }
-    st.scale[i * kDThreads + threadIdx.x] = sc;
-    st.zp[i * kDThreads + threadIdx.x] = zp;
+    m.scale[i] = sc;
+    m.zp[i] = zp;
   }
 }
 
@@ -265,7 +282,7 @@ struct TokMap {
 };
 
 template <typename T, int D, int GS, int SB>
-__device__ __forceinline__ void tok_issue(const TensorDesc& d, int s, int j0, const DStage& st) {
+__device__ __forceinline__ void tok_issue(const TensorDesc& d, int s, int j0, const DStage& st, DMeta& m) {
   using M = TokMap<T, D, GS>;
   constexpr int NB = GS * SB / 8;  // code bytes per channel and group
 #pragma unroll
@@ -284,8 +301,8 @@ __device__ __forceinline__ void tok_issue(const TensorDesc& d, int s, int j0, co
         sc = load_scale(d.scales, gi, d.scale_dtype);
         zp = load_zp(d, gi);
       }
-      st.scale[(i * M::CPW + c) * kDThreads + threadIdx.x] = sc;
-      st.zp[(i * M::CPW + c) * kDThreads + threadIdx.x] = zp;
+      m.scale[i * M::CPW + c] = sc;
+      m.zp[i * M::CPW + c] = zp;
     }
   }
 }
@@ -346,30 +363,30 @@ __device__ void tok_decode(const TensorDesc& d, const DStage& st, int j0, uint8_
 
 // ---- dispatch -------------------------------------------------------------
 template <typename T, int D, int AXIS>
-__device__ __forceinline__ void dq_issue(const TensorDesc& d, int s, int j0, int rows, const DStage& st) {
+__device__ __forceinline__ void dq_issue(const TensorDesc& d, int s, int j0, int rows, const DStage& st, DMeta& m) {
   if constexpr (AXIS == GKV_AXIS_TOKEN) {
     (void)rows;
     if (d.gs == 64) {
-      if (d.sbits == 4) tok_issue<T, D, 64, 4>(d, s, j0, st);
-      else if (d.sbits == 2) tok_issue<T, D, 64, 2>(d, s, j0, st);
-      else tok_issue<T, D, 64, 8>(d, s, j0, st);
+      if (d.sbits == 4) tok_issue<T, D, 64, 4>(d, s, j0, st, m);
+      else if (d.sbits == 2) tok_issue<T, D, 64, 2>(d, s, j0, st, m);
+      else tok_issue<T, D, 64, 8>(d, s, j0, st, m);
     } else {
-      if (d.sbits == 4) tok_issue<T, D, 32, 4>(d, s, j0, st);
-      else if (d.sbits == 2) tok_issue<T, D, 32, 2>(d, s, j0, st);
-      else tok_issue<T, D, 32, 8>(d, s, j0, st);
+      if (d.sbits == 4) tok_issue<T, D, 32, 4>(d, s, j0, st, m);
+      else if (d.sbits == 2) tok_issue<T, D, 32, 2>(d, s, j0, st, m);
+      else tok_issue<T, D, 32, 8>(d, s, j0, st, m);
     }
   } else {
     constexpr int RUN = DGeom<T, D>::kRun;
     if (d.gs < RUN) {
       if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) {
-        if (d.sbits == 4) chan_issue<D, RUN / 2, 4>(d, s, j0, rows, st);
-        else if (d.sbits == 2) chan_issue<D, RUN / 2, 2>(d, s, j0, rows, st);
-        else chan_issue<D, RUN / 2, 8>(d, s, j0, rows, st);
+        if (d.sbits == 4) chan_issue<D, RUN / 2, 4>(d, s, j0, rows, st, m);
+        else if (d.sbits == 2) chan_issue<D, RUN / 2, 2>(d, s, j0, rows, st, m);
+        else chan_issue<D, RUN / 2, 8>(d, s, j0, rows, st, m);
       }
     } else {
-      if (d.sbits == 4) chan_issue<D, RUN, 4>(d, s, j0, rows, st);
-      else if (d.sbits == 2) chan_issue<D, RUN, 2>(d, s, j0, rows, st);
-      else chan_issue<D, RUN, 8>(d, s, j0, rows, st);
+      if (d.sbits == 4) chan_issue<D, RUN, 4>(d, s, j0, rows, st, m);
+      else if (d.sbits == 2) chan_issue<D, RUN, 2>(d, s, j0, rows, st, m);
+      else chan_issue<D, RUN, 8>(d, s, j0, rows, st, m);
     }
   }
 }
@@ -391,7 +408,7 @@ __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const Te
 // Persistent blocks over the tiles of one tensor (`tensor` 1: values, 0: keys),
 // compiled per grouping axis; retained-row tiles are copied when `copy_retained`.
 template <typename T, int D, int AXIS>
-__global__ void __launch_bounds__(kDThreads, 8) dequantize_tile_kernel(const __grid_constant__ DequantParams p,
+__global__ void __launch_bounds__(kDThreads, AXIS == GKV_AXIS_TOKEN ? 5 : 8) dequantize_tile_kernel(const __grid_constant__ DequantParams p,
                                                                        int tensor, int copy_retained,
                                                                        int total_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -402,42 +419,58 @@ __global__ void __launch_bounds__(kDThreads, 8) dequantize_tile_kernel(const __g
   for (; cur < total_tiles; cur += gridDim.x)
     if ((role = dtile_role<AXIS>(p, dtile_ref(p, cur), tensor, copy_retained)) != 0) break;
   int buf = 0;
+  // issue the copies of tile t into buffer b; its metadata comes back in registers
   auto issue = [&](int t, int b) {
+    DMeta m;
+#pragma unroll
+    for (int i = 0; i < kDItems; ++i) { m.scale[i] = 0.f; m.zp[i] = 0; }
     const DTileRef tr = dtile_ref(p, t);
     const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
     const int j0 = tr.k * kDTile;
     const int rows = min(kDTile, p.n_tier[tr.tier] - j0);
-    const DStage st = DStage::at(smem + b * G::kBuf, G::kStage);
-    dq_issue<T, D, AXIS>(d, tr.s, j0, rows, st);
-    int t_out = -1;
+    dq_issue<T, D, AXIS>(d, tr.s, j0, rows, DStage::at(smem + b * G::kBuf, G::kStage), m);
+    m.tok = -1;
     if ((int)threadIdx.x < rows) {
-      t_out = p.idx[tr.tier][j0 + threadIdx.x];
-      if ((unsigned)t_out >= (unsigned)p.T) { raise_error(kErrBadIndex); t_out = -1; }
+      m.tok = p.idx[tr.tier][j0 + threadIdx.x];
+      if ((unsigned)m.tok >= (unsigned)p.T) { raise_error(kErrBadIndex); m.tok = -1; }
     }
-    st.tok[threadIdx.x] = t_out;
+    return m;
   };
-  if (cur < total_tiles && role == 2) issue(cur, 0);
+  if (cur < total_tiles && role == 2) issue(cur, 0).put(DStage::at(smem, G::kStage));
   asm volatile("cp.async.commit_group;" ::: "memory");
   while (cur < total_tiles) {
     int nxt = cur + gridDim.x, nrole = 0;
     for (; nxt < total_tiles; nxt += gridDim.x)
       if ((nrole = dtile_role<AXIS>(p, dtile_ref(p, nxt), tensor, copy_retained)) != 0) break;
-    if (nxt < total_tiles && nrole == 2) issue(nxt, buf ^ 1);
+    const bool stage_next = nxt < total_tiles && nrole == 2;
+    DMeta next_meta;
+    if (stage_next) next_meta = issue(nxt, buf ^ 1);
     asm volatile("cp.async.commit_group;" ::: "memory");
     const DTileRef tr = dtile_ref(p, cur);
     T* out = out_base + (int64_t)tr.s * p.T * D;
     if (role == 1) {
-      constexpr int VEC = 16 / (int)sizeof(T), CPR = D / VEC;
+      // retained rows: thread = (16-byte chunk, rows r0, r0 + STEP, ...), loads before stores
+      constexpr int VEC = 16 / (int)sizeof(T), CPR = D / VEC, STEP = kDThreads / CPR, N = kRetTile / STEP;
       const int R = p.n_tier[0];
       const int j0 = tr.k * kRetTile, rows = min(kRetTile, R - j0);
       const T* src = reinterpret_cast<const T*>(tensor ? p.ret_v : p.ret_k) + ((int64_t)tr.s * R + j0) * D;
-      for (int e = threadIdx.x; e < rows * CPR; e += kDThreads) {
-        const int r = e / CPR, c = e - r * CPR;
-        const int t_out = p.idx[0][j0 + r];
-        if ((unsigned)t_out >= (unsigned)p.T) { raise_error(kErrBadIndex); continue; }
-        *reinterpret_cast<uint4*>(out + (int64_t)t_out * D + c * VEC) =
-            *reinterpret_cast<const uint4*>(src + r * D + c * VEC);
+      const int c = threadIdx.x % CPR, r0 = threadIdx.x / CPR;
+      uint4 v[N];
+      int to[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int r = r0 + i * STEP;
+        to[i] = -1;
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (r < rows) {
+          to[i] = p.idx[0][j0 + r];
+          if ((unsigned)to[i] >= (unsigned)p.T) { raise_error(kErrBadIndex); to[i] = -1; }
+          v[i] = *reinterpret_cast<const uint4*>(src + r * D + c * VEC);
+        }
       }
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if (to[i] >= 0) *reinterpret_cast<uint4*>(out + (int64_t)to[i] * D + c * VEC) = v[i];
     } else {
       asm volatile("cp.async.wait_group 1;" ::: "memory");
       __syncthreads();  // every thread's staged rows / metadata of this tile are visible
@@ -476,6 +509,7 @@ __global__ void __launch_bounds__(kDThreads, 8) dequantize_tile_kernel(const __g
         }
       }
     }
+    if (stage_next) next_meta.put(DStage::at(smem + (buf ^ 1) * G::kBuf, G::kStage));
     __syncthreads();  // this buffer and the tile are rewritten from the next iteration on
     cur = nxt;
     role = nrole;

@@ -54,19 +54,34 @@ struct QGeom {
 // ---------------------------------------------------------------------------
 // retained rows
 // ---------------------------------------------------------------------------
+// Retained rows of one tensor: thread = (16-byte chunk, rows r0, r0 + STEP, ...);
+// all of a thread's loads are issued before its stores.
 template <typename T, int D>
 __device__ void copy_retained_tile(const QuantParams& p, const T* src, int64_t st, void* ret, int gslice, int tile) {
   constexpr int kVec = 16 / (int)sizeof(T);
   constexpr int kChunks = D / kVec;
+  constexpr int STEP = kQThreads / kChunks;
+  constexpr int N = kRetTile / STEP;
   const int R = p.n_tier[0];
   const int j0 = tile * kRetTile;
   const int rows = min(kRetTile, R - j0);
   T* dst = reinterpret_cast<T*>(ret) + ((int64_t)gslice * R + j0) * D;
-  for (int e = threadIdx.x; e < rows * kChunks; e += kQThreads) {
-    const int r = e / kChunks, c = e - r * kChunks;
-    int tok = p.idx[0][j0 + r];
-    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
-    *reinterpret_cast<uint4*>(dst + r * D + c * kVec) = ldg_stream(src + tok * st + c * kVec);
+  const int c = threadIdx.x % kChunks, r0 = threadIdx.x / kChunks;
+  uint4 v[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int r = r0 + i * STEP;
+    v[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (r < rows) {
+      int tok = p.idx[0][j0 + r];
+      if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
+      v[i] = ldg_stream(src + tok * st + c * kVec);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int r = r0 + i * STEP;
+    if (r < rows) *reinterpret_cast<uint4*>(dst + r * D + c * kVec) = v[i];
   }
 }
 
@@ -401,41 +416,54 @@ __device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
   return r;
 }
 
-// Issue the loads of tile `tr` of one tensor into a staging buffer with 16-byte
-// asynchronous copies: thread = (chunk c, rows r0, r0 + STEP, ...), so the lanes
-// of a warp cover whole rows (coalesced).  The rows' token indices are loaded
-// once per warp (one per lane) and handed out with shuffles, so a thread waits
-// for one load before its copies go out.  Rows past the end of the tier are
-// zero-filled (token-axis groups quantize them as padding).  The caller commits.
+// Staging of a tile of one tensor with 16-byte asynchronous copies: thread =
+// (chunk c, rows r0, r0 + STEP, ...), so the lanes of a warp cover whole rows
+// (coalesced).  The rows' token indices are loaded one tile ahead, one per lane
+// (tile_tokens), and handed out with shuffles when the copies are issued
+// (stage_tile), so issuing never waits for a load.  Rows past the end of the
+// tier are zero-filled (token-axis groups quantize them as padding).
 template <typename T, int D>
-__device__ __forceinline__ void stage_tile(const QuantParams& p, const TileRef& tr, const T* base, int64_t st,
-                                           uint8_t* sx) {
+struct StageMap {
   using G = QGeom<T, D>;
-  constexpr int STEP = kQThreads / G::kChunks;  // rows per pass of the block (4 for 16 chunks per row)
-  constexpr int LPR = G::kChunks;               // lanes per row within a pass
-  static_assert(LPR <= 32 && 32 % LPR == 0, "rows of a pass start inside one warp");
-  constexpr int RPW = 32 / LPR;                 // rows of one pass held by a warp
-  constexpr int NPASS = kQTile / STEP;          // passes
-  static_assert(NPASS * RPW <= 32, "one index per lane");
-  const int* idx = p.idx[tr.tier];
+  static constexpr int STEP = kQThreads / G::kChunks;  // rows per pass of the block
+  static constexpr int LPR = G::kChunks;               // lanes per row within a pass
+  static constexpr int RPW = 32 / LPR;                 // rows of one pass held by a warp
+  static constexpr int NPASS = kQTile / STEP;          // passes
+  static_assert(LPR <= 32 && 32 % LPR == 0 && NPASS * RPW <= 32, "one index per lane");
+};
+
+template <typename T, int D>
+__device__ __forceinline__ int tile_tokens(const QuantParams& p, const TileRef& tr) {
+  using M = StageMap<T, D>;
   const int j0 = tr.k * kQTile;
   const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // lane l holds the index of row (l / RPW) * STEP + warp * RPW + l % RPW
-  const int lrow = (lane / RPW) * STEP + warp * RPW + lane % RPW;
-  int ltok = 0;
-  if (lane < NPASS * RPW && lrow < rows) {
-    ltok = idx[j0 + lrow];
-    if ((unsigned)ltok >= (unsigned)p.T) { raise_error(kErrBadIndex); ltok = 0; }
+  const int lrow = (lane / M::RPW) * M::STEP + warp * M::RPW + lane % M::RPW;
+  int tok = 0;
+  if (lane < M::NPASS * M::RPW && lrow < rows) {
+    tok = p.idx[tr.tier][j0 + lrow];
+    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
   }
-  const int c = threadIdx.x % LPR, b = lane / LPR;  // this thread's row in a pass: pass * STEP + warp * RPW + b
+  return tok;
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void stage_tile(const QuantParams& p, const TileRef& tr, const T* base, int64_t st,
+                                           uint8_t* sx, int ltok) {
+  using G = QGeom<T, D>;
+  using M = StageMap<T, D>;
+  const int j0 = tr.k * kQTile;
+  const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = threadIdx.x % M::LPR, b = lane / M::LPR;  // row of a pass: pass * STEP + warp * RPW + b
   const uint8_t* src0 = reinterpret_cast<const uint8_t*>(base) + c * 16;
-  uint8_t* dst0 = sx + (warp * RPW + b) * G::kPitchB + c * 16;
+  uint8_t* dst0 = sx + (warp * M::RPW + b) * G::kPitchB + c * 16;
 #pragma unroll
-  for (int i = 0; i < NPASS; ++i) {
-    const int r = i * STEP + warp * RPW + b;
-    const int tok = __shfl_sync(kFull, ltok, i * RPW + b);
-    cp_async16(dst0 + i * STEP * G::kPitchB, src0 + (int64_t)tok * st * (int64_t)sizeof(T), r < rows ? 16u : 0u);
+  for (int i = 0; i < M::NPASS; ++i) {
+    const int r = i * M::STEP + warp * M::RPW + b;
+    const int tok = __shfl_sync(kFull, ltok, i * M::RPW + b);
+    cp_async16(dst0 + i * M::STEP * G::kPitchB, src0 + (int64_t)tok * st * (int64_t)sizeof(T), r < rows ? 16u : 0u);
   }
 }
 
@@ -469,31 +497,38 @@ __global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __gri
                                                                      int copy_retained, int total_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
-  // first tile of this block that the launch handles
-  int cur = blockIdx.x;
-  int role = 0;
-  for (; cur < total_tiles; cur += gridDim.x)
-    if ((role = tile_role<AXIS>(p, tile_ref(p, cur), tensor, copy_retained)) != 0) break;
+  // tiles of this block that the launch handles: cur, nxt (staged one ahead),
+  // and the one after (its row indices are loaded one ahead of staging)
+  auto next_tile = [&](int from, int& role_out) {
+    int t = from;
+    role_out = 0;
+    for (; t < total_tiles; t += gridDim.x)
+      if ((role_out = tile_role<AXIS>(p, tile_ref(p, t), tensor, copy_retained)) != 0) break;
+    return t;
+  };
+  int role, nrole;
+  int cur = next_tile(blockIdx.x, role);
+  int nxt = next_tile(cur + gridDim.x, nrole);
   int buf = 0;
   if (cur < total_tiles && role == 2) {
     const TileRef tr = tile_ref(p, cur);
     int64_t st;
     const T* base = tensor_base<T>(p, tr.s, tensor, st);
-    stage_tile<T, D>(p, tr, base, st, smem);
+    stage_tile<T, D>(p, tr, base, st, smem, tile_tokens<T, D>(p, tr));
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
+  int ntok = (nxt < total_tiles && nrole == 2) ? tile_tokens<T, D>(p, tile_ref(p, nxt)) : 0;
   while (cur < total_tiles) {
-    // find and stage the next tile
-    int nxt = cur + gridDim.x, nrole = 0;
-    for (; nxt < total_tiles; nxt += gridDim.x)
-      if ((nrole = tile_role<AXIS>(p, tile_ref(p, nxt), tensor, copy_retained)) != 0) break;
+    int nrole2;
+    const int nxt2 = next_tile(nxt + gridDim.x, nrole2);
     if (nxt < total_tiles && nrole == 2) {
       const TileRef tn = tile_ref(p, nxt);
       int64_t st;
       const T* base = tensor_base<T>(p, tn.s, tensor, st);
-      stage_tile<T, D>(p, tn, base, st, smem + (buf ^ 1) * G::kSmem);
+      stage_tile<T, D>(p, tn, base, st, smem + (buf ^ 1) * G::kSmem, ntok);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    const int ntok2 = (nxt2 < total_tiles && nrole2 == 2) ? tile_tokens<T, D>(p, tile_ref(p, nxt2)) : 0;
     const TileRef tr = tile_ref(p, cur);
     const int gslice = p.slice_offset + tr.s;
     int64_t st;
@@ -522,6 +557,9 @@ __global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __gri
     __syncthreads();  // this buffer is refilled from the next iteration on
     cur = nxt;
     role = nrole;
+    nxt = nxt2;
+    nrole = nrole2;
+    ntok = ntok2;
     buf ^= 1;
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
