@@ -28,7 +28,9 @@
 
 namespace gkv {
 
-constexpr int kQThreads = 64;   // threads of a quantize tile block
+constexpr int kQThreads = 128;  // threads of a quantize tile block
+constexpr int kQWarps = kQThreads / 32;
+constexpr int kQRows = 32;      // rows of a token-axis column run (half a tile)
 constexpr int kQTile = 64;      // tier rows of a quantize tile
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
@@ -48,7 +50,8 @@ struct QGeom {
   static constexpr int kChunks = kRowBytes / 16;   // 16-byte chunks per row
   static constexpr int kEPW = 4 / (int)sizeof(T);  // elements per word
   static constexpr int kRun = 128 / (int)sizeof(T);  // elements of a channel-axis run (128 bytes)
-  static constexpr size_t kSmem = (size_t)kQTile * kPitchB;  // one tensor's tile
+  static constexpr size_t kTileBytes = (size_t)kQTile * kPitchB;              // one tensor's tile
+  static constexpr size_t kSmem = kTileBytes + (size_t)kWords * 2 * 2 * 4;   // + token-axis exchange
 };
 
 // ---------------------------------------------------------------------------
@@ -86,13 +89,13 @@ __device__ void copy_retained_tile(const QuantParams& p, const T* src, int64_t s
 }
 
 // Hadamard rotation of the tile's rows in shared memory (token-axis tensors with
-// the rotation), one warp per row, by the two warps of a half-block.
+// the rotation), one warp per row.
 template <typename T, int D>
 __device__ void rotate_rows_smem(T* sx, float div, float inv, int hw) {
   using G = QGeom<T, D>;
   constexpr int EPL = D / 32;
   const int lane = threadIdx.x & 31;
-  for (int r = hw; r < kQTile; r += 2) {
+  for (int r = hw; r < kQTile; r += kQWarps) {
     T* row = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(sx) + r * G::kPitchB) + lane * EPL;
     float v[EPL];
 #pragma unroll
@@ -218,60 +221,127 @@ __device__ __forceinline__ void run_stats(const uint32_t (&w)[NW], float& mn, fl
 }
 
 // ---------------------------------------------------------------------------
-// token-axis groups (K): thread = (column word, group)
+// token-axis groups (K): thread = (column word, run of 32 rows)
 // ---------------------------------------------------------------------------
-template <typename T, int D, int GS, int SB, bool AFF>
-__device__ void quant_tokens(const TensorDesc& d, const uint8_t* sx, int gslice, int j0, int ht) {
-  using G = QGeom<T, D>;
-  constexpr int NG = kQTile / GS;          // groups per tile
-  constexpr int ITEMS = G::kWords * NG;
-#pragma unroll 1
-  for (int item = ht; item < ITEMS; item += kQThreads) {
-    const int g = item / G::kWords, w = item - g * G::kWords;
-    const int tok0 = j0 + g * GS;
-    if (tok0 >= d.n_pad) continue;  // a whole group of padding past the padded tier
-    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (g * GS) * G::kPitchB) + w;
-    uint32_t x[GS];
-#pragma unroll
-    for (int i = 0; i < GS; ++i) x[i] = col[i * G::kPitchW];
+// Statistics of a column run as 32-bit words: 16-bit types keep both channels
+// packed (absmax, or min and max); fp32 keeps the float bits.
+template <typename T, bool AFF>
+struct ColStats {
+  uint32_t a, b;  // symmetric: a = absmax; affine: a = min, b = max
+  __device__ __forceinline__ void init() {
     if constexpr (sizeof(T) == 4) {
-      float mn, mx;
-      run_stats<T, AFF, GS>(x, mn, mx);
+      a = AFF ? 0x7f800000u : 0u;
+      b = 0xff800000u;
+    } else {
+      a = AFF ? Word16<T>::kPosInf : 0u;
+      b = Word16<T>::kNegInf;
+    }
+  }
+  __device__ __forceinline__ void add(uint32_t x) {
+    if constexpr (sizeof(T) == 4) {
+      const float f = __uint_as_float(x);
+      if (AFF) {
+        a = __float_as_uint(fminf(__uint_as_float(a), f));
+        b = __float_as_uint(fmaxf(__uint_as_float(b), f));
+      } else {
+        a = __float_as_uint(fmaxf(__uint_as_float(a), fabsf(f)));
+      }
+    } else {
+      if (AFF) { a = Word16<T>::vmin(a, x); b = Word16<T>::vmax(b, x); }
+      else a = Word16<T>::amax(a, x);
+    }
+  }
+  __device__ __forceinline__ void merge(const ColStats& o) {
+    if constexpr (sizeof(T) == 4) {
+      if (AFF) {
+        a = __float_as_uint(fminf(__uint_as_float(a), __uint_as_float(o.a)));
+        b = __float_as_uint(fmaxf(__uint_as_float(b), __uint_as_float(o.b)));
+      } else {
+        a = __float_as_uint(fmaxf(__uint_as_float(a), __uint_as_float(o.a)));
+      }
+    } else {
+      if (AFF) { a = Word16<T>::vmin(a, o.a); b = Word16<T>::vmax(b, o.b); }
+      else a = Word16<T>::amax(a, o.a);
+    }
+  }
+};
+
+// Tile rows are split into two runs of 32 (thread = (word w, run h)); lanes of a
+// warp own consecutive words of the same rows.  A 64-row group spans both runs:
+// their statistics meet through shared memory (`xch`, 2 words per item).
+template <typename T, int D, int GS, int SB, bool AFF>
+__device__ void quant_tokens(const TensorDesc& d, const uint8_t* sx, int gslice, int j0, uint32_t* xch) {
+  using G = QGeom<T, D>;
+  constexpr int NH = kQTile / kQRows;          // runs per column
+  constexpr int ITEMS = G::kWords * NH;
+  constexpr bool SPLIT = GS > kQRows;          // a group spans the two runs
+  static_assert(GS == 32 || GS == 64, "token-axis groups of 32 or 64 rows");
+  constexpr int CPW = 4 / (int)sizeof(T);
+  for (int base = 0; base < ITEMS; base += kQThreads) {  // uniform trip count: barriers inside
+    const int item = base + (int)threadIdx.x;
+    const bool act = item < ITEMS;
+    const int h = act ? item / G::kWords : 0, w = act ? item - h * G::kWords : 0;
+    const int tok0 = j0 + h * kQRows;            // first tier row of this run
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(sx + (h * kQRows) * G::kPitchB) + w;
+    uint32_t x[kQRows];
+#pragma unroll
+    for (int i = 0; i < kQRows; ++i) x[i] = act ? col[i * G::kPitchW] : 0u;
+    ColStats<T, AFF> cs;
+    cs.init();
+#pragma unroll
+    for (int i = 0; i < kQRows; ++i) cs.add(x[i]);
+    if constexpr (SPLIT) {
+      if (act) { xch[2 * item] = cs.a; xch[2 * item + 1] = cs.b; }
+      __syncthreads();
+      if (act) {
+        const int other = (h ^ 1) * G::kWords + w;
+        ColStats<T, AFF> o;
+        o.a = xch[2 * other];
+        o.b = xch[2 * other + 1];
+        cs.merge(o);
+      }
+      __syncthreads();  // xch is reused by the next round
+    }
+    if (!act || tok0 >= d.n_pad) continue;
+    const bool first = (h * kQRows) % GS == 0;   // this run starts its group: it stores the scales
+    const int gtok = tok0 - (h * kQRows) % GS;
+    constexpr int NB = kQRows * SB / 8;          // code bytes per channel and run
+    if constexpr (CPW == 1) {
+      const float mn = __uint_as_float(cs.a), mx = AFF ? __uint_as_float(cs.b) : __uint_as_float(cs.a);
       const FastCoder c = AFF ? aff_coder(mn, mx, d.qmax, d.rqmax)
                               : sym_coder(mx, d.qmax, d.rqmax, d.bits, d.packed != 0);
       const int ch = w;
-      const int64_t gi = ((int64_t)gslice * D + ch) * d.groups_row + (tok0 >> d.log2gs);
-      store_scale(d.scales, gi, d.scale_dtype, c.scale);
-      if (AFF) d.zps[gi] = (uint8_t)c.zp;
+      if (first) {
+        const int64_t gi = ((int64_t)gslice * D + ch) * d.groups_row + (gtok >> d.log2gs);
+        store_scale(d.scales, gi, d.scale_dtype, c.scale);
+        if (AFF) d.zps[gi] = (uint8_t)c.zp;
+      }
       const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + tok0;
-      encode_store_run<T, SB, AFF, GS>(x, c, d.codes + (e0 * SB) / 8, true);
+      encode_store_run<T, SB, AFF, kQRows>(x, c, d.codes + (e0 * SB) / 8, true);
+      (void)NB;
     } else {
       using W = Word16<T>;
       FastCoder c0, c1;
       if (AFF) {
-        uint32_t a = W::kPosInf, b = W::kNegInf;
-#pragma unroll
-        for (int i = 0; i < GS; ++i) { a = W::vmin(a, x[i]); b = W::vmax(b, x[i]); }
-        c0 = aff_coder(W::lo(a), W::lo(b), d.qmax, d.rqmax);
-        c1 = aff_coder(W::hi(a), W::hi(b), d.qmax, d.rqmax);
+        c0 = aff_coder(W::lo(cs.a), W::lo(cs.b), d.qmax, d.rqmax);
+        c1 = aff_coder(W::hi(cs.a), W::hi(cs.b), d.qmax, d.rqmax);
       } else {
-        uint32_t a = 0u;
-#pragma unroll
-        for (int i = 0; i < GS; ++i) a = W::amax(a, x[i]);
-        a &= 0x7FFF7FFFu;
-        c0 = sym_coder(W::lo(a), d.qmax, d.rqmax, d.bits, d.packed != 0);
-        c1 = sym_coder(W::hi(a), d.qmax, d.rqmax, d.bits, d.packed != 0);
+        const uint32_t am = cs.a & 0x7FFF7FFFu;
+        c0 = sym_coder(W::lo(am), d.qmax, d.rqmax, d.bits, d.packed != 0);
+        c1 = sym_coder(W::hi(am), d.qmax, d.rqmax, d.bits, d.packed != 0);
       }
       const int ch = 2 * w;
-      const int64_t gi0 = ((int64_t)gslice * D + ch) * d.groups_row + (tok0 >> d.log2gs);
-      store_scale(d.scales, gi0, d.scale_dtype, c0.scale);
-      store_scale(d.scales, gi0 + d.groups_row, d.scale_dtype, c1.scale);
-      if (AFF) {
-        d.zps[gi0] = (uint8_t)c0.zp;
-        d.zps[gi0 + d.groups_row] = (uint8_t)c1.zp;
+      if (first) {
+        const int64_t gi0 = ((int64_t)gslice * D + ch) * d.groups_row + (gtok >> d.log2gs);
+        store_scale(d.scales, gi0, d.scale_dtype, c0.scale);
+        store_scale(d.scales, gi0 + d.groups_row, d.scale_dtype, c1.scale);
+        if (AFF) {
+          d.zps[gi0] = (uint8_t)c0.zp;
+          d.zps[gi0 + d.groups_row] = (uint8_t)c1.zp;
+        }
       }
       const int64_t e0 = ((int64_t)gslice * D + ch) * d.n_pad + tok0;
-      encode_store_columns<T, SB, AFF, GS>(x, c0, c1, d.codes + (e0 * SB) / 8, d.codes + ((e0 + d.n_pad) * SB) / 8);
+      encode_store_columns<T, SB, AFF, kQRows>(x, c0, c1, d.codes + (e0 * SB) / 8, d.codes + ((e0 + d.n_pad) * SB) / 8);
     }
   }
 }
@@ -321,7 +391,7 @@ __device__ void quant_channels(const TensorDesc& d, const uint8_t* sx, int gslic
   const int u = k % RPR, rb = k / RPR;
   const int rpg = d.gs / RUN;              // runs per group: 1, 2 or 4 (gs >= RUN)
 #pragma unroll 1
-  for (int step = hw; step < STEPS; step += 2) {
+  for (int step = hw; step < STEPS; step += kQWarps) {
     const int r = step * ROWS_STEP + rb * 8 + j;
     const uint8_t* src = sx + r * G::kPitchB + u * (RUN * (int)sizeof(T));
     uint32_t w[NW];
@@ -356,14 +426,14 @@ __device__ void quant_channels(const TensorDesc& d, const uint8_t* sx, int gslic
 // ---------------------------------------------------------------------------
 template <typename T, int D, int SB>
 __device__ __forceinline__ void quant_tile_tokens_sb(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
-                                                     int ht) {
+                                                     uint32_t* xch) {
   const bool aff = d.quantizer == GKV_AFFINE;
   if (d.gs == 64) {
-    if (aff) quant_tokens<T, D, 64, SB, true>(d, sx, gslice, j0, ht);
-    else quant_tokens<T, D, 64, SB, false>(d, sx, gslice, j0, ht);
+    if (aff) quant_tokens<T, D, 64, SB, true>(d, sx, gslice, j0, xch);
+    else quant_tokens<T, D, 64, SB, false>(d, sx, gslice, j0, xch);
   } else {
-    if (aff) quant_tokens<T, D, 32, SB, true>(d, sx, gslice, j0, ht);
-    else quant_tokens<T, D, 32, SB, false>(d, sx, gslice, j0, ht);
+    if (aff) quant_tokens<T, D, 32, SB, true>(d, sx, gslice, j0, xch);
+    else quant_tokens<T, D, 32, SB, false>(d, sx, gslice, j0, xch);
   }
 }
 
@@ -487,82 +557,43 @@ __device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr
   return d.axis == AXIS ? 2 : 0;                     // 2: quantize
 }
 
-// Persistent blocks over the tiles of one tensor (`tensor` 1: values, 0: keys),
-// compiled per grouping axis (AXIS): tiles of a tier grouped along the other
-// axis are left to the other kernel; retained-row tiles are copied when
-// `copy_retained`.  Two staging buffers: while a tile is quantized, the rows of
-// the block's next tile are in flight (one asynchronous-copy group per tile).
+// One block per tile of one tensor (`tensor` 1: values, 0: keys), compiled per
+// grouping axis (AXIS): tiles of a tier grouped along the other axis are left
+// to the other kernel; retained-row tiles are copied when `copy_retained`.
+// Many small blocks per SM: while some wait for their rows, others compute.
 template <typename T, int D, int AXIS>
-__global__ void __launch_bounds__(kQThreads, 6) quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor,
-                                                                     int copy_retained, int total_tiles) {
+__global__ void __launch_bounds__(kQThreads, AXIS == GKV_AXIS_TOKEN ? 7 : 5)
+    quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
-  // tiles of this block that the launch handles: cur, nxt (staged one ahead),
-  // and the one after (its row indices are loaded one ahead of staging)
-  auto next_tile = [&](int from, int& role_out) {
-    int t = from;
-    role_out = 0;
-    for (; t < total_tiles; t += gridDim.x)
-      if ((role_out = tile_role<AXIS>(p, tile_ref(p, t), tensor, copy_retained)) != 0) break;
-    return t;
-  };
-  int role, nrole;
-  int cur = next_tile(blockIdx.x, role);
-  int nxt = next_tile(cur + gridDim.x, nrole);
-  int buf = 0;
-  if (cur < total_tiles && role == 2) {
-    const TileRef tr = tile_ref(p, cur);
-    int64_t st;
-    const T* base = tensor_base<T>(p, tr.s, tensor, st);
-    stage_tile<T, D>(p, tr, base, st, smem, tile_tokens<T, D>(p, tr));
+  const TileRef tr = tile_ref(p, blockIdx.x);
+  const int role = tile_role<AXIS>(p, tr, tensor, copy_retained);
+  if (role == 0) return;
+  const int gslice = p.slice_offset + tr.s;
+  int64_t st;
+  const T* base = tensor_base<T>(p, tr.s, tensor, st);
+  if (role == 1) {
+    copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
+    return;
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  int ntok = (nxt < total_tiles && nrole == 2) ? tile_tokens<T, D>(p, tile_ref(p, nxt)) : 0;
-  while (cur < total_tiles) {
-    int nrole2;
-    const int nxt2 = next_tile(nxt + gridDim.x, nrole2);
-    if (nxt < total_tiles && nrole == 2) {
-      const TileRef tn = tile_ref(p, nxt);
-      int64_t st;
-      const T* base = tensor_base<T>(p, tn.s, tensor, st);
-      stage_tile<T, D>(p, tn, base, st, smem + (buf ^ 1) * G::kSmem, ntok);
+  stage_tile<T, D>(p, tr, base, st, smem, tile_tokens<T, D>(p, tr));
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+  const int j0 = tr.k * kQTile;
+  if constexpr (AXIS == GKV_AXIS_TOKEN) {
+    if (d.rotation) {
+      rotate_rows_smem<T, D>(reinterpret_cast<T*>(smem), p.had_div, p.had_inv, threadIdx.x >> 5);
+      __syncthreads();
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    const int ntok2 = (nxt2 < total_tiles && nrole2 == 2) ? tile_tokens<T, D>(p, tile_ref(p, nxt2)) : 0;
-    const TileRef tr = tile_ref(p, cur);
-    const int gslice = p.slice_offset + tr.s;
-    int64_t st;
-    const T* base = tensor_base<T>(p, tr.s, tensor, st);
-    if (role == 1) {
-      copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
-    } else {
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-      __syncthreads();  // every thread's rows of this tile have landed
-      uint8_t* sx = smem + buf * G::kSmem;
-      const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-      const int j0 = tr.k * kQTile;
-      const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-      if constexpr (AXIS == GKV_AXIS_TOKEN) {
-        if (d.rotation) {
-          rotate_rows_smem<T, D>(reinterpret_cast<T*>(sx), p.had_div, p.had_inv, threadIdx.x >> 5);
-          __syncthreads();
-        }
-        if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, sx, gslice, j0, threadIdx.x);
-        else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, sx, gslice, j0, threadIdx.x);
-        else quant_tile_tokens_sb<T, D, 8>(d, sx, gslice, j0, threadIdx.x);
-      } else {
-        quant_tile_channels<T, D>(d, sx, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
-      }
-    }
-    __syncthreads();  // this buffer is refilled from the next iteration on
-    cur = nxt;
-    role = nrole;
-    nxt = nxt2;
-    nrole = nrole2;
-    ntok = ntok2;
-    buf ^= 1;
+    uint32_t* xch = reinterpret_cast<uint32_t*>(smem + G::kTileBytes);
+    if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, smem, gslice, j0, xch);
+    else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, smem, gslice, j0, xch);
+    else quant_tile_tokens_sb<T, D, 8>(d, smem, gslice, j0, xch);
+  } else {
+    const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+    quant_tile_channels<T, D>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -729,11 +760,10 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 // ---------------------------------------------------------------------------
 
 // Per tensor (keys, values): one launch per grouping axis its tiers use; the
-// first of them also copies the tensor's retained rows.  Persistent grid: as
-// many blocks as fit on the device at once, at most one per tile.
+// first of them also copies the tensor's retained rows.
 template <typename T, int D>
 static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
-  const size_t sm = 2 * QGeom<T, D>::kSmem;
+  const size_t sm = QGeom<T, D>::kSmem;
   const int64_t tiles = (int64_t)p.S * p.tiles_slice;
   if (tiles == 0) return cudaSuccess;
   cudaError_t e;
@@ -741,12 +771,6 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
   auto kch = quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>;
   if ((e = cudaFuncSetAttribute(ktok, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(kch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess) return e;
-  int occ_tok = 0, occ_ch = 0;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_tok, ktok, kQThreads, sm)) != cudaSuccess) return e;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_ch, kch, kQThreads, sm)) != cudaSuccess) return e;
-  const int sms = device_sm_count();
-  const unsigned g_tok = (unsigned)std::min<int64_t>(tiles, (int64_t)sms * std::max(occ_tok, 1));
-  const unsigned g_ch = (unsigned)std::min<int64_t>(tiles, (int64_t)sms * std::max(occ_ch, 1));
   for (int tensor = 0; tensor < 2; ++tensor) {
     bool token = false, channel = false;
     for (int tier = 1; tier <= 2; ++tier) {
@@ -755,8 +779,8 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
       (d.axis == GKV_AXIS_TOKEN ? token : channel) = true;
     }
     if (!token && !channel) channel = true;  // retained rows only
-    if (token) ktok<<<g_tok, kQThreads, sm, st>>>(p, tensor, 1, (int)tiles);
-    if (channel) kch<<<g_ch, kQThreads, sm, st>>>(p, tensor, token ? 0 : 1, (int)tiles);
+    if (token) ktok<<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, 1);
+    if (channel) kch<<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, token ? 0 : 1);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
