@@ -265,31 +265,27 @@ __device__ void tok_decode(const TensorDesc& d, int s, int j0, uint8_t* tile) {
   }
 }
 
-template <typename T, int D, int RUN>
+template <typename T, int D, int RUN, bool ROT>
 __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows,
                                                 const int* toks, T* out) {
-  if (d.rotation) {
-    if (d.sbits == 4) chan_decode<T, D, RUN, 4, true>(p, d, s, j0, rows, toks, out);
-    else if (d.sbits == 2) chan_decode<T, D, RUN, 2, true>(p, d, s, j0, rows, toks, out);
-    else chan_decode<T, D, RUN, 8, true>(p, d, s, j0, rows, toks, out);
-  } else {
-    if (d.sbits == 4) chan_decode<T, D, RUN, 4, false>(p, d, s, j0, rows, toks, out);
-    else if (d.sbits == 2) chan_decode<T, D, RUN, 2, false>(p, d, s, j0, rows, toks, out);
-    else chan_decode<T, D, RUN, 8, false>(p, d, s, j0, rows, toks, out);
-  }
+  if (d.sbits == 4) chan_decode<T, D, RUN, 4, ROT>(p, d, s, j0, rows, toks, out);
+  else if (d.sbits == 2) chan_decode<T, D, RUN, 2, ROT>(p, d, s, j0, rows, toks, out);
+  else chan_decode<T, D, RUN, 8, ROT>(p, d, s, j0, rows, toks, out);
 }
 
-// One block per tile of one tensor (`tensor` 1: values, 0: keys), compiled per
-// grouping axis; retained-row tiles are copied when `copy_retained`.
-template <typename T, int D, int AXIS>
-__global__ void __launch_bounds__(kDThreads, AXIS == GKV_AXIS_TOKEN ? 7 : 5)
+// One block per tile of one tensor (`tensor` 1: values, 0: keys).  Compiled per
+// grouping axis and rotation (channel axis only: rotated token-axis tensors take
+// the general path); a launch covers the tiers that use its variant, and the
+// retained rows when `copy_retained`.
+template <typename T, int D, int AXIS, bool ROT>
+__global__ void __launch_bounds__(kDThreads, AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7))
     dequantize_tile_kernel(const __grid_constant__ DequantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = DGeom<T, D>;
   const DTileRef tr = dtile_ref(p, blockIdx.x);
   if (tr.tier == 0 && !copy_retained) return;
   const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-  if (tr.tier != 0 && d.axis != AXIS) return;
+  if (tr.tier != 0 && (d.axis != AXIS || (d.rotation != 0) != ROT)) return;
   T* out = reinterpret_cast<T*>(tensor ? p.out_v : p.out_k) + (int64_t)tr.s * p.T * D;
   if (tr.tier == 0) {
     // retained rows: thread = (16-byte chunk, rows r0, r0 + STEP, ...), loads before stores
@@ -339,11 +335,12 @@ __global__ void __launch_bounds__(kDThreads, AXIS == GKV_AXIS_TOKEN ? 7 : 5)
   } else {
     __syncthreads();
     constexpr int RUN = G::kRun;
-    if (d.gs < RUN || d.rotation) {
-      if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) chan_decode_any<T, D, RUN / 2>(p, d, tr.s, j0, rows, toks, out);
-      else chan_decode_any<T, D, RUN>(p, d, tr.s, j0, rows, toks, out);
+    // rotated runs are half as long: 32 fp32 values per thread in the butterflies
+    if (d.gs < RUN || ROT) {
+      if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) chan_decode_any<T, D, RUN / 2, ROT>(p, d, tr.s, j0, rows, toks, out);
+      else chan_decode_any<T, D, RUN, ROT>(p, d, tr.s, j0, rows, toks, out);
     } else {
-      chan_decode_any<T, D, RUN>(p, d, tr.s, j0, rows, toks, out);
+      chan_decode_any<T, D, RUN, ROT>(p, d, tr.s, j0, rows, toks, out);
     }
   }
 }
@@ -417,32 +414,42 @@ __global__ void general_dequant_retained_kernel(const __grid_constant__ DequantP
   reinterpret_cast<T*>(p.out_v)[o] = reinterpret_cast<const T*>(p.ret_v)[i];
 }
 
-// ---------------------------------------------------------------------------
-// host-side launchers
-// ---------------------------------------------------------------------------
+template <typename T, int D, int AXIS, bool ROT>
+static cudaError_t launch_dq_variant(const DequantParams& p, int tensor, bool retained, bool standard, bool cold,
+                                     cudaStream_t st) {
+  using G = DGeom<T, D>;
+  const DequantParams q = tiers_only(p, retained, standard, cold);
+  const int64_t tiles = (int64_t)q.S * q.tiles_slice;
+  if (tiles == 0) return cudaSuccess;
+  const size_t sm = (AXIS == GKV_AXIS_TOKEN ? G::kTile : 0) + kDTile * sizeof(int);
+  auto kern = dequantize_tile_kernel<T, D, AXIS, ROT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  kern<<<(unsigned)tiles, kDThreads, sm, st>>>(q, tensor, retained ? 1 : 0);
+  return cudaGetLastError();
+}
+
 template <typename T, int D>
 static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st) {
-  using G = DGeom<T, D>;
-  const int64_t tiles = (int64_t)p.S * p.tiles_slice;
-  if (tiles == 0) return cudaSuccess;
-  const size_t sm_ch = kDTile * sizeof(int);
-  const size_t sm_tok = G::kTile + kDTile * sizeof(int);
-  auto ktok = dequantize_tile_kernel<T, D, GKV_AXIS_TOKEN>;
-  auto kch = dequantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>;
-  cudaError_t e;
-  if ((e = cudaFuncSetAttribute(ktok, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_tok)) != cudaSuccess)
-    return e;
+  if ((int64_t)p.S * p.tiles_slice == 0) return cudaSuccess;
   for (int tensor = 0; tensor < 2; ++tensor) {
-    bool token = false, channel = false;
-    for (int tier = 1; tier <= 2; ++tier) {
-      if (p.tiles[tier] == 0) continue;
-      const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-      (d.axis == GKV_AXIS_TOKEN ? token : channel) = true;
+    const int v1 = p.tiles[1] ? tier_variant(p.t[GKV_STD_K + tensor]) : -1;
+    const int v2 = p.tiles[2] ? tier_variant(p.t[GKV_COLD_K + tensor]) : -1;
+    bool retained = p.tiles[0] > 0;
+    for (int v = 0; v < 4; ++v) {
+      const bool standard = v1 == v, cold = v2 == v;
+      const bool ret_here = retained && (standard || cold || (v1 < 0 && v2 < 0 && v == 2));
+      if (!standard && !cold && !ret_here) continue;
+      cudaError_t e;
+      switch (v) {
+        case 0: e = launch_dq_variant<T, D, GKV_AXIS_TOKEN, false>(p, tensor, ret_here, standard, cold, st); break;
+        case 2: e = launch_dq_variant<T, D, GKV_AXIS_CHANNEL, false>(p, tensor, ret_here, standard, cold, st); break;
+        case 3: e = launch_dq_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st); break;
+        default: e = cudaErrorInvalidConfiguration; break;  // rotated token axis: general path only
+      }
+      if (e != cudaSuccess) return e;
+      if (ret_here) retained = false;
     }
-    if (!token && !channel) channel = true;  // retained rows only
-    if (token) ktok<<<(unsigned)tiles, kDThreads, sm_tok, st>>>(p, tensor, 1);
-    if (channel) kch<<<(unsigned)tiles, kDThreads, sm_ch, st>>>(p, tensor, token ? 0 : 1);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }

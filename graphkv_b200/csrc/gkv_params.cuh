@@ -109,6 +109,22 @@ struct DequantParams {
   FastDiv tile_div;  // by tiles_slice
 };
 
+// Params restricted to some tiers: the tile counts of the others are zeroed, so
+// a launch's blocks map onto exactly the included tiers' tiles.
+template <typename P>
+P tiers_only(const P& p, bool retained, bool standard, bool cold) {
+  P q = p;
+  q.tiles[0] = retained ? p.tiles[0] : 0;
+  q.tiles[1] = standard ? p.tiles[1] : 0;
+  q.tiles[2] = cold ? p.tiles[2] : 0;
+  q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
+  q.tile_div = make_fastdiv((uint32_t)(q.tiles_slice > 0 ? q.tiles_slice : 1));
+  return q;
+}
+
+// Variant of a tier's tensor: 2 * axis + rotation (0..3).
+inline int tier_variant(const TensorDesc& d) { return 2 * d.axis + (d.rotation ? 1 : 0); }
+
 // Slice -> layer lookup (layers sorted by slice_begin).
 __device__ __forceinline__ int find_layer(const QuantParams& p, int s) {
   if (p.layer_div.d) return (int)p.layer_div.div((uint32_t)s);

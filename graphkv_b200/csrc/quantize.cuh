@@ -437,34 +437,28 @@ __device__ __forceinline__ void quant_tile_tokens_sb(const TensorDesc& d, const 
   }
 }
 
-template <typename T, int D, int RUN, int SB>
+template <typename T, int D, int RUN, int SB, bool ROT>
 __device__ __forceinline__ void quant_tile_channels_sb(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
                                                        int rows, int ht, float div, float rdiv, bool fused) {
-  const bool aff = d.quantizer == GKV_AFFINE;
-  if (d.rotation) {
-    if (aff) quant_channels<T, D, RUN, SB, true, true>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-    else quant_channels<T, D, RUN, SB, false, true>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-  } else {
-    if (aff) quant_channels<T, D, RUN, SB, true, false>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-    else quant_channels<T, D, RUN, SB, false, false>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-  }
+  if (d.quantizer == GKV_AFFINE) quant_channels<T, D, RUN, SB, true, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+  else quant_channels<T, D, RUN, SB, false, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
 }
 
-template <typename T, int D>
+template <typename T, int D, bool ROT>
 __device__ __forceinline__ void quant_tile_channels(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
                                                     int rows, int ht, float div, float rdiv, bool fused) {
   // run = 128 bytes, or half of that when the group is smaller
   constexpr int RUN = QGeom<T, D>::kRun;
   if (d.gs < RUN) {
     if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) {
-      if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN / 2, 4>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-      else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN / 2, 2>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-      else quant_tile_channels_sb<T, D, RUN / 2, 8>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+      if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN / 2, 4, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+      else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN / 2, 2, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+      else quant_tile_channels_sb<T, D, RUN / 2, 8, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
     }
   } else {
-    if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN, 4>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-    else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN, 2>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
-    else quant_tile_channels_sb<T, D, RUN, 8>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    if (d.sbits == 4) quant_tile_channels_sb<T, D, RUN, 4, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    else if (d.sbits == 2) quant_tile_channels_sb<T, D, RUN, 2, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    else quant_tile_channels_sb<T, D, RUN, 8, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
   }
 }
 
@@ -557,18 +551,21 @@ __device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr
   return d.axis == AXIS ? 2 : 0;                     // 2: quantize
 }
 
-// One block per tile of one tensor (`tensor` 1: values, 0: keys), compiled per
-// grouping axis (AXIS): tiles of a tier grouped along the other axis are left
-// to the other kernel; retained-row tiles are copied when `copy_retained`.
+// One block per tile of one tensor (`tensor` 1: values, 0: keys).  Compiled per
+// grouping axis (AXIS) and rotation (ROT), so that each variant keeps only the
+// registers it needs; a launch covers the tiers that use its variant (the host
+// zeroes the tile counts of the others) and the retained rows when `copy_retained`.
 // Many small blocks per SM: while some wait for their rows, others compute.
-template <typename T, int D, int AXIS>
-__global__ void __launch_bounds__(kQThreads, AXIS == GKV_AXIS_TOKEN ? 7 : 5)
+template <typename T, int D, int AXIS, bool ROT>
+__global__ void __launch_bounds__(kQThreads, AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7))
     quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
   const TileRef tr = tile_ref(p, blockIdx.x);
   const int role = tile_role<AXIS>(p, tr, tensor, copy_retained);
   if (role == 0) return;
+  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+  if (role == 2 && (d.rotation != 0) != ROT) return;  // not this variant's tier
   const int gslice = p.slice_offset + tr.s;
   int64_t st;
   const T* base = tensor_base<T>(p, tr.s, tensor, st);
@@ -579,10 +576,9 @@ __global__ void __launch_bounds__(kQThreads, AXIS == GKV_AXIS_TOKEN ? 7 : 5)
   stage_tile<T, D>(p, tr, base, st, smem, tile_tokens<T, D>(p, tr));
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
   const int j0 = tr.k * kQTile;
   if constexpr (AXIS == GKV_AXIS_TOKEN) {
-    if (d.rotation) {
+    if constexpr (ROT) {
       rotate_rows_smem<T, D>(reinterpret_cast<T*>(smem), p.had_div, p.had_inv, threadIdx.x >> 5);
       __syncthreads();
     }
@@ -592,7 +588,7 @@ __global__ void __launch_bounds__(kQThreads, AXIS == GKV_AXIS_TOKEN ? 7 : 5)
     else quant_tile_tokens_sb<T, D, 8>(d, smem, gslice, j0, xch);
   } else {
     const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-    quant_tile_channels<T, D>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
+    quant_tile_channels<T, D, ROT>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
   }
 }
 
@@ -759,29 +755,43 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 // host-side launchers (called from capi.cu)
 // ---------------------------------------------------------------------------
 
-// Per tensor (keys, values): one launch per grouping axis its tiers use; the
+// Per tensor (keys, values): one launch per kernel variant its tiers need; the
 // first of them also copies the tensor's retained rows.
+template <typename T, int D, int AXIS, bool ROT>
+static cudaError_t launch_variant(const QuantParams& p, int tensor, bool retained, bool standard, bool cold,
+                                  cudaStream_t st) {
+  const QuantParams q = tiers_only(p, retained, standard, cold);
+  const int64_t tiles = (int64_t)q.S * q.tiles_slice;
+  if (tiles == 0) return cudaSuccess;
+  const size_t sm = QGeom<T, D>::kSmem;
+  auto kern = quantize_tile_kernel<T, D, AXIS, ROT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  kern<<<(unsigned)tiles, kQThreads, sm, st>>>(q, tensor, retained ? 1 : 0);
+  return cudaGetLastError();
+}
+
 template <typename T, int D>
 static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
-  const size_t sm = QGeom<T, D>::kSmem;
-  const int64_t tiles = (int64_t)p.S * p.tiles_slice;
-  if (tiles == 0) return cudaSuccess;
-  cudaError_t e;
-  auto ktok = quantize_tile_kernel<T, D, GKV_AXIS_TOKEN>;
-  auto kch = quantize_tile_kernel<T, D, GKV_AXIS_CHANNEL>;
-  if ((e = cudaFuncSetAttribute(ktok, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(kch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) != cudaSuccess) return e;
+  if ((int64_t)p.S * p.tiles_slice == 0) return cudaSuccess;
   for (int tensor = 0; tensor < 2; ++tensor) {
-    bool token = false, channel = false;
-    for (int tier = 1; tier <= 2; ++tier) {
-      if (p.tiles[tier] == 0) continue;
-      const TensorDesc& d = p.t[(tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-      (d.axis == GKV_AXIS_TOKEN ? token : channel) = true;
+    const int v1 = p.tiles[1] ? tier_variant(p.t[GKV_STD_K + tensor]) : -1;
+    const int v2 = p.tiles[2] ? tier_variant(p.t[GKV_COLD_K + tensor]) : -1;
+    bool retained = p.tiles[0] > 0;  // copied by the first launch of this tensor
+    for (int v = 0; v < 4; ++v) {
+      const bool standard = v1 == v, cold = v2 == v;
+      const bool ret_here = retained && (standard || cold || (v1 < 0 && v2 < 0 && v == 2));
+      if (!standard && !cold && !ret_here) continue;
+      cudaError_t e;
+      switch (v) {
+        case 0: e = launch_variant<T, D, GKV_AXIS_TOKEN, false>(p, tensor, ret_here, standard, cold, st); break;
+        case 1: e = launch_variant<T, D, GKV_AXIS_TOKEN, true>(p, tensor, ret_here, standard, cold, st); break;
+        case 2: e = launch_variant<T, D, GKV_AXIS_CHANNEL, false>(p, tensor, ret_here, standard, cold, st); break;
+        default: e = launch_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st); break;
+      }
+      if (e != cudaSuccess) return e;
+      if (ret_here) retained = false;
     }
-    if (!token && !channel) channel = true;  // retained rows only
-    if (token) ktok<<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, 1);
-    if (channel) kch<<<(unsigned)tiles, kQThreads, sm, st>>>(p, tensor, token ? 0 : 1);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }

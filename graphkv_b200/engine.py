@@ -3,9 +3,10 @@
 ``CompressionEngine(pairs, config, scores)`` resolves the policy, allocates the
 device arena of every stored tensor and the dequantized outputs, and builds the
 C plans once.  Each ``quantize()`` then issues, per run of same-shaped layers,
-one selection launch and two quantize launches (keys, values) per 40 layers;
-``dequantize()`` issues one dequantize launch -- no allocation, no Python object
-construction.  The
+one selection launch and, per 40 layers, one quantize launch per kernel variant
+(grouping axis x rotation) that each tensor's tiers use -- keys: one; values:
+two when the cold tier is rotated; ``dequantize()`` issues the same number of
+dequantize launches -- no allocation, no Python object construction.  The
 inputs are read at their current addresses on every call, so callers refill
 them in place (e.g. a serving loop that compresses caches of one shape).
 
@@ -43,14 +44,24 @@ class CompressionEngine:
         return [it[1] for it in self.items if it[0] == "run"]
 
     def launches_per_step(self) -> int:
-        """Kernel launches of one quantize() + dequantize() (for the fast path of every run)."""
+        """Kernel launches of one quantize() + dequantize() (for the fast path of every run):
+        per tensor, one tile launch per distinct (axis, rotation) among its non-empty tiers."""
         n = 0
         for it in self.items:
             if it[0] != "run":
                 continue
             run = it[1]
+            plan = run.plan
+            variants = 0
+            for tensor in range(2):
+                kinds = set()
+                for tier, count in ((0, plan.n_standard), (2, plan.n_cold)):
+                    if count > 0:
+                        spec = plan.spec[tier + tensor]
+                        kinds.add((spec.axis, bool(spec.rotation)))
+                variants += max(1, len(kinds))
             chunks = -(-len(run.pairs) // 40)  # gkv_quantize splits calls into 40-layer launches
-            n += (1 if it[3] else 0) + (1 if run.outlier is not None else 0) + 2 * chunks + 1
+            n += (1 if it[3] else 0) + (1 if run.outlier is not None else 0) + variants * chunks + variants
         return n
 
     def quantize(self) -> None:
