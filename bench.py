@@ -191,20 +191,6 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def shard_units(layers, heads, world, rank):
-    """Contiguous range of (layer, kv-head) units of one rank -> [(layer, h0, h1), ...]."""
-    units = layers * heads
-    lo, hi = units * rank // world, units * (rank + 1) // world
-    out = []
-    u = lo
-    while u < hi:
-        l, h0 = divmod(u, heads)
-        h1 = min(heads, h0 + (hi - u))
-        out.append((l, h0, h1))
-        u += h1 - h0
-    return out
-
-
 def measured_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -246,8 +232,8 @@ def run_ours(args):
 
     import graphkv_b200 as g
     from graphkv_b200 import _lib
-    from graphkv_b200.config import layer_memory_bytes, resolve_tiers, tensor_plans
     from graphkv_b200.engine import CompressionEngine
+    from graphkv_b200.sharding import combine_stats, shard_bytes, shard_stats, shard_units
     from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
 
     w = WORKLOADS[args.workload]
@@ -259,14 +245,12 @@ def run_ours(args):
     scores = make_scores(w, device=str(dev))
     cfg = g.get_profile(w.profile).config
     in_bytes = sum(k.numel() * k.element_size() * 2 for k, _ in pairs)
-    comp_bytes = 0
-    for k, _ in pairs:
-        t = resolve_tiers(cfg, k.shape[2], scores is not None)
-        comp_bytes += layer_memory_bytes(tuple(k.shape), k.dtype, t, tensor_plans(cfg, tuple(k.shape), t))
+    comp_bytes = sum(shard_bytes(tuple(k.shape), k.dtype, cfg, scores is not None, h0)[0]
+                     for (k, _), (_, h0, _) in zip(pairs, shard))
     eng = CompressionEngine(pairs, cfg, scores)
     runs = eng.runs
     launches = eng.launches_per_step()
-    stats_vec = torch.tensor([float(comp_bytes), float(in_bytes)], device=dev, dtype=torch.float64)
+    stats_vec = shard_stats(comp_bytes, in_bytes, device=dev)
     gathered = torch.empty(world * 2, device=dev, dtype=torch.float64)
 
     stream = torch.cuda.current_stream(dev)
@@ -412,6 +396,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": args.steps * launches,
+        "cache_stats": combine_stats(gathered.cpu()) if world > 1 else None,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
