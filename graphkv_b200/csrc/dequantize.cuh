@@ -66,11 +66,12 @@ __device__ __forceinline__ int load_zp(const TensorDesc& d, int64_t gi) {
 // codes, scales and output rows straight into registers (the other resident
 // warps cover the latency).
 //  - channel-axis groups (V): item = (row, run of 128 bytes of output), lanes
-//    mapped as in the quantizer (runs of a row 8 lanes apart); decoded, optionally
-//    rotated in registers, and stored as 16-byte vectors at the output row;
+//    mapped as in the quantizer (runs of a row 8 lanes apart); decoded and
+//    optionally rotated in registers;
 //  - token-axis groups (K): item = (column word, run of 32 rows); decoded
-//    column-wise into a shared [64][D] tile whose rows then leave as 16-byte
-//    vectors.
+//    column-wise;
+// both into a shared [64][D] tile whose rows then leave as 16-byte vectors, 16
+// lanes per row (whole 32-byte sectors per store instruction).
 // ---------------------------------------------------------------------------
 constexpr int kDThreads = 128;
 constexpr int kDWarps = kDThreads / 32;
@@ -142,8 +143,7 @@ __device__ __forceinline__ void load_tile_rows(const DequantParams& p, const DTi
 
 // ---- channel axis ---------------------------------------------------------
 template <typename T, int D, int RUN, int SB, bool ROT>
-__device__ void chan_decode(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows, const int* toks,
-                            T* out) {
+__device__ void chan_decode(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows, uint8_t* tile) {
   constexpr int RPR = D / RUN;
   constexpr int ROWS_STEP = 32 / RPR;
   constexpr int STEPS = kDTile / ROWS_STEP;
@@ -173,15 +173,39 @@ __device__ void chan_decode(const DequantParams& p, const TensorDesc& d, int s, 
     const Decoder dc = make_decoder(d, scale, zp);
     const uint64_t base2 = pk2(dc.base, dc.base), sc2 = pk2(dc.scale, dc.scale);
     const uint32_t xm = SB == 8 ? dc.xor_mask : 0u;  // only unpacked symmetric codes flip
-    uint64_t v[RUN / 2];
+    uint4* dst = reinterpret_cast<uint4*>(tile + r * DGeom<T, D>::kPitchB + u * RUN * (int)sizeof(T));
+    if constexpr (!ROT) {
+      // decode and write 16 bytes of output at a time (few live registers)
+      constexpr int OC = 16 / (int)sizeof(T);  // output elements per 16-byte store
 #pragma unroll
-    for (int q = 0; q < NC; ++q) {
-      uint32_t c[EPC];
-      word_codes<SB>(cw[q], c);
+      for (int o = 0; o < RUN / OC; ++o) {
+        uint32_t c[OC];
 #pragma unroll
-      for (int e = 0; e < EPC; e += 2) v[(q * EPC + e) / 2] = decode_pair(c[e], c[e + 1], xm, xm, base2, sc2);
-    }
-    if constexpr (ROT) {
+        for (int q = 0; q < (OC + EPC - 1) / EPC; ++q) {  // the code words covering this chunk
+          const int e0 = o * OC + q * EPC;
+          uint32_t all[EPC];
+          word_codes<SB>(cw[e0 / EPC], all);
+#pragma unroll
+          for (int e = 0; e < (EPC < OC ? EPC : OC); ++e) c[q * EPC + e] = all[(e0 % EPC) + e];
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < OC; e += 2) {
+          const uint64_t v2 = decode_pair(c[e], c[e + 1], xm, xm, base2, sc2);
+          if constexpr (sizeof(T) == 4) { w[e] = (uint32_t)v2; w[e + 1] = (uint32_t)(v2 >> 32); }
+          else w[e / 2] = out_word<T>(v2);
+        }
+        dst[o] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+      uint64_t v[RUN / 2];
+#pragma unroll
+      for (int q = 0; q < NC; ++q) {
+        uint32_t c[EPC];
+        word_codes<SB>(cw[q], c);
+#pragma unroll
+        for (int e = 0; e < EPC; e += 2) v[(q * EPC + e) / 2] = decode_pair(c[e], c[e + 1], xm, xm, base2, sc2);
+      }
       // Decoded values are integer multiples of a stored scale (>= 2^-24 when
       // nonzero), so every nonzero butterfly output is far above the fused
       // quotient's 2^-100 bound.  -0 needs a zero scale (a group that underflowed
@@ -189,10 +213,6 @@ __device__ void chan_decode(const DequantParams& p, const TensorDesc& d, int s, 
       // exactly.  (Padding lanes hold scale 0 but only zeros: they do not vote.)
       const bool fused = (p.had_fused != 0) && __all_sync(kFull, !act || (dc.scale != 0.f && isfinite(dc.scale)));
       rotate_run<RUN, RPR, false>(v, u, p.had_div, p.had_inv, fused);
-    }
-    const int tok = act ? toks[r] : -1;
-    if (tok >= 0) {
-      uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)tok * D + u * RUN);
       if constexpr (sizeof(T) == 4) {
 #pragma unroll
         for (int q = 0; q < RUN / 2; q += 2)
@@ -267,10 +287,10 @@ __device__ void tok_decode(const TensorDesc& d, int s, int j0, uint8_t* tile) {
 
 template <typename T, int D, int RUN, bool ROT>
 __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows,
-                                                const int* toks, T* out) {
-  if (d.sbits == 4) chan_decode<T, D, RUN, 4, ROT>(p, d, s, j0, rows, toks, out);
-  else if (d.sbits == 2) chan_decode<T, D, RUN, 2, ROT>(p, d, s, j0, rows, toks, out);
-  else chan_decode<T, D, RUN, 8, ROT>(p, d, s, j0, rows, toks, out);
+                                                uint8_t* tile) {
+  if (d.sbits == 4) chan_decode<T, D, RUN, 4, ROT>(p, d, s, j0, rows, tile);
+  else if (d.sbits == 2) chan_decode<T, D, RUN, 2, ROT>(p, d, s, j0, rows, tile);
+  else chan_decode<T, D, RUN, 8, ROT>(p, d, s, j0, rows, tile);
 }
 
 // One block per tile of one tensor (`tensor` 1: values, 0: keys).  Compiled per
@@ -278,7 +298,7 @@ __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const Te
 // the general path); a launch covers the tiers that use its variant, and the
 // retained rows when `copy_retained`.
 template <typename T, int D, int AXIS, bool ROT>
-__global__ void __launch_bounds__(kDThreads, AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7))
+__global__ void __launch_bounds__(kDThreads, ROT ? 5 : 10)
     dequantize_tile_kernel(const __grid_constant__ DequantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = DGeom<T, D>;
@@ -314,34 +334,34 @@ __global__ void __launch_bounds__(kDThreads, AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ?
   }
   const int j0 = tr.k * kDTile;
   const int rows = min(kDTile, p.n_tier[tr.tier] - j0);
-  int* toks = reinterpret_cast<int*>(smem + (AXIS == GKV_AXIS_TOKEN ? G::kTile : 0));
+  uint8_t* tile = smem;
+  int* toks = reinterpret_cast<int*>(smem + G::kTile);
   load_tile_rows(p, tr, j0, rows, toks);
   if constexpr (AXIS == GKV_AXIS_TOKEN) {
-    uint8_t* tile = smem;
     if (d.sbits == 4) tok_decode<T, D, 4>(d, tr.s, j0, tile);
     else if (d.sbits == 2) tok_decode<T, D, 2>(d, tr.s, j0, tile);
     else tok_decode<T, D, 8>(d, tr.s, j0, tile);
-    __syncthreads();
-    // the tile's rows leave as 16-byte vectors: thread = (chunk, rows r0, r0 + STEP, ...)
-    constexpr int CH = G::kRowBytes / 16, STEP = kDThreads / CH;
-    const int c = threadIdx.x % CH, r0 = threadIdx.x / CH;
-#pragma unroll 4
-    for (int i = 0; i < kDTile / STEP; ++i) {
-      const int r = r0 + i * STEP;
-      const int t_out = r < rows ? toks[r] : -1;
-      if (t_out >= 0)
-        reinterpret_cast<uint4*>(out + (int64_t)t_out * D)[c] = *reinterpret_cast<const uint4*>(tile + r * G::kPitchB + c * 16);
-    }
   } else {
-    __syncthreads();
     constexpr int RUN = G::kRun;
     // rotated runs are half as long: 32 fp32 values per thread in the butterflies
     if (d.gs < RUN || ROT) {
-      if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) chan_decode_any<T, D, RUN / 2, ROT>(p, d, tr.s, j0, rows, toks, out);
-      else chan_decode_any<T, D, RUN, ROT>(p, d, tr.s, j0, rows, toks, out);
+      if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) chan_decode_any<T, D, RUN / 2, ROT>(p, d, tr.s, j0, rows, tile);
+      else chan_decode_any<T, D, RUN, ROT>(p, d, tr.s, j0, rows, tile);
     } else {
-      chan_decode_any<T, D, RUN, ROT>(p, d, tr.s, j0, rows, toks, out);
+      chan_decode_any<T, D, RUN, ROT>(p, d, tr.s, j0, rows, tile);
     }
+  }
+  __syncthreads();
+  // the tile's rows leave as 16-byte vectors, 16 lanes per 256-byte row: thread =
+  // (chunk, rows r0, r0 + STEP, ...)
+  constexpr int CH = G::kRowBytes / 16, STEP = kDThreads / CH;
+  const int c = threadIdx.x % CH, r0 = threadIdx.x / CH;
+#pragma unroll 4
+  for (int i = 0; i < kDTile / STEP; ++i) {
+    const int r = r0 + i * STEP;
+    const int t_out = r < rows ? toks[r] : -1;
+    if (t_out >= 0)
+      reinterpret_cast<uint4*>(out + (int64_t)t_out * D)[c] = *reinterpret_cast<const uint4*>(tile + r * G::kPitchB + c * 16);
   }
 }
 
@@ -421,7 +441,7 @@ static cudaError_t launch_dq_variant(const DequantParams& p, int tensor, bool re
   const DequantParams q = tiers_only(p, retained, standard, cold);
   const int64_t tiles = (int64_t)q.S * q.tiles_slice;
   if (tiles == 0) return cudaSuccess;
-  const size_t sm = (AXIS == GKV_AXIS_TOKEN ? G::kTile : 0) + kDTile * sizeof(int);
+  const size_t sm = G::kTile + kDTile * sizeof(int);
   auto kern = dequantize_tile_kernel<T, D, AXIS, ROT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
