@@ -364,7 +364,10 @@ def run_ours(args):
     dom_bytes = (algo_q if dominant == "quantize" else algo_dq) / nr
     achieved = dom_bytes / dom_ms / 1e6
     traffic = committed_traffic(args.workload).get(dominant)
-    roofline = {"bound": "hbm", "kernel": "quantize_tile_kernel" if dominant == "quantize" else "dequantize_tile_kernel",
+    roofline = {"bound": "hbm",
+                "kernel": ("quantize call: quantize_tile_kernel launches (keys, values, rotated cold values)"
+                           if dominant == "quantize" else
+                           "dequantize call: dequantize_tile_kernel launches (keys, values, rotated cold values)"),
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
                 "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes}
