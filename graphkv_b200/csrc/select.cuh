@@ -1,17 +1,25 @@
 // Tier selection (core.py:595-644, 685-719, 1034-1048) and outlier scores
 // (core.py:1051-1054).
 //
-// One block of 1024 threads walks the T tokens.  Each top-k / bottom-k step is an
-// MSB-first radix select over 32-bit order keys of the fp32 scores (4 passes of 8
-// bits, histogram in shared memory with warp-aggregated atomics) that yields the
-// k-th key.  When every candidate equal to that key is taken, the set is unique
-// and an ordered pass marks it.  Otherwise (a tie straddles the boundary) the
-// choice is the one torch.topk makes on the CPU, which follows the order libstdc++
-// visits its queue of candidates: select_exact restates std::partial_sort's heap
-// select (k * 64 <= n) and std::nth_element's introselect on the device.  A final
-// ordered pass compacts the three ascending index lists.  Workspace: one tier byte
-// per token, then the candidate queue and the two partition stop tables (int32).
+// A cluster of 8 blocks of 1024 threads walks the T tokens: block r owns one
+// contiguous range of them, with their order keys and tier bytes in its shared
+// memory.  Each top-k / bottom-k step is an MSB-first radix select over 32-bit
+// order keys of the fp32 scores (digits of 11, 11 and 10 bits): every block counts
+// the digit of its own candidates into a histogram in its shared memory (warp-
+// aggregated atomics), and after a cluster barrier every block reads the eight
+// histograms through distributed shared memory and finds the same bin of the k-th
+// key.  When every candidate equal to that key is taken, the set is unique: "at or
+// beyond the k-th key", marked by the next sweep.  Otherwise (a tie straddles the
+// boundary) the choice is the one torch.topk makes on the CPU, which follows the
+// order libstdc++ visits its queue of candidates: select_exact restates
+// std::partial_sort's heap select (k * 64 <= n) and std::nth_element's introselect,
+// run by block 0 over the tier bytes in global memory.  A final ordered pass
+// compacts the three ascending index lists, each block at the offsets of the
+// blocks before it.  Workspace: one tier byte per token, then the candidate queue
+// and the two partition stop tables (int32).
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "gkv_common.cuh"
 
@@ -21,7 +29,8 @@ namespace {
 
 constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
-constexpr int kSelSmemTokens = 40960;  // keys (4 B) + tier (1 B) per token fit in shared memory
+constexpr int kSelCluster = 8;         // blocks of the selection cluster
+constexpr int kSelSmemTokens = 40960;  // tokens per block whose keys (4 B) and tier (1 B) fit in shared memory
 enum : uint8_t { kCand = 0, kRet = 1, kCold = 2 };
 
 struct SelectParams {
@@ -29,7 +38,7 @@ struct SelectParams {
   const float* outlier;
   int T, sink, tail, keep_protect, keep_outlier, keep_cold;
   int n_ret, n_std, n_cold;
-  uint8_t* tier;  // workspace (used when T exceeds kSelSmemTokens)
+  uint8_t* tier;  // workspace: tier bytes (blocks of more than kSelSmemTokens tokens, exact path)
   int* queue;     // workspace [T]: candidate queue of the exact tie path
   int* stop_l;    // workspace [T]: left stops of a partition, by rank
   int* stop_r;    // workspace [T]: right stops of a partition, by rank
@@ -47,25 +56,41 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+constexpr int kBins = 2048;  // 11-bit digits
+
 struct SelShared {
-  uint32_t hist[256];
+  uint32_t hist[2][kBins];  // alternate digit passes, so a block clears one while peers read the other
   uint32_t warp_cnt[3][kSelWarps];
   uint32_t warp_off[3][kSelWarps];
-  uint32_t prefix, mask, remaining;
+  uint32_t wsum[kSelWarps];
+  uint32_t list_tot[3];   // this block's count of each list
+  uint32_t list_off[3];   // counts of the blocks before it
+  uint32_t list_all[3];   // whole cluster
+  uint32_t pick_bin, pick_rem, pick_cnt;
+  int found;
   // exact tie path
   int first, last, depth, done;
   uint32_t pivot;
   int pairs;
 };
 
-// Tokens handled by warp w in the ordered passes: one contiguous chunk per warp.
+namespace cg = cooperative_groups;
+__device__ __forceinline__ void cluster_sync() { cg::this_cluster().sync(); }
+// The same shared-memory object in block r of the cluster.
+template <class U>
+__device__ __forceinline__ U* peer(U* p, int r) {
+  return cg::this_cluster().map_shared_rank(p, r);
+}
+
+// Tokens handled by warp w in the sweeps of [lo, hi): one contiguous chunk per
+// warp, a multiple of 128 tokens (four 32-token slices per step).
 struct Chunk {
   int begin, end;
 };
-__device__ __forceinline__ Chunk warp_chunk(int T, int w) {
-  const int per = ((T + kSelWarps - 1) / kSelWarps + 31) & ~31;
-  const int b = min(T, w * per);
-  return {b, min(T, b + per)};
+__device__ __forceinline__ Chunk warp_chunk(int lo, int hi, int w) {
+  const int per = ((hi - lo + kSelWarps - 1) / kSelWarps + 127) & ~127;
+  const int b = min(hi, lo + w * per);
+  return {b, min(hi, b + per)};
 }
 
 // Exclusive scan of the per-warp counters (n of them) into warp_off; one barrier pair.
@@ -85,15 +110,19 @@ __device__ __forceinline__ void scan_warp_counts(SelShared& sh, int n) {
   __syncthreads();
 }
 
+// Tokens [base, end) of this block.  SMEM: keys of the importance scores and
+// tier bytes in shared memory, indexed from base; otherwise tier points at the
+// workspace byte of token base and keys are read from the scores.
 template <bool SMEM>
 struct SelState {
-  const uint32_t* keys;  // shared-memory keys (SMEM) of the importance scores
+  uint32_t* keys;
   uint8_t* tier;
+  int base, end;
 };
 
 template <bool SMEM>
 __device__ __forceinline__ uint32_t key_at(const SelState<SMEM>& st, const float* src, int t) {
-  if (SMEM && src == nullptr) return st.keys[t];
+  if (SMEM && src == nullptr) return st.keys[t - st.base];
   return order_key(src[t]);
 }
 
@@ -249,8 +278,9 @@ __device__ __forceinline__ Chunk range_chunk(int lo, int hi, int w) {
   return {b, min(hi, b + per)};
 }
 
-// Mark the k candidates torch.topk would choose.  The candidates are compacted
-// into the queue in position order first.
+// Mark the k candidates torch.topk would choose, by one block over all T tokens
+// (st: tier bytes of [0, T)).  The candidates are compacted into the queue in
+// position order first.
 template <bool SMEM>
 __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, const float* src, int k, bool largest,
                              uint8_t mark, SelShared& sh) {
@@ -259,7 +289,7 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
   const KeyOf<SMEM> key{st, src};
   const Before before{largest};
   // queue of candidates in position order
-  const Chunk ch = warp_chunk(p.T, warp);
+  const Chunk ch = warp_chunk(0, p.T, warp);
   uint32_t cnt = 0;
   for (int b = ch.begin; b < ch.end; b += 32) {
     const int t = b + lane;
@@ -399,165 +429,342 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
   __syncthreads();
 }
 
-// Select `k` candidates (tier == kCand) with the largest (or smallest) keys and
-// give them tier `mark`.  src == nullptr: the importance scores (cached keys).
-template <bool SMEM>
-__device__ void select_mark(const SelectParams& p, const SelState<SMEM>& st, const float* src, int k, bool largest,
-                            uint8_t mark, SelShared& sh) {
+// ---------------------------------------------------------------------------
+// Radix selection.  The k-th key is found one digit at a time from the top
+// (bits [21,32), [10,21), [0,10)): each block counts the digit over its own
+// candidates that match the digits found so far, and after a cluster barrier
+// every block sums the eight histograms and scans them in rank order for the bin
+// holding the k-th candidate.  The count in the last bin is the number of
+// candidates equal to the k-th key, so the tie test needs no pass of its own.
+// Without a tie the selection is "every candidate at or beyond the k-th key";
+// that mark is not written at once but applied by the next sweep (the first
+// digit of the next selection, or the count of the final compaction).
+// ---------------------------------------------------------------------------
+
+// A finished selection whose marks the next sweep applies.
+struct MarkOp {
+  const float* src;  // keys: nullptr = importance scores (cached in SMEM mode)
+  uint32_t tau;      // k-th key
+  uint8_t mark;
+  bool largest;
+  bool on;
+};
+__device__ __forceinline__ MarkOp no_mark() { return MarkOp{nullptr, 0u, 0, false, false}; }
+__device__ __forceinline__ bool takes(const MarkOp& m, uint32_t key) {
+  return m.largest ? key >= m.tau : key <= m.tau;
+}
+
+__device__ __forceinline__ int digit_shift(int d) { return d == 0 ? 21 : (d == 1 ? 10 : 0); }
+__device__ __forceinline__ int digit_bins(int d) { return d == 2 ? 1024 : 2048; }
+// bits above digit d
+__device__ __forceinline__ uint32_t high_mask(int d) { return d == 0 ? 0u : (d == 1 ? 0xFFE00000u : 0xFFFFFC00u); }
+
+// Warp-aggregated histogram increment: one shared atomic per distinct digit.
+__device__ __forceinline__ void hist_add(uint32_t* hist, bool act, uint32_t digit) {
+  const uint32_t am = __ballot_sync(0xFFFFFFFFu, act);
+  if (act) {
+    const uint32_t peers = __match_any_sync(am, digit);
+    if ((threadIdx.x & 31) == (unsigned)(__ffs(peers) - 1)) atomicAdd(&hist[digit], __popc(peers));
+  }
+}
+
+struct BinPick {
+  uint32_t bin, remaining, count;
+  bool found;
+};
+
+// Bin of the rem-th candidate in rank order (descending digits for `largest`)
+// over the cluster's histograms hist[buf], the rank left inside it and its count.
+// Call after the cluster barrier that follows the counting; every block computes
+// the same pick, which returns to every thread.
+__device__ BinPick find_bin(SelShared& sh, int buf, int nbins, uint32_t rem, bool largest) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) { sh.prefix = 0; sh.mask = 0; sh.remaining = (uint32_t)k; }
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int i = threadIdx.x; i < 256; i += kSelThreads) sh.hist[i] = 0;
-    __syncthreads();
-    const uint32_t prefix = sh.prefix, mask = sh.mask;
-    for (int base = 0; base < p.T; base += kSelThreads) {
-      const int t = base + threadIdx.x;
-      bool act = false;
-      uint32_t digit = 0;
-      if (t < p.T && st.tier[t] == kCand) {
-        const uint32_t key = key_at<SMEM>(st, src, t);
-        if ((key & mask) == prefix) {
-          act = true;
-          digit = (key >> shift) & 0xFFu;
-        }
-      }
-      const uint32_t am = __ballot_sync(0xFFFFFFFFu, act);
-      if (act) {
-        const uint32_t peers = __match_any_sync(am, digit);
-        if (lane == (__ffs(peers) - 1)) atomicAdd(&sh.hist[digit], __popc(peers));
-      }
-    }
-    __syncthreads();
-    if (warp == 0) {
-      // lane l owns 8 bins in scan order (descending digits for `largest`)
-      uint32_t c[8], sum = 0;
+  const int per = nbins / kSelThreads;  // 1 or 2 scan positions per thread
+  uint32_t c[2] = {0u, 0u}, sum = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int bin = largest ? 255 - (lane * 8 + j) : lane * 8 + j;
-        c[j] = sh.hist[bin];
-        sum += c[j];
-      }
-      uint32_t inc = sum;
+  for (int j = 0; j < 2; ++j)
+    if (j < per) {
+      const int pos = threadIdx.x * per + j;
+      uint32_t* const h = &sh.hist[buf][largest ? nbins - 1 - pos : pos];
+      uint32_t v[kSelCluster];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-        if (lane >= o) inc += t;
-      }
-      const uint32_t rem = sh.remaining;
-      const uint32_t before = inc - sum;
-      const uint32_t hit = __ballot_sync(0xFFFFFFFFu, before < rem && inc >= rem);
-      if (hit == 0) {
-        // fewer candidates than requested: the count check at the end reports it
-        if (lane == 0) { sh.remaining = rem; sh.prefix = prefix; sh.mask = mask | (0xFFu << shift); }
-      } else if (lane == __ffs(hit) - 1) {
-        uint32_t cum = before;
-        int j = 0;
-        for (; j < 8; ++j) {
-          if (cum + c[j] >= rem) break;
-          cum += c[j];
-        }
-        const int bin = largest ? 255 - (lane * 8 + j) : lane * 8 + j;
-        sh.remaining = rem - cum;
-        sh.prefix = prefix | ((uint32_t)bin << shift);
-        sh.mask = mask | (0xFFu << shift);
-      }
+      for (int r = 0; r < kSelCluster; ++r) v[r] = *peer(h, r);
+#pragma unroll
+      for (int r = 0; r < kSelCluster; ++r) c[j] += v[r];
+      sum += c[j];
     }
-    __syncthreads();
+  uint32_t inc = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += t;
   }
-  const uint32_t tau = sh.prefix;
-  const uint32_t take_eq = sh.remaining;
-  const Chunk ch = warp_chunk(p.T, warp);
-  // pass 1: candidates equal to the k-th key, per warp chunk
-  uint32_t cnt = 0;
-  for (int b = ch.begin; b < ch.end; b += 32) {
-    const int t = b + lane;
-    const bool eq = t < ch.end && st.tier[t] == kCand && key_at<SMEM>(st, src, t) == tau;
-    cnt += __popc(__ballot_sync(0xFFFFFFFFu, eq));
+  if (lane == 31) sh.wsum[warp] = inc;
+  if (threadIdx.x == 0) sh.found = 0;
+  __syncthreads();
+  uint32_t winc = sh.wsum[lane];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, winc, o);
+    if (lane >= o) winc += t;
   }
-  if (lane == 0) sh.warp_cnt[0][warp] = cnt;
-  scan_warp_counts(sh, 1);
-  const uint32_t n_eq = sh.warp_off[0][kSelWarps - 1] + sh.warp_cnt[0][kSelWarps - 1];
-  if (take_eq < n_eq) {  // a tie straddles the boundary
-    select_exact<SMEM>(p, st, src, k, largest, mark, sh);
-    return;
-  }
-  // pass 2: mark keys beyond the k-th and every key equal to it
-  uint32_t running = sh.warp_off[0][warp];
-  for (int b = ch.begin; b < ch.end; b += 32) {
-    const int t = b + lane;
-    bool cand = false, beyond = false, eq = false;
-    if (t < ch.end && st.tier[t] == kCand) {
-      cand = true;
-      const uint32_t key = key_at<SMEM>(st, src, t);
-      beyond = largest ? key > tau : key < tau;
-      eq = key == tau;
+  const uint32_t wpre = __shfl_sync(0xFFFFFFFFu, winc, (warp + 31) & 31);
+  const uint32_t before = (warp ? wpre : 0u) + inc - sum;
+  if (before < rem && before + sum >= rem) {  // exactly one thread when rem <= total
+    uint32_t cum = before;
+    int j = 0;
+    if (per == 2 && cum + c[0] < rem) {
+      cum += c[0];
+      j = 1;
     }
-    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, eq);
-    const uint32_t pos = running + __popc(bal & ((1u << lane) - 1u));
-    if (cand && (beyond || (eq && pos < take_eq))) st.tier[t] = mark;
-    running += __popc(bal);
+    const int pos = threadIdx.x * per + j;
+    sh.pick_bin = (uint32_t)(largest ? nbins - 1 - pos : pos);
+    sh.pick_rem = rem - cum;
+    sh.pick_cnt = j ? c[1] : c[0];
+    sh.found = 1;
   }
   __syncthreads();
+  return BinPick{sh.pick_bin, sh.pick_rem, sh.pick_cnt, sh.found != 0};
+}
+
+// Sweep of this block's tokens: apply the pending marks `pm`, then count digit d
+// of the candidates' keys (src) that match `prefix` above it into `hist`.  INIT:
+// the sweep also writes the initial tiers (sink and tail retained) and, in SMEM
+// mode, the cached keys of the importance scores.
+template <bool SMEM, bool INIT>
+__device__ void hist_sweep(const SelectParams& p, const SelState<SMEM>& st, uint32_t* hist, const MarkOp& pm,
+                           const float* src, int d, uint32_t prefix) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int shift = digit_shift(d);
+  const uint32_t dmask = (uint32_t)digit_bins(d) - 1u, hmask = high_mask(d);
+  const Chunk ch = warp_chunk(st.base, st.end, warp);
+  for (int b = ch.begin; b < ch.end; b += 4 * 32) {
+    uint8_t tr[4];
+    uint32_t own[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      tr[j] = 0xFF;
+      own[j] = 0u;
+      if (t < ch.end) {
+        if (INIT) {
+          tr[j] = (t < p.sink || t >= p.T - p.tail) ? kRet : kCand;
+          if (SMEM && p.scores) own[j] = order_key(p.scores[t]);
+        } else {
+          tr[j] = st.tier[t - st.base];
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      if (t < ch.end) {
+        if (INIT && SMEM && p.scores) st.keys[t - st.base] = own[j];
+        bool store = INIT;
+        if (pm.on && tr[j] == kCand && takes(pm, key_at<SMEM>(st, pm.src, t))) {
+          tr[j] = pm.mark;
+          store = true;
+        }
+        if (store) st.tier[t - st.base] = tr[j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      bool act = false;
+      uint32_t digit = 0;
+      if (tr[j] == kCand) {
+        const uint32_t key = (INIT && SMEM && src == nullptr && p.scores) ? own[j] : key_at<SMEM>(st, src, t);
+        if ((key & hmask) == prefix) {
+          act = true;
+          digit = (key >> shift) & dmask;
+        }
+      }
+      hist_add(hist, act, digit);
+    }
+  }
+}
+
+// A tie across the boundary: block 0 runs select_exact over the tier bytes of
+// all T tokens in global memory (SMEM mode: every block copies its own out and
+// back around it).
+template <bool SMEM>
+__device__ void exact_on_block0(const SelectParams& p, const SelState<SMEM>& st, SelShared& sh, const float* src,
+                                int k, bool largest, uint8_t mark) {
+  if (SMEM)
+    for (int t = st.base + (int)threadIdx.x; t < st.end; t += kSelThreads) p.tier[t] = st.tier[t - st.base];
+  cluster_sync();
+  if (cg::this_cluster().block_rank() == 0) {
+    const SelState<false> all{nullptr, p.tier, 0, p.T};
+    select_exact<false>(p, all, src ? src : p.scores, k, largest, mark, sh);
+  }
+  cluster_sync();
+  if (SMEM) {
+    for (int t = st.base + (int)threadIdx.x; t < st.end; t += kSelThreads) st.tier[t - st.base] = p.tier[t];
+    __syncthreads();
+  }
+}
+
+// Select the k candidates (tier == kCand) with the largest (smallest) keys of
+// `src` and return their mark for the next sweep; a tie across the boundary is
+// resolved and marked here.  `pm`: the previous selection's pending marks,
+// applied by the first-digit sweep.  `buf`: histogram buffer of the next pass.
+template <bool SMEM>
+__device__ MarkOp select_radix(const SelectParams& p, const SelState<SMEM>& st, SelShared& sh, const MarkOp& pm,
+                               bool init, const float* src, int k, bool largest, uint8_t mark, int& buf) {
+  BinPick bp{0u, (uint32_t)k, 0u, true};
+  uint32_t prefix = 0u;
+  for (int d = 0; d < 3; ++d) {
+    for (int i = threadIdx.x; i < kBins; i += kSelThreads) sh.hist[buf][i] = 0;
+    __syncthreads();
+    if (d == 0 && init) hist_sweep<SMEM, true>(p, st, sh.hist[buf], pm, src, 0, 0u);
+    else hist_sweep<SMEM, false>(p, st, sh.hist[buf], d == 0 ? pm : no_mark(), src, d, prefix);
+    cluster_sync();
+    bp = find_bin(sh, buf, digit_bins(d), bp.remaining, largest);
+    buf ^= 1;
+    // fewer candidates than k: mark all of them; the final count check reports it
+    if (!bp.found) return MarkOp{src, largest ? 0u : 0xFFFFFFFFu, mark, largest, true};
+    prefix |= bp.bin << digit_shift(d);
+  }
+  if (bp.remaining < bp.count) {  // candidates equal to the k-th key straddle the boundary
+    exact_on_block0<SMEM>(p, st, sh, src, k, largest, mark);
+    return no_mark();
+  }
+  return MarkOp{src, prefix, mark, largest, true};
+}
+
+// Apply the last pending marks and write the three ascending index lists.
+template <bool SMEM>
+__device__ void compact_lists(const SelectParams& p, const SelState<SMEM>& st, SelShared& sh, const MarkOp& pm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const Chunk ch = warp_chunk(st.base, st.end, warp);
+  uint32_t n_ret = 0, n_cold = 0, n_all = 0;
+  for (int b = ch.begin; b < ch.end; b += 4 * 32) {
+    uint8_t tr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      tr[j] = t < ch.end ? st.tier[t - st.base] : 0xFF;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      if (pm.on && tr[j] == kCand && takes(pm, key_at<SMEM>(st, pm.src, t))) {
+        tr[j] = pm.mark;
+        st.tier[t - st.base] = tr[j];
+      }
+      n_ret += tr[j] == kRet;
+      n_cold += tr[j] == kCold;
+      n_all += tr[j] != 0xFF;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    n_ret += __shfl_xor_sync(0xFFFFFFFFu, n_ret, o);
+    n_cold += __shfl_xor_sync(0xFFFFFFFFu, n_cold, o);
+    n_all += __shfl_xor_sync(0xFFFFFFFFu, n_all, o);
+  }
+  if (lane == 0) {
+    sh.warp_cnt[0][warp] = n_ret;
+    sh.warp_cnt[1][warp] = n_all - n_ret - n_cold;
+    sh.warp_cnt[2][warp] = n_cold;
+  }
+  scan_warp_counts(sh, 3);
+  if (threadIdx.x < 3) sh.list_tot[threadIdx.x] = sh.warp_off[threadIdx.x][kSelWarps - 1] +
+                                                  sh.warp_cnt[threadIdx.x][kSelWarps - 1];
+  cluster_sync();
+  if (threadIdx.x < 3) {
+    const int rank = (int)cg::this_cluster().block_rank();
+    uint32_t below = 0, all = 0;
+    for (int r = 0; r < kSelCluster; ++r) {
+      const uint32_t v = *peer(&sh.list_tot[threadIdx.x], r);
+      below += r < rank ? v : 0u;
+      all += v;
+    }
+    sh.list_off[threadIdx.x] = below;
+    sh.list_all[threadIdx.x] = all;
+  }
+  cluster_sync();  // peers' counts read before any block moves on (and exits)
+  uint32_t off_r = sh.list_off[0] + sh.warp_off[0][warp], off_s = sh.list_off[1] + sh.warp_off[1][warp],
+           off_c = sh.list_off[2] + sh.warp_off[2][warp];
+  const uint32_t below = (1u << lane) - 1u;
+  for (int b = ch.begin; b < ch.end; b += 4 * 32) {
+    uint8_t tr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      tr[j] = t < ch.end ? st.tier[t - st.base] : 0xFF;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      const uint32_t br = __ballot_sync(0xFFFFFFFFu, tr[j] == kRet);
+      const uint32_t bs = __ballot_sync(0xFFFFFFFFu, tr[j] == kCand);
+      const uint32_t bc = __ballot_sync(0xFFFFFFFFu, tr[j] == kCold);
+      if (tr[j] == kRet) {
+        const uint32_t pos = off_r + __popc(br & below);
+        if (pos < (uint32_t)p.n_ret) p.idx_ret[pos] = t;
+      } else if (tr[j] == kCand) {
+        const uint32_t pos = off_s + __popc(bs & below);
+        if (pos < (uint32_t)p.n_std) p.idx_std[pos] = t;
+      } else if (tr[j] == kCold) {
+        const uint32_t pos = off_c + __popc(bc & below);
+        if (pos < (uint32_t)p.n_cold) p.idx_cold[pos] = t;
+      }
+      off_r += __popc(br);
+      off_s += __popc(bs);
+      off_c += __popc(bc);
+    }
+  }
+  if (threadIdx.x == 0 && cg::this_cluster().block_rank() == 0) {
+    if (sh.list_all[0] != (uint32_t)p.n_ret || sh.list_all[1] != (uint32_t)p.n_std ||
+        sh.list_all[2] != (uint32_t)p.n_cold)
+      raise_error(kErrSelectCount);
+  }
 }
 
 template <bool SMEM>
 __device__ void select_body(const SelectParams& p, SelState<SMEM> st, SelShared& sh) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int t = threadIdx.x; t < p.T; t += kSelThreads) {
-    st.tier[t] = (t < p.sink || t >= p.T - p.tail) ? kRet : kCand;
-    if (SMEM && p.scores) const_cast<uint32_t*>(st.keys)[t] = order_key(p.scores[t]);
+  const float* const scores_src = SMEM ? nullptr : p.scores;
+  MarkOp pm = no_mark();
+  bool init = true;
+  int buf = 0;
+  if (p.keep_protect > 0) {
+    pm = select_radix<SMEM>(p, st, sh, pm, init, scores_src, p.keep_protect, true, kRet, buf);
+    init = false;
+  }
+  if (p.keep_outlier > 0) {
+    pm = select_radix<SMEM>(p, st, sh, pm, init, p.outlier, p.keep_outlier, true, kRet, buf);
+    init = false;
+  }
+  if (p.keep_cold > 0) {
+    pm = select_radix<SMEM>(p, st, sh, pm, init, scores_src, p.keep_cold, false, kCold, buf);
+    init = false;
+  }
+  if (init) {  // no score selection: sink and tail only
+    for (int t = st.base + (int)threadIdx.x; t < st.end; t += kSelThreads)
+      st.tier[t - st.base] = (t < p.sink || t >= p.T - p.tail) ? kRet : kCand;
   }
   __syncthreads();
-  if (p.keep_protect > 0) select_mark<SMEM>(p, st, SMEM ? nullptr : p.scores, p.keep_protect, true, kRet, sh);
-  if (p.keep_outlier > 0) select_mark<SMEM>(p, st, p.outlier, p.keep_outlier, true, kRet, sh);
-  if (p.keep_cold > 0) select_mark<SMEM>(p, st, SMEM ? nullptr : p.scores, p.keep_cold, false, kCold, sh);
-  // ordered compaction of the three lists
-  const Chunk ch = warp_chunk(p.T, warp);
-  uint32_t n[3] = {0, 0, 0};
-  for (int b = ch.begin; b < ch.end; b += 32) {
-    const int t = b + lane;
-    const uint8_t c = t < ch.end ? st.tier[t] : 0xFF;
-    n[0] += __popc(__ballot_sync(0xFFFFFFFFu, c == kRet));
-    n[1] += __popc(__ballot_sync(0xFFFFFFFFu, c == kCand));
-    n[2] += __popc(__ballot_sync(0xFFFFFFFFu, c == kCold));
-  }
-  if (lane == 0) {
-    sh.warp_cnt[0][warp] = n[0];
-    sh.warp_cnt[1][warp] = n[1];
-    sh.warp_cnt[2][warp] = n[2];
-  }
-  scan_warp_counts(sh, 3);
-  uint32_t off[3] = {sh.warp_off[0][warp], sh.warp_off[1][warp], sh.warp_off[2][warp]};
-  int* const out[3] = {p.idx_ret, p.idx_std, p.idx_cold};
-  const uint32_t lim[3] = {(uint32_t)p.n_ret, (uint32_t)p.n_std, (uint32_t)p.n_cold};
-  const uint8_t code[3] = {kRet, kCand, kCold};
-  for (int b = ch.begin; b < ch.end; b += 32) {
-    const int t = b + lane;
-    const uint8_t c = t < ch.end ? st.tier[t] : 0xFF;
-#pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, c == code[q]);
-      const uint32_t pos = off[q] + __popc(bal & ((1u << lane) - 1u));
-      if (c == code[q] && pos < lim[q]) out[q][pos] = t;
-      off[q] += __popc(bal);
-    }
-  }
-  if (threadIdx.x == 0) {
-    const uint32_t tot[3] = {sh.warp_off[0][31] + sh.warp_cnt[0][31], sh.warp_off[1][31] + sh.warp_cnt[1][31],
-                             sh.warp_off[2][31] + sh.warp_cnt[2][31]};
-    if (tot[0] != lim[0] || tot[1] != lim[1] || tot[2] != lim[2]) raise_error(kErrSelectCount);
-  }
+  compact_lists<SMEM>(p, st, sh, pm);
 }
 
-__global__ void __launch_bounds__(kSelThreads) select_kernel(const SelectParams p) {
+// Tokens per block of the selection cluster (a multiple of 128).
+__host__ __device__ __forceinline__ int select_block_tokens(int T) {
+  return ((T + kSelCluster - 1) / kSelCluster + 127) & ~127;
+}
+
+__global__ void __cluster_dims__(kSelCluster, 1, 1) __launch_bounds__(kSelThreads, 1)
+    select_kernel(const SelectParams p) {
   __shared__ SelShared sh;
   extern __shared__ __align__(16) uint8_t sel_smem[];
-  if (p.T <= kSelSmemTokens) {
-    SelState<true> st{reinterpret_cast<const uint32_t*>(sel_smem), sel_smem + 4 * (size_t)kSelSmemTokens};
+  const int per = select_block_tokens(p.T);
+  const int base = min(p.T, (int)cg::this_cluster().block_rank() * per), end = min(p.T, base + per);
+  if (per <= kSelSmemTokens) {
+    SelState<true> st{reinterpret_cast<uint32_t*>(sel_smem), sel_smem + 4 * (size_t)per, base, end};
     select_body<true>(p, st, sh);
   } else {
-    SelState<false> st{nullptr, p.tier};
+    SelState<false> st{nullptr, p.tier + base, base, end};
     select_body<false>(p, st, sh);
   }
 }
@@ -622,10 +829,11 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
   p.idx_ret = idx_ret;
   p.idx_std = idx_std;
   p.idx_cold = idx_cold;
-  const size_t sm = pol.seq_len <= kSelSmemTokens ? (size_t)kSelSmemTokens * 5 : 0;
+  const int per = select_block_tokens(T);
+  const size_t sm = per <= kSelSmemTokens ? (size_t)per * 5 : 0;
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
-  select_kernel<<<1, kSelThreads, sm, st>>>(p);
+  select_kernel<<<kSelCluster, kSelThreads, sm, st>>>(p);
   return cudaGetLastError();
 }
 

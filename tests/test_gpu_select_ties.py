@@ -7,7 +7,9 @@ that order; these tests call it through the C ABI (gkv_select_tiers) on
 tie-heavy scores and compare the three index lists with the oracle's
 restatement (integer outputs: exact equality).  Both regimes are reached for
 the largest (protection) and the smallest (cold tier) selection, in the
-shared-memory (T <= 40960) and the global-memory variant of the kernel.
+shared-memory variant of the kernel (at most 40960 tokens per block of its
+8-block cluster) and in the global-memory variant (longer sequences), with
+ties inside one block's range and across the ranges of several blocks.
 """
 import ctypes
 from dataclasses import replace
@@ -42,6 +44,8 @@ def _scores(T: int, kind: str, seed: int) -> np.ndarray:
         return s
     if kind == "sorted":
         return np.sort(rng.integers(0, 9, T).astype(np.float32))
+    if kind == "lognormal":  # continuous: no tie at either boundary
+        return np.exp(2.0 * rng.standard_normal(T)).astype(np.float32)
     raise ValueError(kind)
 
 
@@ -69,6 +73,11 @@ CASES = [
     (50000, "graphkv", {}, "levels7"),
     (131072, "graphkv", {}, "levels1000"),
     (131072, "graphkv", {}, "chunks"),
+    (32768, "graphkv", {}, "lognormal"),
+    (393216, "graphkv", {}, "lognormal"),
+    (393216, "graphkv", {}, "levels5000"),
+    (100, "graphkv", {"sink_length": 8, "residual_length": 8, "semantic_protection_min_context": 64,
+                      "low_priority_min_context": 64}, "levels3"),
     (12000, "graphkv-qwen7-nf4", {}, "levels4"),
     (16384, "graphkv", {}, "specials"),
     (16384, "graphkv", {}, "sorted"),
