@@ -192,7 +192,7 @@ __device__ void chan_decode(const DequantParams& p, const TensorDesc& d, int s, 
 #pragma unroll
         for (int e = 0; e < OC; e += 2) {
           const uint64_t v2 = decode_pair(c[e], c[e + 1], xm, xm, base2, sc2);
-          if constexpr (sizeof(T) == 4) { w[e] = (uint32_t)v2; w[e + 1] = (uint32_t)(v2 >> 32); }
+          if constexpr (sizeof(T) == 4) { w[e] = lo32(v2); w[e + 1] = hi32(v2); }
           else w[e / 2] = out_word<T>(v2);
         }
         dst[o] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -216,7 +216,7 @@ __device__ void chan_decode(const DequantParams& p, const TensorDesc& d, int s, 
       if constexpr (sizeof(T) == 4) {
 #pragma unroll
         for (int q = 0; q < RUN / 2; q += 2)
-          dst[q / 2] = make_uint4((uint32_t)v[q], (uint32_t)(v[q] >> 32), (uint32_t)v[q + 1], (uint32_t)(v[q + 1] >> 32));
+          dst[q / 2] = make_uint4(lo32(v[q]), hi32(v[q]), lo32(v[q + 1]), hi32(v[q + 1]));
       } else {
 #pragma unroll
         for (int q = 0; q < RUN / 2; q += 4)
@@ -277,8 +277,8 @@ __device__ void tok_decode(const TensorDesc& d, int s, int j0, uint8_t* tile) {
 #pragma unroll
         for (int e = 0; e < EPC; e += 2) {
           const uint64_t v2 = decode_pair(a[e], a[e + 1], x0, x0, base2, sc2);
-          col[(q * EPC + e) * G::kPitchW] = (uint32_t)v2;
-          col[(q * EPC + e + 1) * G::kPitchW] = (uint32_t)(v2 >> 32);
+          col[(q * EPC + e) * G::kPitchW] = lo32(v2);
+          col[(q * EPC + e + 1) * G::kPitchW] = hi32(v2);
         }
       }
     }

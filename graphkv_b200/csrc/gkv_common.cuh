@@ -142,11 +142,25 @@ __device__ __forceinline__ uint32_t code_of(float x, const GroupCoder& c) {
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest
 // operations per instruction, bitwise the same as two scalar ones)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t pk2(float a, float b) {
-  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+// A register pair from two 32-bit values, and its halves (register moves only).
+__device__ __forceinline__ uint64_t pk2u(uint32_t a, uint32_t b) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(a), "r"(b));
+  return d;
 }
-__device__ __forceinline__ float lo2(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float hi2(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint32_t lo32(uint64_t v) {
+  uint32_t a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  return a;
+}
+__device__ __forceinline__ uint32_t hi32(uint64_t v) {
+  uint32_t a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  return b;
+}
+__device__ __forceinline__ uint64_t pk2(float a, float b) { return pk2u(__float_as_uint(a), __float_as_uint(b)); }
+__device__ __forceinline__ float lo2(uint64_t v) { return __uint_as_float(lo32(v)); }
+__device__ __forceinline__ float hi2(uint64_t v) { return __uint_as_float(hi32(v)); }
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -255,8 +269,8 @@ __device__ __forceinline__ void encode_run(const float* x, const FastCoder& c, u
         a2 = pk2(fminf(fmaxf(lo2(a2), 0.f), c.hi), fminf(fmaxf(hi2(a2), 0.f), c.hi));
       }
       const uint64_t t2 = add2(a2, mg2);
-      acc = acc * (1u << SB) + (uint32_t)(t2 >> 32);
-      acc = acc * (1u << SB) + (uint32_t)t2;
+      acc = acc * (1u << SB) + hi32(t2);
+      acc = acc * (1u << SB) + lo32(t2);
     }
     w[q] = (acc - magic_sum<SB>(cnt)) ^ (c.flip & slot_mask<SB>(cnt));
   }

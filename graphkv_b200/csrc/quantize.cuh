@@ -150,8 +150,8 @@ __device__ __forceinline__ void encode_store_run(const uint32_t (&w)[NW], const 
 #pragma unroll
       for (int j = EPC / 2 - 1; j >= 0; --j) {
         const uint64_t t2 = code_pair<AFF>(pair_at<T>(w, (q0 + q) * EPC + 2 * j), inv2, nsc2, zp2, mg2, c.hi);
-        acc = acc * (1u << SB) + (uint32_t)(t2 >> 32);
-        acc = acc * (1u << SB) + (uint32_t)t2;
+        acc = acc * (1u << SB) + hi32(t2);
+        acc = acc * (1u << SB) + lo32(t2);
       }
       out[q] = (acc - magic_sum<SB>(EPC)) ^ (c.flip & slot_mask<SB>(EPC));
     }
@@ -177,8 +177,8 @@ __device__ __forceinline__ void encode_store_columns(const uint32_t (&x)[GS], co
 #pragma unroll
       for (int i = EPC - 1; i >= 0; --i) {
         const uint64_t t2 = code_pair<AFF>(Word16<T>::pair(x[(q0 + q) * EPC + i]), inv2, nsc2, zp2, mg2, c0.hi);
-        a0 = a0 * (1u << SB) + (uint32_t)t2;
-        a1 = a1 * (1u << SB) + (uint32_t)(t2 >> 32);
+        a0 = a0 * (1u << SB) + lo32(t2);
+        a1 = a1 * (1u << SB) + hi32(t2);
       }
       o0[q] = (a0 - magic_sum<SB>(EPC)) ^ (c0.flip & slot_mask<SB>(EPC));
       o1[q] = (a1 - magic_sum<SB>(EPC)) ^ (c1.flip & slot_mask<SB>(EPC));
@@ -369,8 +369,8 @@ __device__ __forceinline__ void pairs_to_words(const uint64_t (&v)[RUN / 2], uin
 #pragma unroll
   for (int k = 0; k < RUN / 2; ++k) {
     if constexpr (sizeof(T) == 4) {
-      w[2 * k] = (uint32_t)v[k];
-      w[2 * k + 1] = (uint32_t)(v[k] >> 32);
+      w[2 * k] = lo32(v[k]);
+      w[2 * k + 1] = hi32(v[k]);
     } else {
       w[k] = Word16<T>::round2(lo2(v[k]), hi2(v[k]));
     }
