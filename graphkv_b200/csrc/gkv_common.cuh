@@ -149,13 +149,13 @@ __device__ __forceinline__ uint64_t pk2u(uint32_t a, uint32_t b) {
   return d;
 }
 __device__ __forceinline__ uint32_t lo32(uint64_t v) {
-  uint32_t a, b;
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  uint32_t a;
+  asm("{\n\t.reg .b32 h;\n\tmov.b64 {%0, h}, %1;\n\t}" : "=r"(a) : "l"(v));
   return a;
 }
 __device__ __forceinline__ uint32_t hi32(uint64_t v) {
-  uint32_t a, b;
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  uint32_t b;
+  asm("{\n\t.reg .b32 l;\n\tmov.b64 {l, %0}, %1;\n\t}" : "=r"(b) : "l"(v));
   return b;
 }
 __device__ __forceinline__ uint64_t pk2(float a, float b) { return pk2u(__float_as_uint(a), __float_as_uint(b)); }

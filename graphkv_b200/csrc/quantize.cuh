@@ -557,7 +557,7 @@ __device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr
 // zeroes the tile counts of the others) and the retained rows when `copy_retained`.
 // Many small blocks per SM: while some wait for their rows, others compute.
 template <typename T, int D, int AXIS, bool ROT>
-__global__ void __launch_bounds__(kQThreads, AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7))
+__global__ void __launch_bounds__(kQThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 6 : 10)))
     quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
