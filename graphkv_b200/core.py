@@ -353,50 +353,74 @@ class QuantizedKvCache:
         raise ValueError("implementation must be 'dynamic', 'static', 'sliding_window', or 'legacy'.")
 
     def to_hf_dynamic_cache(self, *, config: object | None = None) -> object:
-        """core.py:472-481.  A plain ``DynamicLayer`` receives the dequantized
-        tensors directly (its ``update`` would concatenate them onto an empty
-        tensor, a full copy with the same result); other layer types go through
-        ``update``."""
-        try:
-            from transformers.cache_utils import DynamicCache, DynamicLayer
-        except ImportError as exc:
-            raise RuntimeError("transformers is required to build a DynamicCache.") from exc
-        cache = DynamicCache(config=config)
-        for layer_idx, (keys, values) in enumerate(self.dequantize()):
-            if not getattr(cache, "offloading", False) and getattr(cache, "layer_class_to_replicate", None) is not None:
-                while len(cache.layers) <= layer_idx:
-                    cache.layers.append(cache.layer_class_to_replicate())
-            target = cache.layers[layer_idx] if layer_idx < len(cache.layers) else None
-            if (type(target) is DynamicLayer and not getattr(target, "is_initialized", True)
-                    and not getattr(cache, "offloading", False)):
-                target.lazy_initialization(keys, values)
-                target.keys = keys
-                target.values = values
-            else:
-                cache.update(keys, values, layer_idx)
-        return cache
+        """core.py:472-481."""
+        return _dynamic_cache_from(self.dequantize(), config)
 
     def _to_hf_positioned_cache(self, implementation: Literal["static", "sliding_window"], *,
                                 config: object | None, max_cache_len: int | None) -> object:
-        """core.py:483-508 (same imports, checks and update calls)."""
-        if config is None:
-            raise ValueError("config is required for static or sliding_window HF cache export.")
-        try:
-            from transformers.cache_utils import SlidingWindowCache, StaticCache
-        except ImportError as exc:
-            raise RuntimeError("transformers is required to build a positioned cache.") from exc
-        dequantized = self.dequantize()
-        required = max((keys.shape[2] for keys, _ in dequantized), default=0)
-        if max_cache_len is None:
-            max_cache_len = required
-        if max_cache_len < required:
-            raise ValueError("max_cache_len must be at least the longest KV sequence length.")
-        cache_cls = StaticCache if implementation == "static" else SlidingWindowCache
-        cache = cache_cls(config, max_cache_len=max_cache_len)
-        for layer_idx, (keys, values) in enumerate(dequantized):
-            positions = torch.arange(keys.shape[2], device=keys.device, dtype=torch.long)
-            cache.update(keys, values, layer_idx, cache_kwargs={"cache_position": positions})
-        return cache
+        """core.py:483-508."""
+        return _positioned_cache_from(self.dequantize(), implementation, config, max_cache_len)
+
+
+def _dynamic_cache_from(dequantized, config: object | None) -> object:
+    """DynamicCache of dequantized (K, V) pairs (core.py:472-481).  A plain
+    ``DynamicLayer`` receives the tensors directly (its ``update`` would
+    concatenate them onto an empty tensor, a full copy with the same result);
+    other layer types go through ``update``."""
+    try:
+        from transformers.cache_utils import DynamicCache, DynamicLayer
+    except ImportError as exc:
+        raise RuntimeError("transformers is required to build a DynamicCache.") from exc
+    cache = DynamicCache(config=config)
+    for layer_idx, (keys, values) in enumerate(dequantized):
+        if not getattr(cache, "offloading", False) and getattr(cache, "layer_class_to_replicate", None) is not None:
+            while len(cache.layers) <= layer_idx:
+                cache.layers.append(cache.layer_class_to_replicate())
+        target = cache.layers[layer_idx] if layer_idx < len(cache.layers) else None
+        if (type(target) is DynamicLayer and not getattr(target, "is_initialized", True)
+                and not getattr(cache, "offloading", False)):
+            target.lazy_initialization(keys, values)
+            target.keys = keys
+            target.values = values
+        else:
+            cache.update(keys, values, layer_idx)
+    return cache
+
+
+def _positioned_cache_from(dequantized, implementation: Literal["static", "sliding_window"],
+                           config: object | None, max_cache_len: int | None) -> object:
+    """StaticCache / SlidingWindowCache of dequantized pairs (core.py:483-508:
+    same imports, checks and update calls)."""
+    if config is None:
+        raise ValueError("config is required for static or sliding_window HF cache export.")
+    try:
+        from transformers.cache_utils import SlidingWindowCache, StaticCache
+    except ImportError as exc:
+        raise RuntimeError("transformers is required to build a positioned cache.") from exc
+    required = max((keys.shape[2] for keys, _ in dequantized), default=0)
+    if max_cache_len is None:
+        max_cache_len = required
+    if max_cache_len < required:
+        raise ValueError("max_cache_len must be at least the longest KV sequence length.")
+    cache_cls = StaticCache if implementation == "static" else SlidingWindowCache
+    cache = cache_cls(config, max_cache_len=max_cache_len)
+    for layer_idx, (keys, values) in enumerate(dequantized):
+        positions = torch.arange(keys.shape[2], device=keys.device, dtype=torch.long)
+        cache.update(keys, values, layer_idx, cache_kwargs={"cache_position": positions})
+    return cache
+
+
+def export_dequantized(dequantized, implementation: str, *, config: object | None = None,
+                       max_cache_len: int | None = None) -> object:
+    """Dequantized (K, V) pairs in the cache format ``implementation`` (the
+    dispatch of core.py:450-470)."""
+    if implementation == "legacy":
+        return tuple(dequantized)
+    if implementation == "dynamic":
+        return _dynamic_cache_from(dequantized, config)
+    if implementation in {"static", "sliding_window"}:
+        return _positioned_cache_from(dequantized, implementation, config, max_cache_len)
+    raise ValueError("implementation must be 'dynamic', 'static', 'sliding_window', or 'legacy'.")
 
 
 # ---------------------------------------------------------------------------
@@ -933,6 +957,103 @@ def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
         hv.copy_(outv, non_blocking=True)
         outk, outv = hk, hv
     return [(outk[l], outv[l]) for l in range(nl)]
+
+
+HOST_CHUNK_LAYERS = 4  # layers per stage of the pipelined host round trip
+
+
+def roundtrip_host_cache(pairs, config: KvQuantConfig, importance_scores=None,
+                         chunk_layers: int = HOST_CHUNK_LAYERS):
+    """Compress and dequantize a cache held in pinned host memory, pipelined over
+    chunks of layers on three streams: the host-to-device copy of chunk c + 1,
+    the selection / quantize / dequantize kernels of chunk c and the
+    device-to-host copy of chunk c - 1 overlap (both copy directions at once).
+    The kernels and their outputs are those of ``from_past_key_values`` followed
+    by ``dequantize``; the selection runs once and its index lists serve every
+    chunk.  Returns the dequantized (K, V) pairs in pinned host memory, or None
+    when the cache does not take this path (device or pageable tensors, mixed
+    geometries, per-layer scores or per-layer outlier selections, passthrough
+    layers); the caller then compresses and dequantizes in two steps."""
+    pairs = list(pairs)
+    if not pairs or not torch.cuda.is_available():
+        return None
+    config.validate()
+    for keys, values in pairs:
+        _check_pair(keys, values)
+    k0 = pairs[0][0]
+    shape, dtype = tuple(k0.shape), k0.dtype
+    for keys, values in pairs:
+        if (tuple(keys.shape) != shape or keys.dtype != dtype or keys.device.type != "cpu"
+                or values.device.type != "cpu" or not keys.is_pinned() or not values.is_pinned()
+                or keys.stride(3) != 1 or values.stride(3) != 1):
+            return None
+    if importance_scores is not None and not isinstance(importance_scores, torch.Tensor):
+        return None
+    if config.outlier_protection_ratio > 0.0 or config.min_outlier_tokens > 0:
+        return None
+    B, H, T, D = shape
+    tiers = resolve_tiers(config, T, importance_scores is not None)
+    plans = tensor_plans(config, shape, tiers)
+    if config.skip_if_not_smaller and \
+            layer_memory_bytes(shape, dtype, tiers, plans) >= 2 * B * H * T * D * _dtype_element_size(dtype):
+        return None
+    n = len(pairs)
+    step = max(1, min(int(chunk_layers), n))
+    if step > 1 and any(p is not None and not p.slice_bits_aligned for p in plans):
+        step = 1
+    dev = _compute_device(torch.empty(0))
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    chunks = [(a, min(n, a + step)) for a in range(0, n, step)]
+    slots = min(2, len(chunks))
+    in_k = [torch.empty((step, *shape), dtype=dtype, device=dev) for _ in range(slots)]
+    in_v = [torch.empty((step, *shape), dtype=dtype, device=dev) for _ in range(slots)]
+    out_k = [torch.empty((step, *shape), dtype=dtype, device=dev) for _ in range(slots)]
+    out_v = [torch.empty((step, *shape), dtype=dtype, device=dev) for _ in range(slots)]
+    host_k = torch.empty((n, *shape), dtype=dtype, pin_memory=True)
+    host_v = torch.empty((n, *shape), dtype=dtype, pin_memory=True)
+    scores = None
+    if importance_scores is not None:
+        scores = _normalize_token_scores(T, importance_scores, dev).contiguous()
+    s_in.wait_stream(comp)  # the buffers above may reuse memory of earlier work on this stream
+    s_out.wait_stream(comp)
+    in_free: list = [None] * slots
+    out_free: list = [None] * slots
+    first = None
+    for c, (a, b) in enumerate(chunks):
+        slot, nl = c % slots, b - a
+        with torch.cuda.stream(s_in):
+            if in_free[slot] is not None:
+                s_in.wait_event(in_free[slot])
+            for i in range(nl):
+                in_k[slot][i].copy_(pairs[a + i][0], non_blocking=True)
+                in_v[slot][i].copy_(pairs[a + i][1], non_blocking=True)
+            loaded = torch.cuda.Event()
+            loaded.record(s_in)
+        comp.wait_event(loaded)
+        idx = None if first is None else (first.idx_ret, first.idx_std, first.idx_cold)
+        run = _GroupRun([(in_k[slot][i], in_v[slot][i]) for i in range(nl)], config, tiers, plans, dev,
+                        torch.device("cpu"), idx)
+        if first is None:
+            run.select(scores)
+            first = run
+        run.quantize()
+        in_free[slot] = torch.cuda.Event()
+        in_free[slot].record(comp)
+        if out_free[slot] is not None:
+            comp.wait_event(out_free[slot])
+        run.out_k, run.out_v = out_k[slot][:nl], out_v[slot][:nl]
+        run.dequantize()
+        decoded = torch.cuda.Event()
+        decoded.record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(decoded)
+            host_k[a:b].copy_(out_k[slot][:nl], non_blocking=True)
+            host_v[a:b].copy_(out_v[slot][:nl], non_blocking=True)
+            out_free[slot] = torch.cuda.Event()
+            out_free[slot].record(s_out)
+    s_out.synchronize()
+    return [(host_k[l], host_v[l]) for l in range(n)]
 
 
 # ---------------------------------------------------------------------------

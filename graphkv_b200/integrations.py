@@ -6,7 +6,7 @@ from __future__ import annotations
 import shlex
 from typing import Iterable
 
-from .core import QuantizedKvCache, hf_cache_to_tuple
+from .core import QuantizedKvCache, export_dequantized, hf_cache_to_tuple, roundtrip_host_cache
 from .profiles import GraphKVProfile, get_profile
 
 
@@ -39,7 +39,16 @@ def quantize_hf_cache(
 
         importance_scores = graph_mneme_request_token_scores(
             _hf_cache_seq_len(past_key_values), graph_request, model=graph_mneme_model, device=graph_mneme_device)
-    compressed = QuantizedKvCache.from_hf_cache(past_key_values, selected.config, importance_scores=importance_scores)
+    if output in {"legacy", "dynamic", "static", "sliding_window"}:
+        # a cache in pinned host memory: copies in both directions overlap the kernels
+        pairs = hf_cache_to_tuple(past_key_values, cache_role="self")
+        dequantized = roundtrip_host_cache(pairs, selected.config, importance_scores)
+        if dequantized is not None:
+            return export_dequantized(dequantized, output, config=model_config, max_cache_len=max_cache_len)
+        compressed = QuantizedKvCache.from_past_key_values(pairs, selected.config, importance_scores)
+    else:
+        compressed = QuantizedKvCache.from_hf_cache(past_key_values, selected.config,
+                                                    importance_scores=importance_scores)
     if output == "compressed":
         return compressed
     return compressed.to_hf_cache(output, config=model_config, max_cache_len=max_cache_len)

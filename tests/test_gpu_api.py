@@ -96,3 +96,53 @@ def test_static_export_follows_reference_behaviour():
         comp.to_hf_cache("static")
     with pytest.raises(ValueError, match="implementation must be"):
         comp.to_hf_cache("paged")
+
+
+def _pinned(cache):
+    return tuple((k.pin_memory(), v.pin_memory()) for k, v in cache)
+
+
+@pytest.mark.parametrize("chunk", [1, 2, 4])
+def test_pinned_host_round_trip_pipeline_matches_two_step_path(chunk):
+    """The pipelined host path (copies in both directions overlapping the kernels,
+    one selection shared by every chunk) returns the same bytes as compressing
+    and then dequantizing, for a cache whose cold tier is rotated (T = 32768)."""
+    from graphkv_b200.core import roundtrip_host_cache
+    from graphkv_b200.profiles import get_profile
+    cache = _pinned(_small_cache(T=32768, layers=5, device="cpu"))
+    scores = torch.exp(2.0 * torch.randn(32768, generator=torch.Generator().manual_seed(3)))
+    cfg = get_profile("graphkv").config
+    piped = roundtrip_host_cache(cache, cfg, scores, chunk_layers=chunk)
+    assert piped is not None and len(piped) == 5
+    two_step = g.QuantizedKvCache.from_past_key_values(cache, cfg, scores).dequantize()
+    assert L.device_error() == 0
+    for (pk, pv), (tk, tv) in zip(piped, two_step):
+        assert pk.device.type == "cpu" and pk.is_pinned()
+        assert torch.equal(pk, tk) and torch.equal(pv, tv)
+
+
+def test_quantize_hf_cache_takes_the_pipeline_for_pinned_host_caches(monkeypatch):
+    from graphkv_b200 import core
+    calls = []
+    real = core.roundtrip_host_cache
+
+    def spy(*a, **k):
+        out = real(*a, **k)
+        calls.append(out is not None)
+        return out
+
+    monkeypatch.setattr("graphkv_b200.integrations.roundtrip_host_cache", spy)
+    cache = _small_cache(device="cpu")
+    pinned = _pinned(cache)
+    scores = torch.exp(torch.randn(2048, generator=torch.Generator().manual_seed(1)))
+    legacy = g.quantize_hf_cache(pinned, "graphkv", importance_scores=scores, output="legacy")
+    dyn = g.quantize_hf_cache(pinned, "graphkv", importance_scores=scores, output="dynamic")
+    plain = g.quantize_hf_cache(cache, "graphkv", importance_scores=scores, output="legacy")  # pageable
+    assert calls == [True, True, False]
+    for i, ((lk, lv), (qk, qv)) in enumerate(zip(legacy, plain)):
+        assert torch.equal(lk, qk) and torch.equal(lv, qv)
+        assert torch.equal(dyn.layers[i].keys, qk) and torch.equal(dyn.layers[i].values, qv)
+    with pytest.raises(ValueError, match="config is required"):
+        g.quantize_hf_cache(pinned, "graphkv", importance_scores=scores, output="static")
+    with pytest.raises(ValueError, match="implementation must be"):
+        g.quantize_hf_cache(pinned, "graphkv", importance_scores=scores, output="paged")
