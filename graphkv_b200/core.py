@@ -959,11 +959,10 @@ def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
     return [(outk[l], outv[l]) for l in range(nl)]
 
 
-HOST_CHUNK_LAYERS = 4  # layers per stage of the pipelined host round trip
+HOST_CHUNK_BYTES = 64 << 20  # K+V bytes per stage of the pipelined host round trip (at least one layer)
 
 
-def roundtrip_host_cache(pairs, config: KvQuantConfig, importance_scores=None,
-                         chunk_layers: int = HOST_CHUNK_LAYERS):
+def roundtrip_host_cache(pairs, config: KvQuantConfig, importance_scores=None, chunk_layers: int | None = None):
     """Compress and dequantize a cache held in pinned host memory, pipelined over
     chunks of layers on three streams: the host-to-device copy of chunk c + 1,
     the selection / quantize / dequantize kernels of chunk c and the
@@ -998,6 +997,8 @@ def roundtrip_host_cache(pairs, config: KvQuantConfig, importance_scores=None,
             layer_memory_bytes(shape, dtype, tiers, plans) >= 2 * B * H * T * D * _dtype_element_size(dtype):
         return None
     n = len(pairs)
+    if chunk_layers is None:
+        chunk_layers = -(-HOST_CHUNK_BYTES // (2 * B * H * T * D * _dtype_element_size(dtype)))
     step = max(1, min(int(chunk_layers), n))
     if step > 1 and any(p is not None and not p.slice_bits_aligned for p in plans):
         step = 1
