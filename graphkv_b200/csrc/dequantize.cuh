@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_
   // (chunk, rows r0, r0 + STEP, ...)
   constexpr int CH = G::kRowBytes / 16, STEP = kDThreads / CH;
   const int c = threadIdx.x % CH, r0 = threadIdx.x / CH;
-#pragma unroll 4
+#pragma unroll
   for (int i = 0; i < kDTile / STEP; ++i) {
     const int r = r0 + i * STEP;
     const int t_out = r < rows ? toks[r] : -1;
