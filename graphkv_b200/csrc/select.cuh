@@ -81,6 +81,14 @@ template <class U>
 __device__ __forceinline__ U* peer(U* p, int r) {
   return cg::this_cluster().map_shared_rank(p, r);
 }
+// 32-bit word at the same shared-memory address in block r, read through the
+// cluster's shared window.
+__device__ __forceinline__ uint32_t ld_peer(const uint32_t* p, int r) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(p), ra, v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(r));
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(ra) : "memory");
+  return v;
+}
 
 // Tokens handled by warp w in the sweeps of [lo, hi): one contiguous chunk per
 // warp, a multiple of 128 tokens (four 32-token slices per step).
@@ -488,7 +496,7 @@ __device__ BinPick find_bin(SelShared& sh, int buf, int nbins, uint32_t rem, boo
       uint32_t* const h = &sh.hist[buf][largest ? nbins - 1 - pos : pos];
       uint32_t v[kSelCluster];
 #pragma unroll
-      for (int r = 0; r < kSelCluster; ++r) v[r] = *peer(h, r);
+      for (int r = 0; r < kSelCluster; ++r) v[r] = ld_peer(h, r);
 #pragma unroll
       for (int r = 0; r < kSelCluster; ++r) c[j] += v[r];
       sum += c[j];
@@ -677,7 +685,7 @@ __device__ void compact_lists(const SelectParams& p, const SelState<SMEM>& st, S
     const int rank = (int)cg::this_cluster().block_rank();
     uint32_t below = 0, all = 0;
     for (int r = 0; r < kSelCluster; ++r) {
-      const uint32_t v = *peer(&sh.list_tot[threadIdx.x], r);
+      const uint32_t v = ld_peer(&sh.list_tot[threadIdx.x], r);
       below += r < rank ? v : 0u;
       all += v;
     }
