@@ -6,10 +6,11 @@
 // optional inverse Hadamard (the same butterflies, fp32), then the cast to the
 // cache dtype.
 //
-// Fast path: one block per tile of TT tier rows of one slice.  Token-axis
-// tensors decode a [TT, D] fp32 tile in shared memory (thread per channel and
-// run of 16 rows), channel-axis tensors decode straight from the packed rows
-// (warp per row); both leave through warp-per-row stores of whole output rows.
+// Fast path: one block of 128 threads per tile of 64 tier rows of one slice and
+// tensor.  Token-axis tensors decode column runs (thread per 32-bit column word
+// and run of 32 rows), channel-axis tensors decode row runs (thread per 128-byte
+// run, rotated runs through in-register butterflies); both decode into a shared
+// [64][D] tile whose rows leave as whole 256-byte rows of 16-byte stores.
 #pragma once
 
 #include <algorithm>

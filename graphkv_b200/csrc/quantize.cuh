@@ -1,7 +1,8 @@
 // Quantize + pack kernels (core.py:647-772, 848-910, 945-956, 979-990).
 //
-// Fast path: two launches, one over K and one over V; one block of 64 threads per
-// tile of 64 consecutive tier rows of one slice.  The threads gather the tile's
+// Fast path: one launch per (tensor, kernel variant) -- for the graphkv profile
+// keys, plain values and rotated cold values; one block of 128 threads per tile of
+// 64 consecutive tier rows of one slice.  The threads gather the tile's
 // rows into shared memory with 16-byte asynchronous copies, then quantize them,
 // each thread holding whole quantization groups in registers:
 //  - token-axis groups (K): a thread owns one 32-bit column word (two 16-bit
