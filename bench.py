@@ -9,11 +9,14 @@ whole cache back to [B, H, T, D] bf16.  ``value`` is GB/s of input cache
 (K+V bytes) per step with inputs resident in HBM; ``phases`` gives each phase
 against the HBM roofline (algorithmic bytes = bytes read + bytes written).
 
-N GPUs (torchrun): weak scaling.  The global cache is the same model with batch
-N; its 28 x 4 (layer, kv-head) units are sharded contiguously over the ranks,
-each unit holding all N batch rows, so every rank compresses exactly the work
-of one 32k cache.  The only collective is an all-gather of the per-shard byte
-and token counts each step.
+N GPUs (torchrun), headline: weak scaling.  The global cache is the same model
+with batch N; its 28 x 4 (layer, kv-head) units are sharded contiguously over
+the ranks, each unit holding all N batch rows, so every rank compresses exactly
+the work of one 32k cache.  ``strong`` (second leg, on by default): the
+8 x 131072-token cache (60 GB of K+V) split over the N ranks by the same units
+-- strong scaling of one fixed cache.  No collective runs inside a timed step;
+after the timed steps one all-gather of per-layer byte and token counts
+rebuilds the whole cache's stats() and one more gathers each rank's phase times.
 
 ``--impl reference`` times the CPU port of the reference algorithm (the numpy
 oracle) on the host cores, on a bounded sample of the same workload.
@@ -33,6 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 WORKLOAD = "qwen7b-32k"
+STRONG_WORKLOAD = "qwen7b-8x131k"
 METRIC = "KV quant+pack and dequant GB/s (% HBM peak), Qwen2.5-7B-shape 32k cache"
 
 
@@ -43,6 +47,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=WORKLOAD)
+    ap.add_argument("--strong-workload", default=STRONG_WORKLOAD,
+                    help="cache split over the ranks for the strong-scaling leg ('' to skip)")
+    ap.add_argument("--strong-steps", type=int, default=12)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling case)")
@@ -56,8 +63,6 @@ def parse_args():
 def _oracle_slice(args):
     """Quantize + dequantize one (layer, head) slice with the numpy oracle."""
     wkey, layer, head = args
-    import numpy as np  # noqa: F401
-
     from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
     from oracle import graphkv_oracle as orc
 
@@ -214,47 +219,82 @@ def committed_traffic(workload):
     return out
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
+class Dist:
+    """Rank bookkeeping; every collective below is issued by every rank in the
+    same order, outside the timed steps."""
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
+    def __init__(self):
+        import torch
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
 
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def gather(self, values):
+        """All ranks' float vectors, [world][len] (one all-gather)."""
+        import torch
+
+        t = torch.tensor(values, dtype=torch.float64, device=self.dev)
+        if self.world == 1:
+            return [values]
+        import torch.distributed as dist
+
+        out = torch.empty(self.world * t.numel(), dtype=torch.float64, device=self.dev)
+        dist.all_gather_into_tensor(out, t)
+        return out.view(self.world, -1).tolist()
+
+    def close(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+def time_compression(d: Dist, w, mode: str, steps: int, warmup: int, with_clocks: bool = False):
+    """Prepare this rank's shard of workload `w` on the device and time `steps`
+    select + quantize + dequant steps.  mode "weak": the cache has batch
+    world * B and every rank holds a whole cache's worth of units; "strong": the
+    cache is `w` itself, its units split over the ranks."""
     from dataclasses import replace
+
+    import torch
 
     import graphkv_b200 as g
     from graphkv_b200 import _lib
     from graphkv_b200.engine import CompressionEngine
-    from graphkv_b200.sharding import combine_stats, shard_bytes, shard_stats, shard_units
-    from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
+    from graphkv_b200.sharding import STAT_FIELDS, gather_stat_rows, piece_stat_row, shard_units, stats_from_rows
+    from graphkv_b200.workloads import make_layer, make_scores
 
-    w = WORKLOADS[args.workload]
-    if args.layers:
-        w = replace(w, layers=args.layers)
-    wN = replace(w, batch=w.batch * world)
-    shard = shard_units(w.layers, w.heads, world, rank)
-    pairs = [make_layer(wN, l, device=str(dev), heads=range(h0, h1)) for (l, h0, h1) in shard]
-    scores = make_scores(w, device=str(dev))
+    wx = replace(w, batch=w.batch * d.world) if mode == "weak" else w
+    shard = shard_units(w.layers, w.heads, d.world, d.rank)
+    pairs = [make_layer(wx, l, device=str(d.dev), heads=range(h0, h1)) for (l, h0, h1) in shard]
+    scores = make_scores(w, device=str(d.dev))
     cfg = g.get_profile(w.profile).config
     in_bytes = sum(k.numel() * k.element_size() * 2 for k, _ in pairs)
-    comp_bytes = sum(shard_bytes(tuple(k.shape), k.dtype, cfg, scores is not None, h0)[0]
-                     for (k, _), (_, h0, _) in zip(pairs, shard))
     eng = CompressionEngine(pairs, cfg, scores)
-    runs = eng.runs
+    local = eng.cache()
+    rows = torch.zeros(w.layers, len(STAT_FIELDS), dtype=torch.int64)
+    for lay, (l, h0, _) in zip(local.layers, shard):
+        rows[l] += torch.tensor(piece_stat_row(lay, h0), dtype=torch.int64)
+    comp_bytes = int(rows[:, 0].sum())
     launches = eng.launches_per_step()
-    stats_vec = shard_stats(comp_bytes, in_bytes, device=dev)
-    gathered = torch.empty(world * 2, device=dev, dtype=torch.float64)
-
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.current_stream(d.dev)
     work = [(it[1], it[2], it[3]) for it in eng.items if it[0] == "run"]
+    nr = len(work)
 
     def step(ev=None):
         # ev[i] = 4 events per run: before select, after select, after quantize, after dequantize
@@ -272,29 +312,26 @@ def run_ours(args):
             run.dequantize()
             if ev is not None:
                 ev[i][3].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, stats_vec)
 
-    # warm-up
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
-    torch.cuda.synchronize(dev)
+    torch.cuda.synchronize(d.dev)
     assert _lib.device_error() == 0
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-
-    nr = len(work)
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nr)] for _ in range(args.steps)]
+    d.barrier()
+    torch.cuda.synchronize(d.dev)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nr)] for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for s in range(args.steps):
-            step(evs[s])
-        end.record(stream)
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    clocks = ClockSampler(d.local) if with_clocks else None
+    if clocks:
+        clocks.__enter__()
+    start.record(stream)
+    for s in range(steps):
+        step(evs[s])
+    end.record(stream)
+    torch.cuda.synchronize(d.dev)
+    if clocks:
+        clocks.__exit__()
+    d.barrier()
     elapsed_ms = start.elapsed_time(end)
     t_sel = t_q = t_dq = 0.0
     for e in evs:
@@ -302,66 +339,120 @@ def run_ours(args):
             t_sel += e[i][0].elapsed_time(e[i][1])
             t_q += e[i][1].elapsed_time(e[i][2])
             t_dq += (e[nr - 1][2] if i == 0 else e[i - 1][3]).elapsed_time(e[i][3])
-    if world > 1:
-        t = torch.tensor([elapsed_ms, t_sel, t_q, t_dq], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms, t_sel, t_q, t_dq = (float(x) for x in t.tolist())
     assert _lib.device_error() == 0
+    # after the timed steps: per-rank phase times and the whole cache's stats (one all-gather each)
+    per_rank = d.gather([elapsed_ms / steps, t_sel / steps, t_q / steps, t_dq / steps,
+                         float(in_bytes), float(comp_bytes)])
+    stats = stats_from_rows(gather_stat_rows(rows, device=d.dev))
+    del eng, local, pairs, work
+    torch.cuda.empty_cache()
+    return {"per_rank": per_rank, "stats": stats, "launches": launches, "nr": nr,
+            "clocks": clocks.summary() if clocks else None, "in_bytes": in_bytes, "comp_bytes": comp_bytes}
 
-    # end to end through the public API with host (pinned) buffers
+
+def phase_report(res, peak):
+    """Max-over-ranks phase times and their roofline fractions (per-rank bytes)."""
+    pr = res["per_rank"]
+    worst = max(range(len(pr)), key=lambda r: pr[r][0])
+    ms = max(r[0] for r in pr)
+    sel, q, dq = (max(r[i] for r in pr) for i in (1, 2, 3))
+    in_b, comp_b = pr[worst][4], pr[worst][5]
+    algo = in_b + comp_b
+    return ms, {
+        "select": {"ms": round(sel, 4)},
+        "quantize": {"ms": round(q, 4), "input_gbs": round(in_b / q / 1e6, 1), "algo_gbs": round(algo / q / 1e6, 1),
+                     "frac": round(algo / q / 1e6 / peak, 4)},
+        "dequant": {"ms": round(dq, 4), "input_gbs": round(in_b / dq / 1e6, 1),
+                    "algo_gbs": round(algo / dq / 1e6, 1), "frac": round(algo / dq / 1e6 / peak, 4)},
+    }
+
+
+def run_ours(args):
+    import torch
+
+    import graphkv_b200 as g
+    from dataclasses import replace
+    from graphkv_b200.workloads import WORKLOADS, make_layer, make_scores
+
+    d = Dist()
+    peak, peak_kind = measured_peak()
+    w = WORKLOADS[args.workload]
+    if args.layers:
+        w = replace(w, layers=args.layers)
+
+    # --- headline: weak scaling of the 32k cache ------------------------------------
+    head = time_compression(d, w, "weak", args.steps, args.warmup, with_clocks=True)
+    ms, phases = phase_report(head, peak)
+    in_bytes_rank = head["in_bytes"]
+
+    # --- strong scaling of the 8 x 131k (60 GB) cache ---------------------------------
+    strong = None
+    if args.strong_workload:
+        ws = WORKLOADS[args.strong_workload]
+        from graphkv_b200.sharding import shard_units
+
+        units = shard_units(ws.layers, ws.heads, d.world, d.rank)
+        unit_bytes = ws.batch * ws.seq * ws.head_dim * ws.dtype.itemsize * 2  # K+V of one (layer, head)
+        need = sum(h1 - h0 for _, h0, h1 in units) * unit_bytes * 2.3 + (6 << 30)  # in + out + arena
+        free, _ = torch.cuda.mem_get_info(d.dev)
+        fits = min(r[0] for r in d.gather([1.0 if free > need else 0.0])) > 0
+        if fits:
+            res = time_compression(d, ws, "strong", args.strong_steps, 3)
+            s_ms, s_phases = phase_report(res, peak)
+            strong = {"workload": args.strong_workload, "scaling": "strong", "n_gpus": d.world,
+                      "value": round(ws.input_bytes / (s_ms * 1e6), 2), "unit": "GB/s",
+                      "ms_per_step": round(s_ms, 4), "steps": args.strong_steps,
+                      "input_bytes_total": ws.input_bytes, "phases": s_phases,
+                      "units_per_rank": [len([0 for _ in shard_units(ws.layers, ws.heads, d.world, r)])
+                                         for r in range(d.world)],
+                      "cache_stats": res["stats"]}
+        else:
+            strong = {"workload": args.strong_workload, "skipped": f"needs {need / 2**30:.0f} GiB per GPU"}
+
+    # --- end to end through the public API with host (pinned) buffers -----------------
     e2e = None
     if args.e2e_steps > 0:
+        from graphkv_b200.sharding import shard_units
+
+        wN = replace(w, batch=w.batch * d.world)
+        shard = shard_units(w.layers, w.heads, d.world, d.rank)
         host_pairs = []
-        for k, v in pairs:
+        for (l, h0, h1) in shard:
+            k, v = make_layer(wN, l, device=str(d.dev), heads=range(h0, h1))
             hk = torch.empty(k.shape, dtype=k.dtype, pin_memory=True)
             hv = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
             hk.copy_(k)
             hv.copy_(v)
             host_pairs.append((hk, hv))
-        del eng, runs, work
+            del k, v
         torch.cuda.empty_cache()
-        host_scores = scores.cpu()
+        host_scores = make_scores(w)
         out = g.quantize_hf_cache(tuple(host_pairs), w.profile, importance_scores=host_scores, output="legacy")
         del out
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+        torch.cuda.synchronize(d.dev)
+        d.barrier()
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
             out = g.quantize_hf_cache(tuple(host_pairs), w.profile, importance_scores=host_scores, output="legacy")
-            torch.cuda.synchronize(dev)
+            torch.cuda.synchronize(d.dev)
             del out
-        if world > 1:
-            dist.barrier()
         e2e_s = (time.perf_counter() - t0) / args.e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_s = float(t.item())
-        e2e = {"value": round(world * in_bytes / e2e_s / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": in_bytes + 4 * w.seq, "d2h_bytes_per_step": in_bytes,
+        d.barrier()
+        e2e_s = max(r[0] for r in d.gather([e2e_s]))
+        e2e = {"value": round(d.world * in_bytes_rank / e2e_s / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": in_bytes_rank + 4 * w.seq, "d2h_bytes_per_step": in_bytes_rank,
                "ms_per_step": round(1e3 * e2e_s, 3), "steps": args.e2e_steps,
                "path": "quantize_hf_cache(host pinned legacy cache, output='legacy') -> host tensors"}
 
-    if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
+    if d.rank != 0:
+        d.close()
         return
-    ms = elapsed_ms / args.steps
-    peak, peak_kind = measured_peak()
-    q_ms, dq_ms, sel_ms = t_q / args.steps, t_dq / args.steps, t_sel / args.steps
-    algo_q = in_bytes + comp_bytes
-    algo_dq = comp_bytes + in_bytes
-    phases = {
-        "select": {"ms": round(sel_ms, 4)},
-        "quantize": {"ms": round(q_ms, 4), "input_gbs": round(in_bytes / q_ms / 1e6, 1),
-                     "algo_gbs": round(algo_q / q_ms / 1e6, 1), "frac": round(algo_q / q_ms / 1e6 / peak, 4)},
-        "dequant": {"ms": round(dq_ms, 4), "input_gbs": round(in_bytes / dq_ms / 1e6, 1),
-                    "algo_gbs": round(algo_dq / dq_ms / 1e6, 1), "frac": round(algo_dq / dq_ms / 1e6 / peak, 4)},
-    }
+    q_ms, dq_ms = phases["quantize"]["ms"], phases["dequant"]["ms"]
+    algo = in_bytes_rank + head["comp_bytes"]
     dominant = "quantize" if q_ms >= dq_ms else "dequant"
+    nr = head["nr"]
     dom_ms = (q_ms if dominant == "quantize" else dq_ms) / nr
-    dom_bytes = (algo_q if dominant == "quantize" else algo_dq) / nr
+    dom_bytes = algo / nr
     achieved = dom_bytes / dom_ms / 1e6
     traffic = committed_traffic(args.workload).get(dominant)
     roofline = {"bound": "hbm",
@@ -372,7 +463,7 @@ def run_ours(args):
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
                 "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes}
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if d.world == 1 and not args.no_cpu_baseline:
         workers = os.cpu_count() or 1
         gbs, wall, nb = cpu_sample(args.workload, workers * 2, workers)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": workers, "kind": "port",
@@ -381,30 +472,31 @@ def run_ours(args):
                          f"{workers} processes, {wall:.1f} s"}
     line = {
         "metric": METRIC,
-        "value": round(world * in_bytes / (ms * 1e6), 2),
+        "value": round(d.world * in_bytes_rank / (ms * 1e6), 2),
         "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": args.workload, "layers": w.layers, "kv_heads": w.heads, "head_dim": w.head_dim,
                    "batch_per_gpu": w.batch, "seq_len": w.seq, "profile": w.profile,
-                   "input_bytes_per_gpu": in_bytes, "compressed_bytes_per_gpu": comp_bytes,
+                   "input_bytes_per_gpu": in_bytes_rank, "compressed_bytes_per_gpu": head["comp_bytes"],
                    "l2": "inputs (1.88 GB) larger than L2; no flush",
-                   "value_definition": "K+V input bytes of all ranks / device time of one "
+                   "value_definition": "K+V input bytes of all ranks / max over ranks of the device time of one "
                                        "select+quantize+pack+dequant step",
-                   "parallelism": f"weak shards of (layer, kv-head) units over {world} GPU(s)"},
+                   "parallelism": f"weak shards of (layer, kv-head) units over {d.world} GPU(s)"},
         "phases": phases,
+        "rank_ms": [round(r[0], 4) for r in head["per_rank"]],
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * launches,
-        "cache_stats": combine_stats(gathered.cpu()) if world > 1 else None,
-        "clocks": clocks.summary(),
+        "strong": strong,
+        "gpu_launches": args.steps * head["launches"],
+        "cache_stats": head["stats"],
+        "clocks": head["clocks"],
     }
     print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    d.close()
 
 
 def main():

@@ -66,6 +66,7 @@ _PROTOTYPES = {
     "gkv_select_tiers": (c_i32, [c_ptr, c_ptr, ctypes.POINTER(SelectPolicy), c_ptr, c_ptr, c_ptr, c_ptr,
                                  ctypes.c_size_t, c_ptr]),
     "gkv_select_tiers_static": (c_i32, [c_ptr, c_ptr, ctypes.POINTER(SelectPolicy), c_ptr, c_ptr, c_ptr, c_ptr]),
+    "gkv_mean_scores": (c_i32, [c_ptr, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "gkv_outlier_scores": (c_i32, [ctypes.POINTER(LayerIn), c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "gkv_quantize_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Plan), ctypes.POINTER(LayerIn), c_i32]),
     "gkv_quantize": (c_i32, [ctypes.POINTER(Plan), ctypes.POINTER(LayerIn), c_i32, c_ptr, ctypes.c_size_t, c_ptr]),

@@ -121,8 +121,9 @@ class QuantizedTensor:
             plan.zero_points[slot] = L.ptr(self.zero_points)
         plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
         out = torch.empty((2, B, H, n, D), dtype=self.original_dtype, device=dev)
-        L.check(lib.gkv_dequantize(ctypes.byref(plan), B * H, out[0].data_ptr(), out[1].data_ptr(), None, 0,
-                                   L.stream_handle(dev)))
+        with torch.cuda.device(dev):
+            L.check(lib.gkv_dequantize(ctypes.byref(plan), B * H, out[0].data_ptr(), out[1].data_ptr(), None, 0,
+                                       L.stream_handle(dev)))
         return out[0]
 
 
@@ -502,16 +503,52 @@ def _cache_layer_seq_length(layer: object, keys: torch.Tensor) -> int:
 # selection helpers with the reference's signatures
 # ---------------------------------------------------------------------------
 
+def _sum_last_block(rows: int, cols: int, threads: int) -> int:
+    """First column of the last per-thread column block of torch's CPU reduction
+    of a contiguous [rows, cols] tensor over rows: at::parallel_for splits the
+    columns into ceil(cols / threads)-wide blocks whose ends are rounded down to
+    32 columns (the last end excepted); small reductions (fewer than 32768
+    elements) and single-threaded runs form one block."""
+    if rows * cols < 32768 or threads <= 1 or cols <= 1:
+        return 0
+    nt = min(threads, cols)
+    width = -(-cols // nt)
+    last = 0
+    for tid in range(nt):
+        begin = tid * width
+        if begin >= cols:
+            break
+        end = min(cols, begin + width)
+        begin -= begin % 32
+        if end != cols:
+            end -= end % 32
+        if begin < end:
+            last = begin
+    return last
+
+
 def _normalize_token_scores(seq_len: int, scores: torch.Tensor, device: torch.device) -> torch.Tensor:
-    """core.py:1019-1031 (computed on ``device``)."""
+    """fp32 [T] scores on ``device`` (core.py:1019-1031).  Multi-dimensional
+    scores are averaged by ``gkv_mean_scores`` in the fp32 addition order of
+    torch's CPU mean for this process's thread count, so the means -- and the
+    selections that depend on their last bit -- are those of the reference run
+    on the CPU."""
     scores = scores.to(device=device, dtype=torch.float32)
     if scores.numel() == seq_len:
         return scores.reshape(seq_len)
     if scores.ndim >= 1 and scores.shape[-1] == seq_len:
-        return scores.reshape(-1, seq_len).mean(dim=0)
-    if scores.ndim >= 1 and scores.shape[0] == seq_len:
-        return scores.reshape(seq_len, -1).mean(dim=1)
-    raise ValueError("importance_scores must have one score per token or a final token dimension.")
+        x, axis, n_out = scores.reshape(-1, seq_len).contiguous(), 0, seq_len
+    elif scores.ndim >= 1 and scores.shape[0] == seq_len:
+        x, axis, n_out = scores.reshape(seq_len, -1).contiguous(), 1, seq_len
+    else:
+        raise ValueError("importance_scores must have one score per token or a final token dimension.")
+    rows, cols = x.shape
+    last = _sum_last_block(rows, cols, torch.get_num_threads()) if axis == 0 else 0
+    out = torch.empty(n_out, dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        L.check(L.lib().gkv_mean_scores(x.data_ptr(), rows, cols, axis, last, out.data_ptr(),
+                                        L.stream_handle(device)))
+    return out
 
 
 def _select(T: int, config: KvQuantConfig, scores: torch.Tensor | None, device: torch.device,
@@ -526,9 +563,10 @@ def _select(T: int, config: KvQuantConfig, scores: torch.Tensor | None, device: 
     idx_ret, idx_std, idx_cold = torch.split(idx, [tiers.n_retained, tiers.n_standard, tiers.n_cold])
     ws = torch.empty(max(int(lib.gkv_select_workspace_bytes(T)), 1), dtype=torch.uint8, device=device)
     pol = tiers.policy()
-    L.check(lib.gkv_select_tiers(L.ptr(s), L.ptr(outlier), ctypes.byref(pol), idx_ret.data_ptr(),
-                                 idx_std.data_ptr(), idx_cold.data_ptr(), ws.data_ptr(), ws.numel(),
-                                 L.stream_handle(device)))
+    with torch.cuda.device(device):
+        L.check(lib.gkv_select_tiers(L.ptr(s), L.ptr(outlier), ctypes.byref(pol), idx_ret.data_ptr(),
+                                     idx_std.data_ptr(), idx_cold.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     L.stream_handle(device)))
     return tiers, idx_ret, idx_std, idx_cold
 
 
@@ -710,18 +748,20 @@ class _GroupRun:
         """Selection kernel(s) for normalized fp32 [T] scores on the device."""
         lib = L.lib()
         st = L.stream_handle(self.device)
-        if self.outlier is not None:
-            li = self.layer_ins[0]
-            B, _, T, D = self.shape
-            L.check(lib.gkv_outlier_scores(ctypes.byref(li), B, T, D, L.DTYPE_CODE[self.dtype],
-                                           self.outlier.data_ptr(), st))
-        L.check(lib.gkv_select_tiers(L.ptr(scores), L.ptr(self.outlier), ctypes.byref(self.policy),
-                                     self.idx_ret.data_ptr(), self.idx_std.data_ptr(), self.idx_cold.data_ptr(),
-                                     self.sel_ws.data_ptr(), self.sel_ws.numel(), st))
+        with torch.cuda.device(self.device):
+            if self.outlier is not None:
+                li = self.layer_ins[0]
+                B, _, T, D = self.shape
+                L.check(lib.gkv_outlier_scores(ctypes.byref(li), B, T, D, L.DTYPE_CODE[self.dtype],
+                                               self.outlier.data_ptr(), st))
+            L.check(lib.gkv_select_tiers(L.ptr(scores), L.ptr(self.outlier), ctypes.byref(self.policy),
+                                         self.idx_ret.data_ptr(), self.idx_std.data_ptr(), self.idx_cold.data_ptr(),
+                                         self.sel_ws.data_ptr(), self.sel_ws.numel(), st))
 
     def quantize(self) -> None:
-        L.check(L.lib().gkv_quantize(ctypes.byref(self.plan), self.layer_ins, len(self.pairs), self.ws.data_ptr(),
-                                     self.ws_bytes, L.stream_handle(self.device)))
+        with torch.cuda.device(self.device):
+            L.check(L.lib().gkv_quantize(ctypes.byref(self.plan), self.layer_ins, len(self.pairs),
+                                         self.ws.data_ptr(), self.ws_bytes, L.stream_handle(self.device)))
 
     def dequantize(self) -> None:
         """Dequantize every layer of the run into preallocated [L, B, H, T, D] outputs."""
@@ -730,8 +770,9 @@ class _GroupRun:
             self.out_k = torch.empty(shp, dtype=self.dtype, device=self.device)
             self.out_v = torch.empty(shp, dtype=self.dtype, device=self.device)
         B, H = self.shape[:2]
-        L.check(L.lib().gkv_dequantize(ctypes.byref(self.plan), len(self.pairs) * B * H, self.out_k.data_ptr(),
-                                       self.out_v.data_ptr(), None, 0, L.stream_handle(self.device)))
+        with torch.cuda.device(self.device):
+            L.check(L.lib().gkv_dequantize(ctypes.byref(self.plan), len(self.pairs) * B * H, self.out_k.data_ptr(),
+                                           self.out_v.data_ptr(), None, 0, L.stream_handle(self.device)))
 
     def layers(self) -> list:
         """QuantizedKvLayer objects whose tensors are views into the arena."""
@@ -900,6 +941,7 @@ def _follows(a: QuantizedKvLayer, b: QuantizedKvLayer) -> bool:
 
 def _dequantize_layers(layers: list[QuantizedKvLayer]) -> list:
     out = []
+    host_copies = set()  # GPUs whose results are being copied into host memory
     i = 0
     while i < len(layers):
         lay = layers[i]
@@ -910,10 +952,13 @@ def _dequantize_layers(layers: list[QuantizedKvLayer]) -> list:
         j = i + 1
         while j < len(layers) and layers[j].passthrough_keys is None and _follows(layers[j - 1], layers[j]):
             j += 1
-        out.extend(_dequantize_run(layers[i:j]))
+        for k, v, dev in _dequantize_run(layers[i:j]):
+            if k.device.type == "cpu":
+                host_copies.add(dev)
+            out.append((k, v))
         i = j
-    if any(o[0].device.type == "cpu" for o in out):
-        torch.cuda.synchronize()
+    for dev in host_copies:
+        torch.cuda.synchronize(dev)
     return out
 
 
@@ -947,8 +992,9 @@ def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
     nl = len(run)
     outk = torch.empty((nl, B, H, T, D), dtype=dtype, device=dev)
     outv = torch.empty((nl, B, H, T, D), dtype=dtype, device=dev)
-    L.check(lib.gkv_dequantize(ctypes.byref(plan), nl * B * H, outk.data_ptr(), outv.data_ptr(), None, 0,
-                               L.stream_handle(dev)))
+    with torch.cuda.device(dev):
+        L.check(lib.gkv_dequantize(ctypes.byref(plan), nl * B * H, outk.data_ptr(), outv.data_ptr(), None, 0,
+                                   L.stream_handle(dev)))
     home = first.home_device
     if home is not None and home.type == "cpu":
         hk = torch.empty(outk.shape, dtype=dtype, pin_memory=True)
@@ -956,7 +1002,7 @@ def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
         hk.copy_(outk, non_blocking=True)
         hv.copy_(outv, non_blocking=True)
         outk, outv = hk, hv
-    return [(outk[l], outv[l]) for l in range(nl)]
+    return [(outk[l], outv[l], dev) for l in range(nl)]
 
 
 HOST_CHUNK_BYTES = 64 << 20  # K+V bytes per stage of the pipelined host round trip (at least one layer)

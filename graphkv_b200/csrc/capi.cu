@@ -2,6 +2,7 @@
 // argument validation, routing of each tier to the tile kernels or the general
 // kernels, workspace layout, and launches.  Nothing here allocates device memory.
 // The library is one translation unit: the kernel sources are included below.
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <string>
@@ -9,21 +10,23 @@
 #include "dequantize.cuh"
 #include "gkv_params.cuh"
 #include "quantize.cuh"
+#include "scores.cuh"
 #include "select.cuh"
 
 namespace gkv {
 
-// Multiprocessor count of the current device (cached per device).
+// Multiprocessor count of the current device (cached per device; host threads
+// may race to fill an entry, and they all store the same value).
 int device_sm_count() {
-  static int counts[64] = {};
+  static std::atomic<int> counts[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (counts[dev] == 0) {
-    int n = 0;
+  int n = counts[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    counts[dev] = n;
+    counts[dev].store(n, std::memory_order_relaxed);
   }
-  return counts[dev];
+  return n;
 }
 
 namespace {
@@ -258,6 +261,18 @@ int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const
   cudaError_t e = launch_select(scores, outlier_scores, p, idx_retained, idx_standard, idx_cold,
                                 static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? GKV_OK : cuda_fail(e, "select kernel launch");
+}
+
+int32_t gkv_mean_scores(const float* scores, int32_t rows, int32_t cols, int32_t axis, int32_t last_block,
+                        float* out, gkv_stream_t stream) {
+  if (!scores || !out) return fail(GKV_ERR_INVALID, "NULL argument");
+  if (rows < 1 || cols < 1) return fail(GKV_ERR_INVALID, "rows and cols must be >= 1");
+  if (axis != 0 && axis != 1) return fail(GKV_ERR_INVALID, "axis must be 0 or 1");
+  if (axis == 0 && (last_block < 0 || last_block >= cols || last_block % 32))
+    return fail(GKV_ERR_INVALID, "last_block must be a multiple of 32 in [0, cols)");
+  cudaError_t e = launch_mean_scores(scores, rows, cols, axis, axis == 0 ? last_block : 0, out,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GKV_OK : cuda_fail(e, "score mean kernel launch");
 }
 
 int32_t gkv_outlier_scores(const gkv_layer_in* layer, int32_t batch, int32_t seq_len, int32_t head_dim,

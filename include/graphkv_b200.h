@@ -164,14 +164,27 @@ int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
  *    before any stream capture.
- *  - All calls share the one array: calls whose kernels can overlap on the GPU
- *    (different streams, or several host threads) race and must be ordered by
- *    the caller.  No clearing is needed between calls: the kernel writes every
- *    token's tier byte before reading it. */
+ *  - Each GPU has its own copy of the array, shared by every call on that
+ *    GPU: calls on one GPU whose kernels can overlap (different streams, or
+ *    several host threads) race and must be ordered by the caller; calls on
+ *    different GPUs do not interact.  No clearing is needed between calls: the
+ *    kernel writes every token's tier byte before reading it. */
 #define GKV_STATIC_SELECT_MAX_TOKENS 1048576
 int32_t gkv_select_tiers_static(const float* scores, const float* outlier_scores, const gkv_select_policy* policy,
                                 int32_t* idx_retained, int32_t* idx_standard, int32_t* idx_cold,
                                 gkv_stream_t stream);
+
+/* Mean of fp32 scores [rows, cols] (contiguous) over axis 0 (-> [cols]) or
+ * axis 1 (-> [rows]).  Replaces the averaging of multi-dimensional importance
+ * scores in _normalize_token_scores (core.py:1027-1030: reshape(-1, T).mean(0)
+ * and reshape(T, -1).mean(1)), bit-identical to torch's CPU mean: the sums
+ * follow the fp32 addition order of ATen's CPU cascade sum, then one division
+ * by the count.  last_block (axis 0 only): first column of the last per-thread
+ * column block of that CPU reduction, a multiple of 32 that depends on the
+ * thread count (0 for a single-threaded reduction); the Python layer derives
+ * it from torch.get_num_threads(). */
+int32_t gkv_mean_scores(const float* scores, int32_t rows, int32_t cols, int32_t axis, int32_t last_block,
+                        float* out, gkv_stream_t stream);
 
 /* Per-token outlier score mean(K^2) + mean(V^2) over (batch, head, head_dim)
  * for one layer, fp32 [T].  Replaces _kv_outlier_scores (core.py:1051-1054);

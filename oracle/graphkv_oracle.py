@@ -309,15 +309,142 @@ def boundary_tie(scores: np.ndarray, k: int, largest: bool) -> bool:
     return bool(keys[order[k - 1]] == keys[order[k]])
 
 
-def normalize_token_scores(T: int, scores: np.ndarray) -> np.ndarray:
-    """core.py:1019-1031 (the [..., T] mean is an fp32 reduction)."""
+# ---------------------------------------------------------------------------
+# torch's CPU fp32 sum, restated in its summation order.  The reference averages
+# [..., T] / [T, ...] scores with Tensor.mean (core.py:1027-1030), which on the CPU
+# is sum (ATen's cascade_sum, native/cpu/SumKernel.cpp) followed by one division
+# by the element count.  The order of the fp32 additions is:
+#  * cascade (multi_row_sum): rows are added one by one into level 0; after every
+#    2^p rows (p = max(4, ceil_log2(n) // 4)) level j-1 is folded into level j
+#    while the row count is a multiple of 2^(p*j); leftover rows go into level 0;
+#    finally level 0 += level 1, += level 2, += level 3;
+#  * row_sum: four interleaved cascades over rows 4i+k, leftover rows added to
+#    partial 0, then partial 0 += partial 1, += 2, += 3;
+#  * outer reduction ([R, T] over R): columns are split into per-thread blocks
+#    (at::parallel_for over columns, block ends rounded down to 32 columns unless
+#    at the end); inside a block, whole groups of 32 columns take the cascade and
+#    the rest of the block takes row_sum (a block narrower than 8 columns: whole
+#    groups of 4 columns cascade);
+#  * inner reduction ([T, X] over X): 8-lane vectors (the sum kernel is the AVX2
+#    one on every x86 host), lane l is a row_sum over elements 8v + l, the
+#    leftover X % 8 elements are added into a scalar starting at 0, followed by
+#    lanes 0..7; X < 8: one scalar row_sum;
+#  * the output is pre-filled with 0 and receives 0 + sum.
+# ---------------------------------------------------------------------------
+SUM_LANES = 8
+SUM_GRAIN = 32768      # at::internal::GRAIN_SIZE
+SUM_THREADS = 1        # at::get_num_threads() of the process that ran the reference (set by the tests)
+
+
+def _ceil_log2(x: int) -> int:
+    return 1 if x <= 2 else int(x - 1).bit_length()
+
+
+def _cascade(rows: list) -> np.ndarray:
+    n = len(rows)
+    p = max(4, _ceil_log2(n) // 4)
+    step, mask = 1 << p, (1 << p) - 1
+    acc = [np.zeros_like(rows[0]) for _ in range(4)]
+    i = 0
+    while i + step <= n:
+        for _ in range(step):
+            acc[0] = (acc[0] + rows[i]).astype(F32)
+            i += 1
+        for j in range(1, 4):
+            acc[j] = (acc[j] + acc[j - 1]).astype(F32)
+            acc[j - 1] = np.zeros_like(acc[j - 1])
+            if i & (mask << (j * p)):
+                break
+    while i < n:
+        acc[0] = (acc[0] + rows[i]).astype(F32)
+        i += 1
+    for j in range(1, 4):
+        acc[0] = (acc[0] + acc[j]).astype(F32)
+    return acc[0]
+
+
+def _row_sum(rows: list) -> np.ndarray:
+    n4 = len(rows) // 4
+    parts = [_cascade(rows[k::4][:n4]) if n4 else np.zeros_like(rows[0]) for k in range(4)]
+    for i in range(4 * n4, len(rows)):
+        parts[0] = (parts[0] + rows[i]).astype(F32)
+    for k in range(1, 4):
+        parts[0] = (parts[0] + parts[k]).astype(F32)
+    return parts[0]
+
+
+def sum_last_block(rows: int, cols: int, threads: int) -> int:
+    """First column of the last per-thread block of an outer reduction."""
+    if rows * cols < SUM_GRAIN or threads <= 1 or cols <= 1:
+        return 0
+    nt = min(threads, cols)
+    cs = -(-cols // nt)
+    last = 0
+    for tid in range(nt):
+        b, e = tid * cs, min(cols, tid * cs + cs)
+        if b >= cols:
+            continue
+        b -= b % 32
+        if e != cols:
+            e -= e % 32
+        if b < e:
+            last = b
+    return last
+
+
+def torch_cpu_sum(x: np.ndarray, axis: int, threads: int) -> np.ndarray:
+    """Sum of a contiguous fp32 [R, C] array over `axis` in torch's CPU order."""
+    x = np.ascontiguousarray(x, dtype=F32)
+    if axis == 0:
+        R, C = x.shape
+        out = np.zeros(C, F32)
+        blocks, b0 = [], 0
+        last = sum_last_block(R, C, threads)
+        for b in range(0, last, 32):  # blocks before the last one are whole 32-column groups
+            blocks.append((b, b + 32))
+        blocks.append((last, C))
+        for b, e in blocks:
+            n = e - b
+            if n >= SUM_LANES:
+                a_end = n // (4 * SUM_LANES) * (4 * SUM_LANES)
+            else:
+                a_end = n // 4 * 4
+            rows = [x[r, b:e] for r in range(R)]
+            res = np.empty(n, F32)
+            if a_end:
+                res[:a_end] = _cascade([r[:a_end] for r in rows])
+            if n > a_end:
+                res[a_end:] = _row_sum([r[a_end:] for r in rows])
+            out[b:e] = (out[b:e] + res).astype(F32)
+        return out
+    T, X = x.shape
+    cols = [x[:, c] for c in range(X)]
+    if X >= SUM_LANES:
+        nv = X // SUM_LANES
+        fin = np.zeros(T, F32)
+        for c in range(nv * SUM_LANES, X):
+            fin = (fin + cols[c]).astype(F32)
+        for lane in range(SUM_LANES):
+            fin = (fin + _row_sum([cols[v * SUM_LANES + lane] for v in range(nv)])).astype(F32)
+    else:
+        fin = _row_sum(cols)
+    return (np.zeros(T, F32) + fin).astype(F32)
+
+
+def normalize_token_scores(T: int, scores: np.ndarray, threads: Optional[int] = None) -> np.ndarray:
+    """core.py:1019-1031: scores as fp32 [T]; [..., T] and [T, ...] scores are
+    averaged over the other dimension as torch's CPU mean does (sum in the order
+    above, then one fp32 division by the count)."""
     s = np.asarray(scores, dtype=np.float32)
+    th = SUM_THREADS if threads is None else threads
     if s.size == T:
         return s.reshape(T)
     if s.ndim >= 1 and s.shape[-1] == T:
-        return s.reshape(-1, T).mean(axis=0, dtype=np.float32)
+        x = s.reshape(-1, T)
+        return (torch_cpu_sum(x, 0, th) / F32(x.shape[0])).astype(F32)
     if s.ndim >= 1 and s.shape[0] == T:
-        return s.reshape(T, -1).mean(axis=1, dtype=np.float32)
+        x = s.reshape(T, -1)
+        return (torch_cpu_sum(x, 1, th) / F32(x.shape[1])).astype(F32)
     raise ValueError("importance_scores must have one score per token or a final token dimension.")
 
 

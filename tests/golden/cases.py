@@ -33,6 +33,7 @@ class Case:
     workload: str = ""                      # full-size workload key (digest-only case)
     layer_subset: tuple = ()                # layers of the workload to record (empty = all)
     full_arrays: bool = True                # store whole arrays (small cases) or digests only
+    score_rows: int = 0                     # rows_adv / tx_adv: size of the averaged dimension
 
 
 def _gen(seed):
@@ -97,7 +98,28 @@ def case_scores(c: Case):
         return torch.exp(torch.randn(H, T, generator=g))
     if c.scores == "per_layer":
         return [torch.exp(2.0 * torch.randn(T, generator=g)) for _ in range(c.layers)]
+    if c.scores in ("rows_adv", "tx_adv", "rows3_adv"):
+        vals = adversarial_score_rows(T, c.score_rows, g)  # [T, R]
+        if c.scores == "tx_adv":
+            return vals.contiguous()
+        rows = vals.t().contiguous()
+        return rows.reshape(2, c.score_rows // 2, T) if c.scores == "rows3_adv" else rows
     raise ValueError(c.scores)
+
+
+def adversarial_score_rows(T: int, R: int, g: torch.Generator) -> torch.Tensor:
+    """[T, R] fp32 scores whose per-token means tie in exact arithmetic within a
+    few levels and differ only through fp32 rounding: every token's R values are
+    one fixed multiset of magnitudes from 1e-2 to 1e4 with alternating signs, in
+    a different order per token, plus one of six base levels.  The selection
+    boundaries fall inside a level, so which tokens are kept is decided by the
+    order of the fp32 additions of the mean."""
+    mags = torch.pow(10.0, torch.rand(R, generator=g, dtype=torch.float64) * 6.0 - 2.0)
+    signs = torch.where(torch.arange(R) % 2 == 0, 1.0, -1.0).double()
+    multiset = (mags * signs).float()
+    base = 1.0 + 0.25 * torch.randint(0, 6, (T,), generator=g).float()
+    order = torch.argsort(torch.rand(T, R, generator=g), dim=1)
+    return multiset[order] + base[:, None]
 
 
 def tensor_digest(arr: np.ndarray) -> str:
@@ -153,6 +175,11 @@ CASES = [
     Case("scores_heads", "graphkv", (1, 2, 8192, 64), "bf16", scores="heads"),
     Case("scores_per_layer", "graphkv", (1, 1, 8192, 64), "bf16", layers=2, scores="per_layer"),
     Case("scores_ties", "graphkv", (1, 1, 8192, 64), "bf16", scores="ties"),
+    Case("scores_rows64_adv", "graphkv", (1, 1, 8192, 64), "bf16", scores="rows_adv", score_rows=64),
+    Case("scores_rows8_tail5", "graphkv", (1, 1, 8197, 64), "bf16", scores="rows_adv", score_rows=8),
+    Case("scores_rows3d_adv", "graphkv", (1, 2, 8192, 64), "bf16", scores="rows3_adv", score_rows=48),
+    Case("scores_tx27_adv", "graphkv", (1, 1, 8192, 64), "bf16", scores="tx_adv", score_rows=27),
+    Case("scores_tx5_adv", "graphkv", (1, 1, 8192, 64), "bf16", scores="tx_adv", score_rows=5),
     Case("cold_bits_mix", "graphkv", (1, 1, 8192, 64), "bf16", scores="lognormal",
          overrides={"low_priority_bits": 2, "low_priority_key_bits": 8, "group_size": 32}),
     # --- full-size workloads, digests only ------------------------------------------------

@@ -2,7 +2,7 @@
 
 Run in a container where the reference package is importable (pure Python):
 
-    python tests/golden/make_golden.py [--src /root/reference/src] [--only NAME ...]
+    python tests/golden/make_golden.py --src <reference>/src [--only NAME ...]
 
 For every case in ``cases.py`` this imports the reference ``graphkv`` package,
 runs ``quantize_kv_layer`` (``core.py:647-772``) layer by layer on the seeded
@@ -126,13 +126,18 @@ def run_case(ref, ref_core, case):
     rec["stats"] = cache.stats()
     T = layers[0][0].shape[2]
     rec["ties"] = boundary_ties(ref_core, T, cfg, scores)
+    rec["torch_threads"] = torch.get_num_threads()  # sets the column blocks of a CPU mean over rows
+    if isinstance(scores, torch.Tensor) and scores.numel() != T:
+        mean_bits = bits_of(ref_core._normalize_token_scores(T, scores, torch.device("cpu")))
+        rec["score_mean"] = tensor_digest(mean_bits)
+        arrays["score_mean"] = mean_bits
     rec["seconds"] = round(time.time() - t0, 2)
     return rec, arrays
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default=os.environ.get("GRAPHKV_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--src", required=True, help="the reference package's src directory (holds graphkv/)")
     ap.add_argument("--only", nargs="*")
     ap.add_argument("--small", action="store_true", help="only the small (non-workload) cases")
     args = ap.parse_args()

@@ -2,7 +2,7 @@
 
 Run where the reference package is importable (pure Python, CPU):
 
-    python tests/golden/make_graph_golden.py [--src <reference>/src]
+    python tests/golden/make_graph_golden.py --src <reference>/src
 
 For each case: the scorer's parameter names and shapes, the query/candidate
 fact banks (``graph_model.py:362-422``), the raw chunk scores of
@@ -104,7 +104,7 @@ def run(ref_pkg, gm, c) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default=os.environ.get("GRAPHKV_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--src", required=True, help="the reference package's src directory (holds graphkv/)")
     args = ap.parse_args()
     sys.path.insert(0, args.src)
     import graphkv as ref_pkg

@@ -3,6 +3,7 @@ from __future__ import annotations
 
 import json
 import os
+from contextlib import contextmanager
 from dataclasses import replace
 
 import numpy as np
@@ -76,3 +77,19 @@ def compare_arrays(name, mine: dict, golden_layer: dict, golden_arrays: dict, li
                     detail = f" (shape {a.shape} vs {g.shape})"
             problems.append(f"{name} l{li}: {n} digest mismatch dtype {a.dtype}/{gt[n]['dtype']}{detail}")
     return problems
+
+
+@contextmanager
+def reference_threads(rec: dict):
+    """Run with the torch CPU thread count the golden was recorded with: it sets
+    the column blocks of torch's CPU mean over score rows, which both the oracle
+    and the library's score averaging follow."""
+    n = int(rec.get("torch_threads", torch.get_num_threads()))
+    old_torch, old_oracle = torch.get_num_threads(), orc.SUM_THREADS
+    torch.set_num_threads(n)
+    orc.SUM_THREADS = n
+    try:
+        yield n
+    finally:
+        torch.set_num_threads(old_torch)
+        orc.SUM_THREADS = old_oracle

@@ -146,3 +146,54 @@ def test_quantize_hf_cache_takes_the_pipeline_for_pinned_host_caches(monkeypatch
         g.quantize_hf_cache(pinned, "graphkv", importance_scores=scores, output="static")
     with pytest.raises(ValueError, match="implementation must be"):
         g.quantize_hf_cache(pinned, "graphkv", importance_scores=scores, output="paged")
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tensors_on_another_gpu_than_the_current_one():
+    """Every call runs on the GPU that holds its tensors, whichever GPU is
+    current: cache on cuda:1 with cuda:0 current gives the same bytes as on cuda:0."""
+    cache0 = _small_cache(T=4096, layers=2)
+    scores = torch.exp(torch.randn(4, 4096, generator=torch.Generator().manual_seed(2)))
+    torch.cuda.set_device(0)
+    ref = g.quantize_hf_cache(cache0, "graphkv", importance_scores=scores.cuda(0), output="compressed")
+    cache1 = tuple((k.to("cuda:1"), v.to("cuda:1")) for k, v in cache0)
+    other = g.quantize_hf_cache(cache1, "graphkv", importance_scores=scores.cuda(1), output="compressed")
+    assert torch.cuda.current_device() == 0
+    for la, lb in zip(ref.layers, other.layers):
+        assert lb.compressed_keys.q.device == torch.device("cuda:1")
+        assert torch.equal(la.retained_indices.cpu(), lb.retained_indices.cpu())
+        assert torch.equal(la.compressed_keys.q.cpu(), lb.compressed_keys.q.cpu())
+        assert torch.equal(la.low_priority_compressed_values.q.cpu(), lb.low_priority_compressed_values.q.cpu())
+    for (ka, va), (kb, vb) in zip(ref.dequantize(), other.dequantize()):
+        assert kb.device == torch.device("cuda:1")
+        assert torch.equal(ka.cpu(), kb.cpu()) and torch.equal(va.cpu(), vb.cpu())
+    host = g.quantize_hf_cache(tuple((k.cpu(), v.cpu()) for k, v in cache1), "graphkv-int4-balanced",
+                               output="legacy")
+    assert host[0][0].device.type == "cpu"
+    with torch.cuda.device(1):
+        assert L.device_error() == 0
+    assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_pieces_rebuild_the_whole_cache(world):
+    """Every rank's ShardedKvCache (built here in one process, one after the
+    other) dequantizes to its slice of the unsharded result, and the summed
+    per-layer counters give exactly the unsharded stats()."""
+    from graphkv_b200.sharding import ShardedKvCache, shard_units, stats_from_rows
+
+    cache = _small_cache(T=8192, layers=3)
+    scores = torch.exp(2 * torch.randn(8192, generator=torch.Generator().manual_seed(4))).cuda()
+    cfg = g.get_profile("graphkv").config
+    whole = g.QuantizedKvCache.from_past_key_values(cache, cfg, scores)
+    whole_deq = whole.dequantize()
+    rows = 0
+    for rank in range(world):
+        units = shard_units(3, 2, world, rank)
+        pieces = [(cache[l][0][:, h0:h1], cache[l][1][:, h0:h1]) for l, h0, h1 in units]
+        sh = ShardedKvCache.from_past_key_values(pieces, units, 3, 2, cfg, scores)
+        rows = rows + sh.stat_rows()
+        for (k, v), (l, h0, h1) in zip(sh.dequantize(), units):
+            assert torch.equal(k, whole_deq[l][0][:, h0:h1]) and torch.equal(v, whole_deq[l][1][:, h0:h1])
+    assert stats_from_rows(rows) == whole.stats()
+    assert L.device_error() == 0

@@ -16,7 +16,7 @@ from graphkv_b200 import _lib as L
 from oracle import graphkv_oracle as orc
 from tests.golden.cases import CASES, CASE_BY_NAME, bits_of, case_layers, case_scores, tensor_digest
 from tests.helpers import config_for, layer_arrays
-from tests.oracle_bridge import compare_arrays, load_golden, oracle_arrays, oracle_layers, scores_np
+from tests.oracle_bridge import compare_arrays, load_golden, oracle_arrays, oracle_layers, reference_threads, scores_np
 
 pytestmark = pytest.mark.gpu
 
@@ -32,9 +32,10 @@ def _to_cuda(scores):
     return scores.cuda()
 
 
-def _run(case, layers, scores):
+def _run(case, layers, scores, rec):
     pairs = [(k.cuda(), v.cuda()) for k, v in layers]
-    cache = QuantizedKvCache.from_past_key_values(pairs, config_for(case), _to_cuda(scores))
+    with reference_threads(rec):  # the averaging of multi-dimensional scores follows the recorded thread count
+        cache = QuantizedKvCache.from_past_key_values(pairs, config_for(case), _to_cuda(scores))
     deq = cache.dequantize()
     torch.cuda.synchronize()
     assert L.device_error() == 0
@@ -57,10 +58,11 @@ def _check_against_golden(case, cache, deq, rec, arrays):
 def test_small_cases_match_reference(case):
     rec, arrays = load_golden(case.name)
     layers = case_layers(case)
-    cache, deq = _run(case, layers, case_scores(case))
+    cache, deq = _run(case, layers, case_scores(case), rec)
     problems = _check_against_golden(case, cache, deq, rec, arrays)
     if problems:  # locate the first differing element against the oracle
-        qls = oracle_layers(case, layers, scores_np(case_scores(case)))
+        with reference_threads(rec):
+            qls = oracle_layers(case, layers, scores_np(case_scores(case)))
         for li, ql in enumerate(qls):
             mine, ref = layer_arrays(cache.layers[li]), oracle_arrays(ql)
             for name in sorted(ref):
@@ -77,7 +79,7 @@ def test_full_workloads_match_reference(case):
     layers = case_layers(case)
     for li, (k, v) in enumerate(layers):
         assert tensor_digest(bits_of(k)) == rec["layers"][li]["inputs"]["k"], "input generation drifted"
-    cache, deq = _run(case, layers, case_scores(case))
+    cache, deq = _run(case, layers, case_scores(case), rec)
     problems = _check_against_golden(case, cache, deq, rec, {})
     assert not problems, problems[:10]
 
@@ -88,6 +90,6 @@ def test_batch8_131k_layer_matches_reference():
     case = CASE_BY_NAME["w_qwen7b_8x131k_l0"]
     rec, _ = load_golden(case.name)
     layers = case_layers(case)
-    cache, deq = _run(case, layers, case_scores(case))
+    cache, deq = _run(case, layers, case_scores(case), rec)
     problems = _check_against_golden(case, cache, deq, rec, {})
     assert not problems, problems[:10]

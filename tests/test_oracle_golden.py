@@ -5,7 +5,7 @@ import torch
 
 from oracle import graphkv_oracle as orc
 from tests.golden.cases import CASES, case_layers, case_scores, tensor_digest
-from tests.oracle_bridge import compare_arrays, load_golden, oracle_arrays, oracle_layers, scores_np
+from tests.oracle_bridge import compare_arrays, load_golden, oracle_arrays, oracle_layers, reference_threads, scores_np
 
 SMALL = [c for c in CASES if not c.workload]
 
@@ -17,7 +17,8 @@ def test_oracle_matches_reference(case):
     for li, (k, v) in enumerate(layers):
         from tests.golden.cases import bits_of
         assert tensor_digest(bits_of(k)) == rec["layers"][li]["inputs"]["k"], "input generation drifted"
-    qls = oracle_layers(case, layers, scores_np(case_scores(case)))
+    with reference_threads(rec):
+        qls = oracle_layers(case, layers, scores_np(case_scores(case)))
     problems = []
     for li, ql in enumerate(qls):
         problems += compare_arrays(case.name, oracle_arrays(ql), rec["layers"][li], arrays, li)

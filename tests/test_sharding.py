@@ -1,5 +1,7 @@
-"""Weak sharding by (layer, kv-head) and the all-gather of per-shard byte counts
-(the multi-GPU path of the benchmark), run as two gloo ranks on the CPU."""
+"""Sharding by (layer, kv-head) unit and the one all-gather of per-layer counts
+that rebuilds the whole cache's stats() (run as gloo ranks on the CPU).  The
+single-process statistics the ranks must reproduce are the reference's own,
+recorded for the 16k and 32k Qwen2.5-7B-shaped workloads."""
 import os
 
 import pytest
@@ -8,9 +10,10 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from graphkv_b200 import get_profile
-from graphkv_b200.sharding import combine_stats, shard_bytes, shard_stats, shard_units
-
-GEOM = dict(layers=3, heads=4, batch=2, seq=9000, dim=64)
+from graphkv_b200.sharding import (STAT_FIELDS, gather_stat_rows, planned_piece_row, shard_units,
+                                   stats_from_rows)
+from graphkv_b200.workloads import WORKLOADS
+from tests.oracle_bridge import load_golden
 
 
 @pytest.mark.parametrize("layers,heads", [(1, 1), (3, 4), (28, 4), (5, 8)])
@@ -25,41 +28,53 @@ def test_shards_partition_the_units(layers, heads, world):
     assert len(seen) == len(set(seen))
 
 
-def _whole_cache_bytes(cfg):
-    g = GEOM
-    comp = orig = 0
-    for _ in range(g["layers"]):
-        c, o = shard_bytes((g["batch"], g["heads"], g["seq"], g["dim"]), torch.bfloat16, cfg, True, 0)
-        comp, orig = comp + c, orig + o
-    return comp, orig
+def _rank_rows(wkey, world, rank, profile=None):
+    w = WORKLOADS[wkey]
+    cfg = get_profile(profile or w.profile).config
+    rows = torch.zeros(w.layers, len(STAT_FIELDS), dtype=torch.int64)
+    for layer, h0, h1 in shard_units(w.layers, w.heads, world, rank):
+        piece = (w.batch, h1 - h0, w.seq, w.head_dim)
+        rows[layer] += torch.tensor(planned_piece_row(piece, w.dtype, cfg, w.with_scores, h0, w.heads))
+    return rows
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, wkey, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg = get_profile("graphkv").config
-        g = GEOM
-        comp = orig = 0
-        for layer, h0, h1 in shard_units(g["layers"], g["heads"], world, rank):
-            c, o = shard_bytes((g["batch"], h1 - h0, g["seq"], g["dim"]), torch.bfloat16, cfg, True, h0)
-            comp, orig = comp + c, orig + o
-        gathered = torch.empty(world * 2, dtype=torch.float64)
-        dist.all_gather_into_tensor(gathered, shard_stats(comp, orig))
-        out[rank] = combine_stats(gathered)
+        out[rank] = stats_from_rows(gather_stat_rows(_rank_rows(wkey, world, rank)))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("wkey,golden", [("qwen7b-16k", "w_qwen7b_16k"), ("qwen7b-32k", "w_qwen7b_32k")])
 @pytest.mark.parametrize("world", [2, 3])
-def test_gathered_shard_bytes_equal_the_whole_cache(world):
-    port = 29400 + world + (os.getpid() % 200)
+def test_gathered_stats_equal_the_reference_stats(wkey, golden, world):
+    port = 29400 + 7 * world + len(wkey) + (os.getpid() % 200)
     with mp.Manager() as m:
         out = m.dict()
-        mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
+        mp.spawn(_rank, args=(world, port, wkey, out), nprocs=world, join=True)
         results = [out[r] for r in range(world)]
-    comp, orig = _whole_cache_bytes(get_profile("graphkv").config)
-    for r in results:  # every rank derives the same whole-cache statistics
-        assert r["shards"] == world
-        assert r["memory_bytes"] == comp and r["original_memory_bytes"] == orig
-        assert r["compression_ratio"] == pytest.approx(orig / comp)
+    rec, _ = load_golden(golden)
+    for r in results:  # every rank rebuilds exactly the reference's 12 numbers
+        assert r == rec["stats"]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8, 5])
+def test_planned_rows_of_any_split_sum_to_the_same_stats(world):
+    whole = stats_from_rows(sum(_rank_rows("qwen7b-8x131k", 1, 0) for _ in range(1)))
+    split = stats_from_rows(sum(_rank_rows("qwen7b-8x131k", world, r) for r in range(world)))
+    assert split == whole
+    assert whole["compressed_bytes"] == 15219853824.0 and whole["original_bytes"] == 60129542144.0
+
+
+def test_passthrough_is_decided_on_the_whole_layer():
+    """A layer that is not smaller as a whole stays passthrough in every piece,
+    and its tokens are counted once."""
+    cfg = get_profile("graphkv-int4-balanced").config
+    from dataclasses import replace
+    cfg = replace(cfg, bits=8, group_size=1)
+    rows = [planned_piece_row((1, 1, 16, 8), torch.bfloat16, cfg, False, h, 2) for h in (0, 1)]
+    assert rows[0] == [512, 512, 16, 0, 0] and rows[1] == [512, 512, 0, 0, 0]
+    st = stats_from_rows(torch.tensor([[a + b for a, b in zip(*rows)]]))
+    assert st["retained_tokens"] == 16.0 and st["compression_ratio"] == 1.0

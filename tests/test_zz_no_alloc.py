@@ -49,6 +49,9 @@ def _select(static: bool, scores: torch.Tensor, tiers) -> torch.Tensor:
     (9000, "graphkv-qwen7-nf4", "lognormal"),
     (131072, "graphkv", "lognormal"),
     (8192, "graphkv", "ties"),
+    # beyond 327,680 tokens the tier bytes live in the scratch array itself
+    (393216, "graphkv", "ties"),
+    (1048576, "graphkv", "lognormal"),
 ])
 def test_static_selection_matches_workspace_selection(T, profile, kind):
     g = torch.Generator().manual_seed(T)
@@ -65,15 +68,40 @@ def test_static_selection_matches_workspace_selection(T, profile, kind):
     assert L.device_error() == 0
 
 
-def test_consecutive_calls_of_different_sizes():
+@pytest.mark.parametrize("big_T,small_T", [(65536, 12000), (1048576, 400000)])
+def test_consecutive_calls_of_different_sizes(big_T, small_T):
     """The shared scratch keeps the previous call's bytes; a following smaller
-    call must not see them."""
+    call must not see them (the second pair keeps its tier bytes in the scratch)."""
     cfg = get_profile("graphkv").config
-    big = torch.exp(torch.randn(65536, generator=torch.Generator().manual_seed(1))).cuda()
-    small = torch.exp(torch.randn(12000, generator=torch.Generator().manual_seed(2))).cuda()
-    t_big, t_small = resolve_tiers(cfg, 65536, True), resolve_tiers(cfg, 12000, True)
-    _select(True, big, t_big)
+    big = torch.randint(0, 5, (big_T,), generator=torch.Generator().manual_seed(1)).float().cuda()
+    small = torch.exp(torch.randn(small_T, generator=torch.Generator().manual_seed(2))).cuda()
+    t_big, t_small = resolve_tiers(cfg, big_T, True), resolve_tiers(cfg, small_T, True)
+    assert torch.equal(_select(True, big, t_big), _select(False, big, t_big))
     assert torch.equal(_select(True, small, t_small), _select(False, small, t_small))
+    assert L.device_error() == 0
+
+
+def test_static_selection_allocates_no_device_memory():
+    """What the entry point exists for: device memory in use is the same before
+    and after a call (the outputs are allocated beforehand, by the caller)."""
+    lib = L.lib()
+    T = 131072
+    scores = torch.exp(torch.randn(T, generator=torch.Generator().manual_seed(3))).cuda()
+    tiers = resolve_tiers(get_profile("graphkv").config, T, True)
+    idx = torch.empty(T, dtype=torch.int32, device="cuda")
+    r, s, c = torch.split(idx, [tiers.n_retained, tiers.n_standard, tiers.n_cold])
+    pol = tiers.policy()
+    st = L.stream_handle(scores.device)
+    L.check(lib.gkv_select_tiers_static(scores.data_ptr(), None, ctypes.byref(pol), r.data_ptr(), s.data_ptr(),
+                                        c.data_ptr(), st))  # first call: looks up the scratch address
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        L.check(lib.gkv_select_tiers_static(scores.data_ptr(), None, ctypes.byref(pol), r.data_ptr(),
+                                            s.data_ptr(), c.data_ptr(), st))
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
     assert L.device_error() == 0
 
 
