@@ -286,9 +286,144 @@ __device__ void tok_decode(const TensorDesc& d, int s, int j0, uint8_t* tile) {
   }
 }
 
+// ---- rotated channel axis, 16-bit rows of 128 -----------------------------
+// Two threads per row, thread u (lane bit 3) decoding elements 64u .. 64u + 63
+// (one group of 64, or half of a group of 128) as 32 packed fp32 pairs.  The
+// decoded values are integer codes times one stored scale per group, so the
+// butterfly stages h = 1 .. 32, which stay inside a group, are exact in fp32
+// (at most 64 codes of magnitude <= 128 per sum, times a 16-bit-mantissa
+// scale); only h = 64 mixes the two groups' scales and rounds, as in the
+// reference.  As in the quantizer, thread 1 holds its halves swapped so that
+// both threads hand over pairs 16 .. 31, and the h = 64 stage pairs element e of
+// the two halves through the threads' own 128 bytes of the output tile row.
+template <typename T, int SB>
+__device__ void dequant_rot_pair(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows,
+                                 uint8_t* tile) {
+  using G = DGeom<T, 128>;
+  using W = Word16<T>;
+  constexpr int HB = 4 * SB;   // code bytes of 32 elements
+  constexpr int HC = HB / 4;   // code words of 32 elements
+  constexpr int EPC = 32 / SB;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = lane & 7, k = lane >> 3;
+  const int u = k & 1, rb = k >> 1;
+  const float sg = u ? -1.f : 1.f;
+  const uint64_t sgp = pk2(sg, sg), sgn = pk2(-sg, -sg);
+#pragma unroll 1
+  for (int step = warp; step < kDTile / 16; step += kDWarps) {
+    const int r = step * 16 + rb * 8 + j;
+    const bool act = r < rows;
+    uint32_t h0[HC], h1[HC];
+    float scale = 0.f;
+    int zp = 0;
+    if (act) {
+      const int64_t row = (int64_t)s * d.n + j0 + r;
+      const uint8_t* src = d.codes + ((row * d.n_pad + 64 * u) * SB) / 8;
+      load_codes<HB>(src + (u ? HB : 0), h0);
+      load_codes<HB>(src + (u ? 0 : HB), h1);
+      const int64_t gi = row * d.groups_row + ((64 * u) >> d.log2gs);
+      scale = load_scale(d.scales, gi, d.scale_dtype);
+      zp = load_zp(d, gi);
+    } else {
+#pragma unroll
+      for (int q = 0; q < HC; ++q) h0[q] = h1[q] = 0u;
+    }
+    const Decoder dc = make_decoder(d, scale, zp);
+    const uint64_t base2 = pk2(dc.base, dc.base), sc2 = pk2(dc.scale, dc.scale);
+    const uint32_t xm = SB == 8 ? dc.xor_mask : 0u;
+    uint64_t v[32];
+#pragma unroll
+    for (int q = 0; q < HC; ++q) {
+      uint32_t c0[EPC], c1[EPC];
+      word_codes<SB>(h0[q], c0);
+      word_codes<SB>(h1[q], c1);
+#pragma unroll
+      for (int e = 0; e < EPC; e += 2) {
+        v[(q * EPC + e) / 2] = decode_pair(c0[e], c0[e + 1], xm, xm, base2, sc2);
+        v[16 + (q * EPC + e) / 2] = decode_pair(c1[e], c1[e + 1], xm, xm, base2, sc2);
+      }
+    }
+    // h = 1 (inside each pair), h = 2 .. 16, h = 32 (thread 1: lower element in m + 16)
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      const float a = lo2(v[m]), b = hi2(v[m]);
+      v[m] = pk2(__fadd_rn(a, b), __fsub_rn(a, b));
+    }
+#pragma unroll
+    for (int h = 2; h < 32; h <<= 1) {
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        if ((2 * m) & h) continue;
+        const uint64_t a = v[m], b = v[m + h / 2];
+        v[m] = add2(a, b);
+        v[m + h / 2] = sub2(a, b);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const uint64_t a = v[m], b = v[m + 16];
+      v[m] = fma2(sgp, a, b);
+      v[m + 16] = fma2(sgn, b, a);
+    }
+    // Nonzero decoded values are >= 2^-24 (a code times a stored scale), so the
+    // fused quotient is exact; -0 needs a zero scale and infinities an overflowed
+    // one, and then the warp divides exactly (padding rows hold zeros only).
+    const bool fused = (p.had_fused != 0) && __all_sync(kFull, !act || (scale != 0.f && isfinite(scale)));
+    uint8_t* own = tile + r * G::kPitchB + u * 128;
+    uint4* mine = reinterpret_cast<uint4*>(own);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      mine[q] = make_uint4(lo32(v[16 + 2 * q]), hi32(v[16 + 2 * q]), lo32(v[17 + 2 * q]), hi32(v[17 + 2 * q]));
+    __syncwarp();
+    const uint4* theirs = reinterpret_cast<const uint4*>(tile + r * G::kPitchB + (u ^ 1) * 128);
+    uint32_t ws[16], wd[16];
+    const uint64_t nd2 = pk2(-p.had_div, -p.had_div), rd2 = pk2(p.had_inv, p.had_inv);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 t = theirs[q];
+      const uint64_t o0 = pk2u(t.x, t.y), o1 = pk2u(t.z, t.w);
+      uint64_t s0 = add2(v[2 * q], o0), s1 = add2(v[2 * q + 1], o1);
+      uint64_t d0 = sub2(v[2 * q], o0), d1 = sub2(v[2 * q + 1], o1);
+      if (fused) {
+        s0 = quot2(s0, nd2, rd2);
+        s1 = quot2(s1, nd2, rd2);
+        d0 = quot2(d0, nd2, rd2);
+        d1 = quot2(d1, nd2, rd2);
+      } else {
+        const float dv = p.had_div;
+        s0 = pk2(__fdiv_rn(lo2(s0), dv), __fdiv_rn(hi2(s0), dv));
+        s1 = pk2(__fdiv_rn(lo2(s1), dv), __fdiv_rn(hi2(s1), dv));
+        d0 = pk2(__fdiv_rn(lo2(d0), dv), __fdiv_rn(hi2(d0), dv));
+        d1 = pk2(__fdiv_rn(lo2(d1), dv), __fdiv_rn(hi2(d1), dv));
+      }
+      ws[2 * q] = W::round2(lo2(s0), hi2(s0));
+      ws[2 * q + 1] = W::round2(lo2(s1), hi2(s1));
+      wd[2 * q] = W::round2(lo2(d0), hi2(d0));
+      wd[2 * q + 1] = W::round2(lo2(d1), hi2(d1));
+    }
+    __syncwarp();  // the partner has read this thread's half row
+    const uint32_t flip = u ? 0x80008000u : 0u;  // thread 1's differences come out negated
+    uint4* out_s = reinterpret_cast<uint4*>(tile + r * G::kPitchB + 64 * u);
+    uint4* out_d = reinterpret_cast<uint4*>(tile + r * G::kPitchB + 128 + 64 * u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      out_s[i] = make_uint4(ws[4 * i], ws[4 * i + 1], ws[4 * i + 2], ws[4 * i + 3]);
+      out_d[i] = make_uint4(wd[4 * i] ^ flip, wd[4 * i + 1] ^ flip, wd[4 * i + 2] ^ flip, wd[4 * i + 3] ^ flip);
+    }
+  }
+}
+
 template <typename T, int D, int RUN, bool ROT>
 __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows,
                                                 uint8_t* tile) {
+  if constexpr (ROT && D == 128 && sizeof(T) == 2) {
+    if (d.gs >= 64) {
+      if (d.sbits == 4) dequant_rot_pair<T, 4>(p, d, s, j0, rows, tile);
+      else if (d.sbits == 2) dequant_rot_pair<T, 2>(p, d, s, j0, rows, tile);
+      else dequant_rot_pair<T, 8>(p, d, s, j0, rows, tile);
+      return;
+    }
+  }
   if (d.sbits == 4) chan_decode<T, D, RUN, 4, ROT>(p, d, s, j0, rows, tile);
   else if (d.sbits == 2) chan_decode<T, D, RUN, 2, ROT>(p, d, s, j0, rows, tile);
   else chan_decode<T, D, RUN, 8, ROT>(p, d, s, j0, rows, tile);
@@ -299,7 +434,7 @@ __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const Te
 // the general path); a launch covers the tiers that use its variant, and the
 // retained rows when `copy_retained`.
 template <typename T, int D, int AXIS, bool ROT>
-__global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 10)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 8 : 10)))
+__global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 10)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 6 : 10)))
     dequantize_tile_kernel(const __grid_constant__ DequantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = DGeom<T, D>;

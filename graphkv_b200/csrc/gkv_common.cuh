@@ -355,7 +355,13 @@ template <> struct Word16<__nv_bfloat16> {
     asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
   }
-  static constexpr uint32_t kNegInf = 0xFF80FF80u, kPosInf = 0x7F807F80u;
+  // packed minimum of magnitudes (the result's sign is the XOR of the signs)
+  __device__ __forceinline__ static uint32_t amin(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static constexpr uint32_t kNegInf = 0xFF80FF80u, kPosInf = 0x7F807F80u, kMaxFinite = 0x7F7F7F7Fu;
   __device__ __forceinline__ static float lo(uint32_t w) { return __uint_as_float(w << 16); }
   __device__ __forceinline__ static float hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
   __device__ __forceinline__ static uint64_t pair(uint32_t w) { return pk2(lo(w), hi(w)); }
@@ -380,7 +386,12 @@ template <> struct Word16<__half> {
     asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
   }
-  static constexpr uint32_t kNegInf = 0xFC00FC00u, kPosInf = 0x7C007C00u;
+  __device__ __forceinline__ static uint32_t amin(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static constexpr uint32_t kNegInf = 0xFC00FC00u, kPosInf = 0x7C007C00u, kMaxFinite = 0x7BFF7BFFu;
   __device__ __forceinline__ static float lo(uint32_t w) {
     return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
   }

@@ -378,9 +378,196 @@ __device__ __forceinline__ void pairs_to_words(const uint64_t (&v)[RUN / 2], uin
   }
 }
 
+// ---------------------------------------------------------------------------
+// Rotated channel-axis groups of 16-bit rows of 128 elements (the long-context
+// cold value tier): two threads per row, thread u (lane bit 3) holding elements
+// 64u .. 64u + 63 as 32 packed fp32 pairs (element 2m, 2m + 1 in pair m).
+//  - Stages h = 1 .. 32 (core.py:950-955) run in the thread: h = 1 inside a pair,
+//    h >= 2 between pairs.  Thread 1 holds its halves swapped (pair m <-> m ^ 16)
+//    so that both threads hand over pairs 16 .. 31 below; its h = 32 butterfly
+//    writes the sum to the pair that holds the lower element, through a signed
+//    fused multiply-add that rounds like the add / subtract.
+//  - Stage h = 64 pairs element e of the two halves: each thread writes the 32
+//    values it hands over as fp32 into its own 128 bytes of the staged row
+//    (already in registers) and reads the partner's; thread 0 then computes
+//    outputs 0..31 and 64..95, thread 1 outputs 32..63 and 96..127 (its
+//    differences come out negated and are flipped after rounding -- division and
+//    rounding are sign-symmetric).
+//  - Then y / sqrt(128) (fused quotient when proven exact: every input of the
+//    warp's rows is +0 or at least 2^-88 in magnitude, so no output is -0 or
+//    below 2^-99; IEEE division otherwise), the cast to the input dtype, group
+//    statistics (two groups of 64 or one of 128) and the codes.
+//  - int2 symmetric codes of 16-bit values: q = round(y / s) with |y| <= s takes
+//    one fused multiply-add y * inv + magic with inv = fl(1 / s) * (1 - 2^-16):
+//    distinct 16-bit values differ by at least 2^-11 relative, so y / s is 0.5
+//    exactly (a tie, rounded to 0 by the reference) or at least 2^-12 away from
+//    it, and the product stays on the same side of 0.5 as the exact quotient.
+// ---------------------------------------------------------------------------
+template <int SB, bool AFF, int NW, typename T>
+__device__ __forceinline__ void encode_int2_sym16(const uint32_t (&w)[NW], float inv_lo, uint8_t* dst, bool store) {
+  static_assert(SB == 2 && NW == 16, "32 int2 codes");
+  const uint64_t inv2 = pk2(inv_lo, inv_lo);
+  const float mg = kMagic + 2.f;
+  const uint64_t mg2 = pk2(mg, mg);
+  uint32_t out[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {  // 16 codes per 32-bit word
+    uint32_t acc = 0;
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+      const uint64_t t2 = fma2(Word16<T>::pair(w[8 * q + j]), inv2, mg2);
+      acc = acc * 4u + hi32(t2);
+      acc = acc * 4u + lo32(t2);
+    }
+    out[q] = acc - magic_sum<2>(16);
+  }
+  if (store) store_bytes<8>(dst, out);
+}
+
+template <typename T, int SB, bool AFF>
+__device__ void quant_rot_pair(const TensorDesc& d, uint8_t* sx, int gslice, int j0, int rows, int ht, float div,
+                               float rdiv, bool fused_ok) {
+  using G = QGeom<T, 128>;
+  using W = Word16<T>;
+  constexpr int ROWS_STEP = 16;
+  constexpr int STEPS = kQTile / ROWS_STEP;
+  const int lane = ht & 31, hw = ht >> 5;
+  const int j = lane & 7, k = lane >> 3;
+  const int u = k & 1, rb = k >> 1;
+  const float sg = u ? -1.f : 1.f;
+  const uint64_t sgp = pk2(sg, sg), sgn = pk2(-sg, -sg);
+#pragma unroll 1
+  for (int step = hw; step < STEPS; step += kQWarps) {
+    const int r = step * ROWS_STEP + rb * 8 + j;
+    uint8_t* own = sx + r * G::kPitchB + u * 128;
+    uint64_t v[32];
+    uint32_t lowest = W::kMaxFinite;  // packed magnitude minimum of the inputs
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      // thread 1 takes its two 32-element halves in swapped order
+      const uint4 a = reinterpret_cast<const uint4*>(own)[u ? (q ^ 4) : q];
+      const uint32_t wq[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        lowest = W::amin(lowest, wq[i]);
+        const float x0 = W::lo(wq[i]), x1 = W::hi(wq[i]);
+        v[4 * q + i] = pk2(__fadd_rn(x0, x1), __fsub_rn(x0, x1));  // h = 1
+      }
+    }
+    // h = 2 .. 16: pairs m and m + h/2 (inside each half of 16 pairs)
+#pragma unroll
+    for (int h = 2; h < 32; h <<= 1) {
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        if ((2 * m) & h) continue;
+        const uint64_t a = v[m], b = v[m + h / 2];
+        v[m] = add2(a, b);
+        v[m + h / 2] = sub2(a, b);
+      }
+    }
+    // h = 32: pairs m and m + 16 (thread 1: lower element in m + 16)
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const uint64_t a = v[m], b = v[m + 16];
+      v[m] = fma2(sgp, a, b);
+      v[m + 16] = fma2(sgn, b, a);
+    }
+    // Outputs are sums of multiples of the smallest input's unit in the last
+    // place, so with every input at least 2^-88 in magnitude no output is below
+    // 2^-95 (quotient >= 2^-99) and none is -0: the fused quotient is exact.
+    // Rows with a zero or tiny input divide exactly (whole warp).
+    const uint32_t mag = lowest & 0x7FFF7FFFu;
+    const bool small = !(fminf(W::lo(mag), W::hi(mag)) >= 3.2311742677852644e-27f /* 2^-88 */);
+    const bool fused = fused_ok && !__any_sync(kFull, small);
+    // hand over pairs 16 .. 31 through the thread's own (consumed) 128 bytes
+    uint4* mine = reinterpret_cast<uint4*>(own);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      mine[q] = make_uint4(lo32(v[16 + 2 * q]), hi32(v[16 + 2 * q]), lo32(v[17 + 2 * q]), hi32(v[17 + 2 * q]));
+    __syncwarp();
+    const uint4* theirs = reinterpret_cast<const uint4*>(sx + r * G::kPitchB + (u ^ 1) * 128);
+    uint32_t ws[16], wd[16];  // rounded outputs: sums (group of the lower half), differences
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 t = theirs[q];
+      const uint64_t o0 = pk2u(t.x, t.y), o1 = pk2u(t.z, t.w);
+      uint64_t s0 = add2(v[2 * q], o0), s1 = add2(v[2 * q + 1], o1);
+      uint64_t d0 = sub2(v[2 * q], o0), d1 = sub2(v[2 * q + 1], o1);
+      if (fused) {
+        const uint64_t nd2 = pk2(-div, -div), rd2 = pk2(rdiv, rdiv);
+        s0 = quot2(s0, nd2, rd2);
+        s1 = quot2(s1, nd2, rd2);
+        d0 = quot2(d0, nd2, rd2);
+        d1 = quot2(d1, nd2, rd2);
+      } else {
+        s0 = pk2(__fdiv_rn(lo2(s0), div), __fdiv_rn(hi2(s0), div));
+        s1 = pk2(__fdiv_rn(lo2(s1), div), __fdiv_rn(hi2(s1), div));
+        d0 = pk2(__fdiv_rn(lo2(d0), div), __fdiv_rn(hi2(d0), div));
+        d1 = pk2(__fdiv_rn(lo2(d1), div), __fdiv_rn(hi2(d1), div));
+      }
+      ws[2 * q] = W::round2(lo2(s0), hi2(s0));
+      ws[2 * q + 1] = W::round2(lo2(s1), hi2(s1));
+      wd[2 * q] = W::round2(lo2(d0), hi2(d0));
+      wd[2 * q + 1] = W::round2(lo2(d1), hi2(d1));
+    }
+    const uint32_t flip = u ? 0x80008000u : 0u;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) wd[i] ^= flip;
+    // statistics of the two groups (sums: elements 0..63, differences: 64..127)
+    float mn0, mx0, mn1, mx1;
+    run_stats<T, AFF, 16>(ws, mn0, mx0);
+    run_stats<T, AFF, 16>(wd, mn1, mx1);
+    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 8));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 8));
+    if (AFF) {
+      mn0 = fminf(mn0, __shfl_xor_sync(kFull, mn0, 8));
+      mn1 = fminf(mn1, __shfl_xor_sync(kFull, mn1, 8));
+    }
+    if (d.gs == 128) {
+      mx0 = mx1 = fmaxf(mx0, mx1);
+      mn0 = mn1 = fminf(mn0, mn1);
+    }
+    const FastCoder c0 = AFF ? aff_coder(mn0, mx0, d.qmax, d.rqmax) : sym_coder(mx0, d.qmax, d.rqmax, d.bits, d.packed != 0);
+    const FastCoder c1 = AFF ? aff_coder(mn1, mx1, d.qmax, d.rqmax) : sym_coder(mx1, d.qmax, d.rqmax, d.bits, d.packed != 0);
+    const bool act = r < rows;
+    const int64_t row = (int64_t)gslice * d.n + j0 + r;
+    if (act) {
+      if (d.gs == 128) {
+        if (u == 0) {
+          store_scale(d.scales, row, d.scale_dtype, c0.scale);
+          if (AFF) d.zps[row] = (uint8_t)c0.zp;
+        }
+      } else {
+        const FastCoder& c = u ? c1 : c0;
+        store_scale(d.scales, row * 2 + u, d.scale_dtype, c.scale);
+        if (AFF) d.zps[row * 2 + u] = (uint8_t)c.zp;
+      }
+    }
+    uint8_t* codes = d.codes + ((row * d.n_pad) * SB) / 8;
+    uint8_t* dst0 = codes + (32 * u * SB) / 8;          // sums: elements 32u .. 32u + 31
+    uint8_t* dst1 = codes + ((64 + 32 * u) * SB) / 8;   // differences: 64 + 32u ..
+    if constexpr (SB == 2 && !AFF) {
+      // the one-FMA coder needs |y| <= s with s a 16-bit value (s >= 1e-8)
+      const bool fast = d.packed && !(mx0 < kEps) && !(mx1 < kEps);
+      if (fast) {
+        const float k16 = 0.9999847412109375f;  // 1 - 2^-16
+        encode_int2_sym16<2, false, 16, T>(ws, __fmul_rn(c0.inv, k16), dst0, act);
+        encode_int2_sym16<2, false, 16, T>(wd, __fmul_rn(c1.inv, k16), dst1, act);
+        continue;
+      }
+    }
+    encode_store_run<T, SB, AFF, 16>(ws, c0, dst0, act);
+    encode_store_run<T, SB, AFF, 16>(wd, c1, dst1, act);
+  }
+}
+
 template <typename T, int D, int RUN, int SB, bool AFF, bool ROT>
-__device__ void quant_channels(const TensorDesc& d, const uint8_t* sx, int gslice, int j0, int rows, int ht,
+__device__ void quant_channels(const TensorDesc& d, uint8_t* sx, int gslice, int j0, int rows, int ht,
                                float div, float rdiv, bool fused) {
+  if constexpr (ROT && D == 128 && RUN == 64 && sizeof(T) == 2) {
+    quant_rot_pair<T, SB, AFF>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
+    return;
+  }
   using G = QGeom<T, D>;
   constexpr int RPR = D / RUN;             // runs per row (1, 2 or 4)
   constexpr int NW = RUN * (int)sizeof(T) / 4;
@@ -439,14 +626,14 @@ __device__ __forceinline__ void quant_tile_tokens_sb(const TensorDesc& d, const 
 }
 
 template <typename T, int D, int RUN, int SB, bool ROT>
-__device__ __forceinline__ void quant_tile_channels_sb(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
+__device__ __forceinline__ void quant_tile_channels_sb(const TensorDesc& d, uint8_t* sx, int gslice, int j0,
                                                        int rows, int ht, float div, float rdiv, bool fused) {
   if (d.quantizer == GKV_AFFINE) quant_channels<T, D, RUN, SB, true, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
   else quant_channels<T, D, RUN, SB, false, ROT>(d, sx, gslice, j0, rows, ht, div, rdiv, fused);
 }
 
 template <typename T, int D, bool ROT>
-__device__ __forceinline__ void quant_tile_channels(const TensorDesc& d, const uint8_t* sx, int gslice, int j0,
+__device__ __forceinline__ void quant_tile_channels(const TensorDesc& d, uint8_t* sx, int gslice, int j0,
                                                     int rows, int ht, float div, float rdiv, bool fused) {
   // run = 128 bytes, or half of that when the group is smaller
   constexpr int RUN = QGeom<T, D>::kRun;
@@ -557,8 +744,11 @@ __device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr
 // registers it needs; a launch covers the tiers that use its variant (the host
 // zeroes the tile counts of the others) and the retained rows when `copy_retained`.
 // Many small blocks per SM: while some wait for their rows, others compute.
-template <typename T, int D, int AXIS, bool ROT>
-__global__ void __launch_bounds__(kQThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 6 : 10)))
+// INT2: the launch's rotated tiers are all packed int2 symmetric with groups of
+// 64 or 128 (16-bit rows of 128): only that coder is compiled, which keeps the
+// variant at 64 registers.
+template <typename T, int D, int AXIS, bool ROT, bool INT2 = false>
+__global__ void __launch_bounds__(kQThreads, INT2 ? 7 : sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 5 : 10)))
     quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
@@ -589,7 +779,13 @@ __global__ void __launch_bounds__(kQThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_
     else quant_tile_tokens_sb<T, D, 8>(d, smem, gslice, j0, xch);
   } else {
     const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-    quant_tile_channels<T, D, ROT>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv, p.had_fused != 0);
+    if constexpr (INT2) {
+      quant_channels<T, D, 64, 2, false, true>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv,
+                                               p.had_fused != 0);
+    } else {
+      quant_tile_channels<T, D, ROT>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv,
+                                     p.had_fused != 0);
+    }
   }
 }
 
@@ -758,14 +954,20 @@ __global__ void general_retained_kernel(const __grid_constant__ QuantParams p) {
 
 // Per tensor (keys, values): one launch per kernel variant its tiers need; the
 // first of them also copies the tensor's retained rows.
-template <typename T, int D, int AXIS, bool ROT>
+// Packed int2 symmetric tensor with groups of 64 or 128 along 16-bit rows of 128.
+inline bool int2_rot_tensor(const TensorDesc& d, int esize, int D) {
+  return esize == 2 && D == 128 && d.bits == 2 && d.quantizer == GKV_SYMMETRIC && d.packed &&
+         d.axis == GKV_AXIS_CHANNEL && d.rotation && (d.gs == 64 || d.gs == 128);
+}
+
+template <typename T, int D, int AXIS, bool ROT, bool INT2 = false>
 static cudaError_t launch_variant(const QuantParams& p, int tensor, bool retained, bool standard, bool cold,
                                   cudaStream_t st) {
   const QuantParams q = tiers_only(p, retained, standard, cold);
   const int64_t tiles = (int64_t)q.S * q.tiles_slice;
   if (tiles == 0) return cudaSuccess;
   const size_t sm = QGeom<T, D>::kSmem;
-  auto kern = quantize_tile_kernel<T, D, AXIS, ROT>;
+  auto kern = quantize_tile_kernel<T, D, AXIS, ROT, INT2>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
   kern<<<(unsigned)tiles, kQThreads, sm, st>>>(q, tensor, retained ? 1 : 0);
@@ -788,7 +990,18 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
         case 0: e = launch_variant<T, D, GKV_AXIS_TOKEN, false>(p, tensor, ret_here, standard, cold, st); break;
         case 1: e = launch_variant<T, D, GKV_AXIS_TOKEN, true>(p, tensor, ret_here, standard, cold, st); break;
         case 2: e = launch_variant<T, D, GKV_AXIS_CHANNEL, false>(p, tensor, ret_here, standard, cold, st); break;
-        default: e = launch_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st); break;
+        default: {
+          const bool int2 = (!standard || int2_rot_tensor(p.t[GKV_STD_K + tensor], sizeof(T), D)) &&
+                            (!cold || int2_rot_tensor(p.t[GKV_COLD_K + tensor], sizeof(T), D));
+          if constexpr (sizeof(T) == 2 && D == 128) {
+            if (int2) {
+              e = launch_variant<T, D, GKV_AXIS_CHANNEL, true, true>(p, tensor, ret_here, standard, cold, st);
+              break;
+            }
+          }
+          e = launch_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st);
+          break;
+        }
       }
       if (e != cudaSuccess) return e;
       if (ret_here) retained = false;

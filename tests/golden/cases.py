@@ -67,6 +67,10 @@ def case_layers(c: Case):
             k[:, :, :, ::5] = 0.0
         elif c.keys == "zeros":
             k = torch.zeros(B, H, T, D)
+        elif c.keys == "tiny":
+            # values rows scaled toward the bottom of the fp32 range, with -0 entries:
+            # the rotated paths must divide these exactly
+            k = torch.randn(B, H, T, D, generator=g)
         elif c.keys == "smallrange":
             # tiny positive offsets: ranges below 1e-8 and min > 0
             k = 3.0 + torch.randn(B, H, T, D, generator=g) * 1e-9
@@ -75,6 +79,10 @@ def case_layers(c: Case):
         v = torch.randn(B, H, T, D, generator=g)
         if c.keys == "zeros":
             v[:, :, 1::2, :] = 0.0
+        if c.keys == "tiny":
+            v[:, :, ::3, :] *= 2.0 ** -100
+            v[:, :, 1::7, 5] = -0.0
+            v[:, :, 2::5, :] = -0.0
         out.append((k.to(dt).contiguous(), v.to(dt).contiguous()))
     return out
 
@@ -169,6 +177,18 @@ CASES = [
          overrides={"key_group_axis": "channel", "value_group_axis": "token", "rotation": "hadamard"}),
     Case("affine_sink_tail", "graphkv-int4-balanced", (1, 2, 2048, 128), "bf16",
          overrides={"quantizer": "affine", "sink_length": 64, "residual_length": 128}),
+    # rotated channel-axis values over 128 channels: two threads per row in the tile kernels
+    Case("rot128_int4_sym", "graphkv-int4-balanced", (1, 2, 512, 128), "bf16", overrides={"rotation": "hadamard"}),
+    Case("rot128_affine_gs128", "graphkv-int4-balanced", (1, 1, 384, 128), "bf16",
+         overrides={"rotation": "hadamard", "quantizer": "affine", "group_size": 128}),
+    Case("rot128_int8_f16", "graphkv-int4-balanced", (1, 1, 256, 128), "f16",
+         overrides={"rotation": "hadamard", "bits": 8}),
+    Case("rot128_int2_gs128", "graphkv-int4-balanced", (1, 2, 512, 128), "bf16",
+         overrides={"rotation": "hadamard", "bits": 2, "group_size": 128}),
+    Case("rot128_int2_zeros", "graphkv-int4-balanced", (1, 1, 256, 128), "bf16", keys="zeros",
+         overrides={"rotation": "hadamard", "bits": 2}),
+    Case("rot128_int2_tiny", "graphkv-int4-balanced", (1, 1, 320, 128), "bf16", keys="tiny",
+         overrides={"rotation": "hadamard", "bits": 2}),
     Case("scale_bf16", "graphkv-int4-balanced", (1, 1, 256, 64), "bf16", overrides={"scale_dtype": "bf16"}),
     Case("scale_f32_affine", "graphkv-int2-max", (1, 1, 256, 64), "bf16", overrides={"scale_dtype": "f32"}),
     Case("scores_batch", "graphkv", (2, 1, 8192, 64), "bf16", scores="batch"),
