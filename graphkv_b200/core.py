@@ -213,23 +213,21 @@ class QuantizedKvLayer:
         return _dequantize_layers([self])[0]
 
     def report(self, original_keys: torch.Tensor, original_values: torch.Tensor) -> dict[str, float]:
-        """Fidelity report (core.py:309-323)."""
+        """Bytes, token counts and reconstruction error against the original
+        tensors (core.py:309-323)."""
         keys, values = self.dequantize()
-        original_bytes = _tensor_nbytes(original_keys) + _tensor_nbytes(original_values)
-        quantized_bytes = self.memory_bytes()
-        ok = original_keys.to(keys.device)
-        ov = original_values.to(values.device)
-        return {
-            "original_bytes": float(original_bytes),
-            "quantized_bytes": float(quantized_bytes),
-            "compression_ratio": original_bytes / max(quantized_bytes, 1),
-            "retained_tokens": float(self.retained_token_count()),
-            "compressed_tokens": float(self.compressed_token_count()),
-            "key_mse": float(F.mse_loss(keys.float(), ok.float()).cpu()),
-            "value_mse": float(F.mse_loss(values.float(), ov.float()).cpu()),
-            "key_cosine": _flat_cosine(keys, ok),
-            "value_cosine": _flat_cosine(values, ov),
-        }
+        given = _tensor_nbytes(original_keys) + _tensor_nbytes(original_values)
+        stored = self.memory_bytes()
+        out = {"original_bytes": float(given), "quantized_bytes": float(stored),
+               "compression_ratio": given / max(stored, 1),
+               "retained_tokens": float(self.retained_token_count()),
+               "compressed_tokens": float(self.compressed_token_count())}
+        pairs = (("key", keys, original_keys.to(keys.device)), ("value", values, original_values.to(values.device)))
+        for name, got, want in pairs:
+            out[f"{name}_mse"] = float(F.mse_loss(got.float(), want.float()).cpu())
+        for name, got, want in pairs:
+            out[f"{name}_cosine"] = _flat_cosine(got, want)
+        return out
 
     def append(self, new_keys: torch.Tensor, new_values: torch.Tensor, config: KvQuantConfig,
                importance_scores: torch.Tensor | None = None) -> "QuantizedKvLayer":
@@ -360,7 +358,7 @@ class QuantizedKvCache:
     def _to_hf_positioned_cache(self, implementation: Literal["static", "sliding_window"], *,
                                 config: object | None, max_cache_len: int | None) -> object:
         """core.py:483-508."""
-        return _positioned_cache_from(self.dequantize(), implementation, config, max_cache_len)
+        return _positioned_cache_from(self.dequantize, implementation, config, max_cache_len)
 
 
 def _dynamic_cache_from(dequantized, config: object | None) -> object:
@@ -388,26 +386,30 @@ def _dynamic_cache_from(dequantized, config: object | None) -> object:
     return cache
 
 
+_POSITIONED_CACHES = {"static": "StaticCache", "sliding_window": "SlidingWindowCache"}
+
+
 def _positioned_cache_from(dequantized, implementation: Literal["static", "sliding_window"],
                            config: object | None, max_cache_len: int | None) -> object:
-    """StaticCache / SlidingWindowCache of dequantized pairs (core.py:483-508:
-    same imports, checks and update calls)."""
+    """Static / sliding-window HF cache of the dequantized pairs (core.py:483-508);
+    ``dequantized`` is a callable, so a missing config or transformers raises
+    before any dequantization."""
     if config is None:
         raise ValueError("config is required for static or sliding_window HF cache export.")
     try:
-        from transformers.cache_utils import SlidingWindowCache, StaticCache
-    except ImportError as exc:
+        from transformers import cache_utils
+        cache_cls = getattr(cache_utils, _POSITIONED_CACHES[implementation])
+    except (ImportError, AttributeError) as exc:
         raise RuntimeError("transformers is required to build a positioned cache.") from exc
-    required = max((keys.shape[2] for keys, _ in dequantized), default=0)
-    if max_cache_len is None:
-        max_cache_len = required
-    if max_cache_len < required:
+    pairs = list(dequantized())
+    longest = max((k.shape[2] for k, _ in pairs), default=0)
+    capacity = longest if max_cache_len is None else max_cache_len
+    if capacity < longest:
         raise ValueError("max_cache_len must be at least the longest KV sequence length.")
-    cache_cls = StaticCache if implementation == "static" else SlidingWindowCache
-    cache = cache_cls(config, max_cache_len=max_cache_len)
-    for layer_idx, (keys, values) in enumerate(dequantized):
-        positions = torch.arange(keys.shape[2], device=keys.device, dtype=torch.long)
-        cache.update(keys, values, layer_idx, cache_kwargs={"cache_position": positions})
+    cache = cache_cls(config, max_cache_len=capacity)
+    for index, (keys, values) in enumerate(pairs):
+        where = torch.arange(keys.shape[2], device=keys.device, dtype=torch.long)
+        cache.update(keys, values, index, cache_kwargs={"cache_position": where})
     return cache
 
 
@@ -420,7 +422,7 @@ def export_dequantized(dequantized, implementation: str, *, config: object | Non
     if implementation == "dynamic":
         return _dynamic_cache_from(dequantized, config)
     if implementation in {"static", "sliding_window"}:
-        return _positioned_cache_from(dequantized, implementation, config, max_cache_len)
+        return _positioned_cache_from(lambda: dequantized, implementation, config, max_cache_len)
     raise ValueError("implementation must be 'dynamic', 'static', 'sliding_window', or 'legacy'.")
 
 
@@ -428,75 +430,99 @@ def export_dequantized(dequantized, implementation: str, *, config: object | Non
 # HF cache extraction (core.py:511-592)
 # ---------------------------------------------------------------------------
 
+def _encoder_decoder_pairs(cache: object, role: str):
+    """An encoder-decoder cache: the pairs of its self or cross attention part."""
+    if not (hasattr(cache, "self_attention_cache") or hasattr(cache, "cross_attention_cache")):
+        return None
+    if role not in ("self", "cross"):
+        raise ValueError("cache_role must be 'self' or 'cross'.")
+    part = getattr(cache, f"{role}_attention_cache", None)
+    if part is None:
+        raise TypeError(f"HF encoder-decoder cache has no {role!r} attention cache.")
+    return hf_cache_to_tuple(part)
+
+
+def _legacy_pairs(cache: object, role: str):
+    """A legacy tuple / list of (K, V, ...) entries; empty entries are skipped."""
+    if not isinstance(cache, (tuple, list)):
+        return None
+    pairs = []
+    for entry in cache:
+        if entry is None:
+            continue
+        if not isinstance(entry, (tuple, list)) or len(entry) < 2:
+            raise TypeError("Legacy cache layers must be tuples/lists with at least key and value tensors.")
+        if entry[0] is not None and entry[1] is not None:
+            pairs.append((entry[0], entry[1]))
+    return tuple(pairs)
+
+
+def _reported_length(layer: object):
+    """Filled length a cache layer reports: get_seq_length(), else cumulative_length."""
+    get_length = getattr(layer, "get_seq_length", None)
+    if callable(get_length):
+        try:
+            n = get_length()
+        except TypeError:
+            n = None
+        if n is not None:
+            return n
+    return getattr(layer, "cumulative_length", None)
+
+
+def _filled_length(layer: object, keys: torch.Tensor) -> int:
+    """Tokens of a cache layer that hold data: a dynamic layer is full; a layer
+    with preallocated storage (static / sliding) reports its filled length."""
+    capacity = keys.shape[2]
+    if "dynamic" in type(layer).__name__.lower():
+        return capacity
+    n = _reported_length(layer)
+    if n is None:
+        return capacity
+    if isinstance(n, torch.Tensor):
+        n = int(n.max().item()) if n.numel() else 0
+    return min(max(int(n), 0), capacity)
+
+
+def _layered_pairs(cache: object, role: str):
+    """A cache with ``.layers`` (transformers >= 4.56): each layer's filled prefix."""
+    layers = getattr(cache, "layers", None)
+    if layers is None:
+        return None
+    pairs = []
+    for layer in layers:
+        keys, values = getattr(layer, "keys", None), getattr(layer, "values", None)
+        if keys is None or values is None:
+            continue
+        n = _filled_length(layer, keys)
+        if n == 0:
+            continue
+        if n < keys.shape[2]:
+            keys, values = keys[:, :, :n].contiguous(), values[:, :, :n].contiguous()
+        pairs.append((keys, values))
+    return tuple(pairs)
+
+
+def _split_lists_pairs(cache: object, role: str):
+    """A cache with parallel ``key_cache`` / ``value_cache`` lists."""
+    key_list, value_list = getattr(cache, "key_cache", None), getattr(cache, "value_cache", None)
+    if key_list is None or value_list is None:
+        return None
+    return tuple((k, v) for k, v in zip(key_list, value_list) if k is not None and v is not None)
+
+
+_CACHE_READERS = (_encoder_decoder_pairs, _legacy_pairs, _layered_pairs, _split_lists_pairs)
+
+
 def hf_cache_to_tuple(cache: object, *, cache_role: Literal["self", "cross"] = "self"
                       ) -> tuple[tuple[torch.Tensor, torch.Tensor], ...]:
-    """Extract ``(keys, values)`` tuples from legacy or modern HF caches."""
-    if hasattr(cache, "self_attention_cache") or hasattr(cache, "cross_attention_cache"):
-        if cache_role == "self":
-            selected = getattr(cache, "self_attention_cache", None)
-        elif cache_role == "cross":
-            selected = getattr(cache, "cross_attention_cache", None)
-        else:
-            raise ValueError("cache_role must be 'self' or 'cross'.")
-        if selected is None:
-            raise TypeError(f"HF encoder-decoder cache has no {cache_role!r} attention cache.")
-        return hf_cache_to_tuple(selected)
-    if isinstance(cache, (tuple, list)):
-        layers = []
-        for layer in cache:
-            if layer is None:
-                continue
-            if not isinstance(layer, (tuple, list)) or len(layer) < 2:
-                raise TypeError("Legacy cache layers must be tuples/lists with at least key and value tensors.")
-            keys, values = layer[0], layer[1]
-            if keys is None or values is None:
-                continue
-            layers.append((keys, values))
-        return tuple(layers)
-    layers = getattr(cache, "layers", None)
-    if layers is not None:
-        extracted = []
-        for layer in layers:
-            keys = getattr(layer, "keys", None)
-            values = getattr(layer, "values", None)
-            if keys is None or values is None:
-                continue
-            seq_len = _cache_layer_seq_length(layer, keys)
-            if seq_len == 0:
-                continue
-            if seq_len < keys.shape[2]:
-                keys = keys.narrow(2, 0, seq_len).contiguous()
-                values = values.narrow(2, 0, seq_len).contiguous()
-            extracted.append((keys, values))
-        return tuple(extracted)
-    key_cache = getattr(cache, "key_cache", None)
-    value_cache = getattr(cache, "value_cache", None)
-    if key_cache is not None and value_cache is not None:
-        return tuple((k, v) for k, v in zip(key_cache, value_cache) if k is not None and v is not None)
+    """(keys, values) pairs of a legacy or Hugging Face cache (core.py:511-592):
+    the first reader that recognises the cache's form decides."""
+    for read in _CACHE_READERS:
+        pairs = read(cache, cache_role)
+        if pairs is not None:
+            return pairs
     raise TypeError(f"Unsupported cache type: {type(cache)!r}")
-
-
-def _cache_layer_seq_length(layer: object, keys: torch.Tensor) -> int:
-    if "dynamic" in type(layer).__name__.lower():
-        return keys.shape[2]
-    seq_len = None
-    get_seq_length = getattr(layer, "get_seq_length", None)
-    if callable(get_seq_length):
-        try:
-            seq_len = get_seq_length()
-        except TypeError:
-            seq_len = None
-    if seq_len is None:
-        seq_len = getattr(layer, "cumulative_length", None)
-    if seq_len is None:
-        return keys.shape[2]
-    if isinstance(seq_len, torch.Tensor):
-        if seq_len.numel() == 0:
-            return 0
-        seq_len = int(seq_len.max().item())
-    else:
-        seq_len = int(seq_len)
-    return min(max(seq_len, 0), keys.shape[2])
 
 
 # ---------------------------------------------------------------------------
@@ -1109,32 +1135,40 @@ def roundtrip_host_cache(pairs, config: KvQuantConfig, importance_scores=None, c
 
 def attention_from_kv(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
                       mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Scaled dot-product attention for [B, H, Q, D] x [B, H, T, D] in fp32."""
-    if query.ndim != 4 or keys.ndim != 4 or values.ndim != 4:
+    """fp32 softmax(q k^T / sqrt(d)) v for [B, H, Q, D] queries against [B, H, T, D]
+    keys / values (core.py:800-820); masked-out positions get logit -1e9.
+    Returns (output, weights)."""
+    if min(query.ndim, keys.ndim, values.ndim) != 4 or max(query.ndim, keys.ndim, values.ndim) != 4:
         raise ValueError("query, keys, and values must be rank-4 tensors.")
     if keys.shape != values.shape:
         raise ValueError("keys and values must have the same shape.")
     if query.shape[:2] != keys.shape[:2] or query.shape[-1] != keys.shape[-1]:
         raise ValueError("query and KV batch/head/head_dim dimensions must match.")
-    scores = query.float().matmul(keys.float().transpose(-2, -1)) / sqrt(query.size(-1))
+    logits = torch.matmul(query.float(), keys.float().transpose(-2, -1)) / sqrt(query.size(-1))
     if mask is not None:
-        scores = scores.masked_fill(~mask.to(device=scores.device, dtype=torch.bool), -1.0e9)
-    weights = F.softmax(scores, dim=-1)
-    return weights.matmul(values.float()), weights
+        keep = mask.to(device=logits.device, dtype=torch.bool)
+        logits = logits.masked_fill(keep.logical_not(), -1.0e9)
+    weights = logits.softmax(dim=-1)
+    return torch.matmul(weights, values.float()), weights
 
 
 def attention_report(query: torch.Tensor, original_keys: torch.Tensor, original_values: torch.Tensor,
                      quantized_layer: QuantizedKvLayer, mask: torch.Tensor | None = None) -> dict[str, float]:
-    """Attention output / weight drift caused by the compression."""
-    qk, qv = quantized_layer.dequantize()
-    dev = qk.device
-    oo, ow = attention_from_kv(query.to(dev), original_keys.to(dev), original_values.to(dev), mask)
-    qo, qw = attention_from_kv(query.to(dev), qk, qv, mask)
-    kl = (ow.clamp_min(1.0e-9) * (ow.clamp_min(1.0e-9).log() - qw.clamp_min(1.0e-9).log())).sum(dim=-1).mean()
+    """How much the compression moves attention (core.py:823-845): output MSE,
+    cosine and largest absolute change, and KL(original || compressed) of the
+    weights (clamped at 1e-9), averaged over queries."""
+    keys_q, values_q = quantized_layer.dequantize()
+    dev = keys_q.device
+    q = query.to(dev)
+    out_ref, w_ref = attention_from_kv(q, original_keys.to(dev), original_values.to(dev), mask)
+    out_q, w_q = attention_from_kv(q, keys_q, values_q, mask)
+    p_ref, p_q = w_ref.clamp_min(1.0e-9), w_q.clamp_min(1.0e-9)
+    kl = (p_ref * (p_ref.log() - p_q.log())).sum(dim=-1).mean()
+    change = out_q - out_ref
     return {
-        "attention_output_mse": float(F.mse_loss(qo, oo).cpu()),
-        "attention_output_cosine": _flat_cosine(qo, oo),
-        "attention_output_max_abs": float((qo - oo).abs().max().cpu()),
+        "attention_output_mse": float(F.mse_loss(out_q, out_ref).cpu()),
+        "attention_output_cosine": _flat_cosine(out_q, out_ref),
+        "attention_output_max_abs": float(change.abs().max().cpu()),
         "attention_weight_kl": float(kl.cpu()),
     }
 

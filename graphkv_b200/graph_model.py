@@ -233,70 +233,86 @@ def load_bundled_graph_model(device: str | torch.device = "auto") -> GraphMemory
 # requests -> fact banks -> scores
 # ---------------------------------------------------------------------------
 
-def _slot(mapping: dict[int, int], key: int, limit: int) -> int:
-    """Local id of a global id: first-seen order, saturating at ``limit - 1``
-    (``graph_model.py:425-428``)."""
-    if key not in mapping:
-        mapping[key] = min(len(mapping), limit - 1)
-    return mapping[key]
+class _LocalIds:
+    """First-seen numbering of global ids into ``limit`` local slots: the k-th
+    new id gets slot k, and ids beyond the last slot share it
+    (``graph_model.py:425-428``).  ``first`` takes slot 0."""
+
+    def __init__(self, limit: int, first: int | None = None):
+        self.limit = limit
+        self.ids: dict[int, int] = {} if first is None else {int(first): 0}
+
+    def add(self, key) -> None:
+        self.ids.setdefault(int(key), min(len(self.ids), self.limit - 1))
+
+    def __getitem__(self, key) -> int:
+        return self.ids.get(int(key), 0)
 
 
 def build_fact_bank(anchor: int, facts: Iterable[Fact], *, num_facts: int, num_entities: int, num_relations: int,
                     shuffle_seed: int | None = None) -> GraphFactBank:
-    """Relabel a fact list into local slots, anchor entity = slot 0, keep the
-    first ``num_facts`` facts, zero-pad (``graph_model.py:362-388``).  The
+    """A fact list in local ids (``graph_model.py:362-388``): entities numbered
+    from the anchor (slot 0) in order of appearance, relations likewise, the
+    first ``num_facts`` facts as (src, rel, dst) columns, zero-padded.  The
     optional shuffle is Python's ``random.Random(seed).shuffle``."""
     items = list(facts)
     if shuffle_seed is not None:
         random.Random(shuffle_seed).shuffle(items)
-    entities: dict[int, int] = {int(anchor): 0}
-    relations: dict[int, int] = {}
-    for s, r, d in items:
-        _slot(entities, int(s), num_entities)
-        _slot(entities, int(d), num_entities)
-        _slot(relations, int(r), num_relations)
-    kept = items[:num_facts]
-    table = torch.zeros(3, num_facts, dtype=torch.long)
-    if kept:
-        table[:, : len(kept)] = torch.tensor(
-            [[entities.get(int(s), 0), relations.get(int(r), 0), entities.get(int(d), 0)] for s, r, d in kept],
-            dtype=torch.long).t()
-    return GraphFactBank(src=table[0].clone(), rel=table[1].clone(), dst=table[2].clone(),
-                         relation_map=relations, entity_map=entities)
+    entities, relations = _LocalIds(num_entities, first=anchor), _LocalIds(num_relations)
+    for src, rel, dst in items:
+        entities.add(src)
+        entities.add(dst)
+        relations.add(rel)
+    table = torch.zeros(num_facts, 3, dtype=torch.long)
+    local = [(entities[src], relations[rel], entities[dst]) for src, rel, dst in items[:num_facts]]
+    if local:
+        table[: len(local)] = torch.tensor(local, dtype=torch.long)
+    return GraphFactBank(src=table[:, 0].contiguous(), rel=table[:, 1].contiguous(), dst=table[:, 2].contiguous(),
+                         relation_map=relations.ids, entity_map=entities.ids)
 
 
 def build_query_bank(anchor: int, query_relation: int, facts: Iterable[Fact], cfg: GraphMemoryConfig,
                      shuffle_seed: int | None = None) -> GraphQueryBank:
-    """Query facts; an unseen query relation maps to the last relation slot (``graph_model.py:391-406``)."""
+    """The query's fact bank; a query relation that none of its facts uses gets
+    the last relation slot (``graph_model.py:391-406``)."""
     bank = build_fact_bank(anchor, facts, num_facts=cfg.num_facts, num_entities=cfg.num_entities,
                            num_relations=cfg.num_relations, shuffle_seed=shuffle_seed)
-    return GraphQueryBank(facts=bank, query_relation=bank.relation_map.get(int(query_relation), cfg.num_relations - 1))
+    rel = bank.relation_map.get(int(query_relation), cfg.num_relations - 1)
+    return GraphQueryBank(facts=bank, query_relation=rel)
 
 
 def build_candidate_bank(anchor: int, facts: Iterable[Fact], cfg: GraphMemoryConfig,
                          shuffle_seed: int | None = None) -> GraphFactBank:
+    """A candidate chunk's fact bank (``num_cand_facts`` rows)."""
     return build_fact_bank(anchor, facts, num_facts=cfg.num_cand_facts, num_entities=cfg.num_entities,
                            num_relations=cfg.num_relations, shuffle_seed=shuffle_seed)
 
 
+def _minmax(scores: torch.Tensor) -> torch.Tensor:
+    lo, hi = scores.min(), scores.max()
+    span = hi - lo
+    return torch.ones_like(scores) if bool(span.abs() < 1.0e-8) else (scores - lo) / span
+
+
+def _zscore(scores: torch.Tensor) -> torch.Tensor:
+    centre, spread = scores.mean(), scores.std(unbiased=False)
+    return torch.zeros_like(scores) if bool(spread < 1.0e-8) else (scores - centre) / spread
+
+
+_NORMALIZERS = {"minmax": _minmax, "zscore": _zscore}
+
+
 def normalize_graph_scores(scores: torch.Tensor, *, mode: Normalize = "minmax") -> torch.Tensor:
-    """Rank-preserving normalisation (``graph_model.py:337-359``): minmax maps to
-    [0, 1] (all ones when the range is below 1e-8); zscore uses the population
-    std (all zeros when it is below 1e-8)."""
+    """Rank-preserving rescaling of fp32 scores (``graph_model.py:337-359``):
+    ``minmax`` onto [0, 1] (all ones for a range below 1e-8), ``zscore`` by the
+    population standard deviation (all zeros below 1e-8), ``none`` unchanged."""
     scores = scores.to(dtype=torch.float32)
     if mode == "none" or scores.numel() == 0:
         return scores
-    if mode == "minmax":
-        lo, hi = scores.min(), scores.max()
-        if bool((hi - lo).abs() < 1.0e-8):
-            return torch.ones_like(scores)
-        return (scores - lo) / (hi - lo)
-    if mode == "zscore":
-        mean, std = scores.mean(), scores.std(unbiased=False)
-        if bool(std < 1.0e-8):
-            return torch.zeros_like(scores)
-        return (scores - mean) / std
-    raise ValueError("mode must be 'none', 'minmax', or 'zscore'.")
+    rescale = _NORMALIZERS.get(mode)
+    if rescale is None:
+        raise ValueError("mode must be 'none', 'minmax', or 'zscore'.")
+    return rescale(scores)
 
 
 def _resolve_graph_device(device: str | torch.device) -> torch.device:
@@ -305,14 +321,20 @@ def _resolve_graph_device(device: str | torch.device) -> torch.device:
     return torch.device(device)
 
 
-def graph_mneme_chunk_scores(query: GraphQueryBank, candidates: Sequence[GraphFactBank], *,
-                             model: GraphMemory17L | None = None, device: torch.device | str | None = None,
-                             normalize: Normalize = "minmax") -> torch.Tensor:
-    """Normalised scores of the candidate chunks (``graph_model.py:227-242``)."""
+def _scoring_model(model: GraphMemory17L | None, device) -> tuple[GraphMemory17L, torch.device]:
+    """The model that scores (the bundled one when none is given) moved to the
+    requested device, or left on its own device when none is requested."""
     if model is None:
         model = load_bundled_graph_model(device=device or "auto")
     target = _resolve_graph_device(device) if device is not None else next(model.parameters()).device
-    model = model.to(target)
+    return model.to(target), target
+
+
+def graph_mneme_chunk_scores(query: GraphQueryBank, candidates: Sequence[GraphFactBank], *,
+                             model: GraphMemory17L | None = None, device: torch.device | str | None = None,
+                             normalize: Normalize = "minmax") -> torch.Tensor:
+    """Normalised relevance of each candidate chunk to the query (``graph_model.py:227-242``)."""
+    model, target = _scoring_model(model, device)
     return normalize_graph_scores(model.score(query, candidates, device=target), mode=normalize)
 
 
@@ -320,34 +342,36 @@ def graph_mneme_token_scores(seq_len: int, chunk_spans: Iterable[tuple[int, int]
                              candidates: Sequence[GraphFactBank], *, model: GraphMemory17L | None = None,
                              device: torch.device | str | None = None,
                              normalize: Normalize = "minmax") -> torch.Tensor:
-    """One score per token: the max over the chunks covering it, 0 elsewhere (``graph_model.py:245-266``)."""
+    """Chunk scores spread over token positions: each token takes the largest
+    score of the chunks covering it, uncovered tokens 0 (``graph_model.py:245-266``)."""
     from .core import chunk_scores_to_token_scores
 
-    scores = graph_mneme_chunk_scores(query, candidates, model=model, device=device, normalize=normalize)
-    return chunk_scores_to_token_scores(seq_len, chunk_spans, scores, device=scores.device)
+    per_chunk = graph_mneme_chunk_scores(query, candidates, model=model, device=device, normalize=normalize)
+    return chunk_scores_to_token_scores(seq_len, chunk_spans, per_chunk, device=per_chunk.device)
 
 
 def build_graph_mneme_token_scores(seq_len: int, *, query_anchor: int, query_relation: int,
                                    query_facts: Iterable[Fact], chunks: Sequence[GraphRetentionChunk],
                                    model: GraphMemory17L | None = None, device: torch.device | str | None = None,
                                    normalize: Normalize = "minmax", shuffle_seed: int | None = None) -> torch.Tensor:
-    """Banks from the raw facts, chunk scores, token scores (``graph_model.py:269-312``)."""
+    """Token scores from raw facts: the query and candidate banks are built with
+    the model's sizes, then scored (``graph_model.py:269-312``)."""
     if model is None:
         model = load_bundled_graph_model(device=device or "auto")
-    if device is not None:
-        device = _resolve_graph_device(device)
-    cfg = model.cfg
-    query = build_query_bank(query_anchor, query_relation, query_facts, cfg, shuffle_seed=shuffle_seed)
-    candidates = [build_candidate_bank(c.anchor, c.facts, cfg, shuffle_seed=c.shuffle_seed) for c in chunks]
-    return graph_mneme_token_scores(seq_len, [c.span for c in chunks], query, candidates, model=model, device=device,
+    query = build_query_bank(query_anchor, query_relation, query_facts, model.cfg, shuffle_seed=shuffle_seed)
+    banks = [build_candidate_bank(c.anchor, c.facts, model.cfg, shuffle_seed=c.shuffle_seed) for c in chunks]
+    target = None if device is None else _resolve_graph_device(device)
+    return graph_mneme_token_scores(seq_len, [c.span for c in chunks], query, banks, model=model, device=target,
                                     normalize=normalize)
+
+
+_REQUEST_FIELDS = ("query_anchor", "query_relation", "query_facts", "chunks", "normalize", "shuffle_seed")
 
 
 def graph_mneme_request_token_scores(seq_len: int, request: GraphMemoryRequest, *,
                                      model: GraphMemory17L | None = None,
                                      device: torch.device | str | None = None) -> torch.Tensor:
-    """Score a ``GraphMemoryRequest`` over a cache of ``seq_len`` tokens (``graph_model.py:315-334``)."""
-    return build_graph_mneme_token_scores(
-        seq_len, query_anchor=request.query_anchor, query_relation=request.query_relation,
-        query_facts=request.query_facts, chunks=request.chunks, model=model, device=device,
-        normalize=request.normalize, shuffle_seed=request.shuffle_seed)
+    """Token scores of a ``GraphMemoryRequest`` for a cache of ``seq_len`` tokens
+    (``graph_model.py:315-334``)."""
+    fields = {name: getattr(request, name) for name in _REQUEST_FIELDS}
+    return build_graph_mneme_token_scores(seq_len, model=model, device=device, **fields)
