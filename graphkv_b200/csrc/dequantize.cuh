@@ -296,6 +296,8 @@ __device__ void tok_decode(const TensorDesc& d, int s, int j0, uint8_t* tile) {
 // reference.  As in the quantizer, thread 1 holds its halves swapped so that
 // both threads hand over pairs 16 .. 31, and the h = 64 stage pairs element e of
 // the two halves through the threads' own 128 bytes of the output tile row.
+// Unlike codes, output bits carry the sign of zero, so the h = 64 sums and
+// differences are formed with the reference's operand order (below).
 template <typename T, int SB>
 __device__ void dequant_rot_pair(const DequantParams& p, const TensorDesc& d, int s, int j0, int rows,
                                  uint8_t* tile) {
@@ -378,12 +380,18 @@ __device__ void dequant_rot_pair(const DequantParams& p, const TensorDesc& d, in
     const uint4* theirs = reinterpret_cast<const uint4*>(tile + r * G::kPitchB + (u ^ 1) * 128);
     uint32_t ws[16], wd[16];
     const uint64_t nd2 = pk2(-p.had_div, -p.had_div), rd2 = pk2(p.had_inv, p.had_inv);
+    // Sums a + b and differences a - b of the two halves' elements with the
+    // reference's zero signs (a: thread 0's values, b: thread 1's): thread 0
+    // negates what it receives (-b) and forms a + (-b) and (-1)(-b) + a, thread 1
+    // forms (-1) b + a and a + b -- in IEEE arithmetic x - y is x + (-y), and the
+    // products with -1 are exact.
+    const uint32_t nm = u ? 0u : 0x80000000u;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const uint4 t = theirs[q];
-      const uint64_t o0 = pk2u(t.x, t.y), o1 = pk2u(t.z, t.w);
-      uint64_t s0 = add2(v[2 * q], o0), s1 = add2(v[2 * q + 1], o1);
-      uint64_t d0 = sub2(v[2 * q], o0), d1 = sub2(v[2 * q + 1], o1);
+      const uint64_t o0 = pk2u(t.x ^ nm, t.y ^ nm), o1 = pk2u(t.z ^ nm, t.w ^ nm);
+      uint64_t s0 = fma2(sgn, o0, v[2 * q]), s1 = fma2(sgn, o1, v[2 * q + 1]);
+      uint64_t d0 = fma2(sgp, v[2 * q], o0), d1 = fma2(sgp, v[2 * q + 1], o1);
       if (fused) {
         s0 = quot2(s0, nd2, rd2);
         s1 = quot2(s1, nd2, rd2);
@@ -402,13 +410,12 @@ __device__ void dequant_rot_pair(const DequantParams& p, const TensorDesc& d, in
       wd[2 * q + 1] = W::round2(lo2(d1), hi2(d1));
     }
     __syncwarp();  // the partner has read this thread's half row
-    const uint32_t flip = u ? 0x80008000u : 0u;  // thread 1's differences come out negated
     uint4* out_s = reinterpret_cast<uint4*>(tile + r * G::kPitchB + 64 * u);
     uint4* out_d = reinterpret_cast<uint4*>(tile + r * G::kPitchB + 128 + 64 * u);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       out_s[i] = make_uint4(ws[4 * i], ws[4 * i + 1], ws[4 * i + 2], ws[4 * i + 3]);
-      out_d[i] = make_uint4(wd[4 * i] ^ flip, wd[4 * i + 1] ^ flip, wd[4 * i + 2] ^ flip, wd[4 * i + 3] ^ flip);
+      out_d[i] = make_uint4(wd[4 * i], wd[4 * i + 1], wd[4 * i + 2], wd[4 * i + 3]);
     }
   }
 }
