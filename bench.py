@@ -350,6 +350,56 @@ def time_compression(d: Dist, w, mode: str, steps: int, warmup: int, with_clocks
             "clocks": clocks.summary() if clocks else None, "in_bytes": in_bytes, "comp_bytes": comp_bytes}
 
 
+def time_selection(dev, T: int, scores, reps: int = 20) -> float:
+    """Device ms of one gkv_select_tiers call (graphkv profile) on fp32 [T] scores."""
+    import ctypes
+
+    import torch
+
+    import graphkv_b200 as g
+    from graphkv_b200 import _lib as L
+    from graphkv_b200.config import resolve_tiers
+
+    tiers = resolve_tiers(g.get_profile("graphkv").config, T, True)
+    idx = torch.empty(T, dtype=torch.int32, device=dev)
+    r, s, c = torch.split(idx, [tiers.n_retained, tiers.n_standard, tiers.n_cold])
+    ws = torch.empty(int(L.lib().gkv_select_workspace_bytes(T)), dtype=torch.uint8, device=dev)
+    pol = tiers.policy()
+    st = L.stream_handle(dev)
+
+    def call():
+        L.check(L.lib().gkv_select_tiers(scores.data_ptr(), None, ctypes.byref(pol), r.data_ptr(), s.data_ptr(),
+                                         c.data_ptr(), ws.data_ptr(), ws.numel(), st))
+
+    for _ in range(3):
+        call()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(torch.cuda.current_stream(dev))
+    for _ in range(reps):
+        call()
+    b.record(torch.cuda.current_stream(dev))
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / reps
+
+
+def selection_report(dev) -> dict:
+    """Selection times: log-normal scores, and scores tied across 64-token chunks
+    (what graph-memory requests produce), where both boundaries fall inside runs
+    of equal scores and the selection takes its exact tie path."""
+    import torch
+
+    out = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    for T in (32768, 131072):
+        plain = torch.exp(2.0 * torch.randn(T, generator=gen, device=dev))
+        chunks = torch.randint(0, 16, (T // 64,), generator=gen, device=dev).float()
+        tied = chunks.repeat_interleave(64).contiguous()
+        out[f"{T}"] = {"lognormal_ms": round(time_selection(dev, T, plain), 4),
+                       "chunk_ties_ms": round(time_selection(dev, T, tied), 4)}
+    return out
+
+
 def phase_report(res, peak):
     """Max-over-ranks phase times and their roofline fractions (per-rank bytes)."""
     pr = res["per_rank"]
@@ -384,6 +434,8 @@ def run_ours(args):
     head = time_compression(d, w, "weak", args.steps, args.warmup, with_clocks=True)
     ms, phases = phase_report(head, peak)
     in_bytes_rank = head["in_bytes"]
+
+    select_times = selection_report(d.dev) if d.rank == 0 else None
 
     # --- strong scaling of the 8 x 131k (60 GB) cache ---------------------------------
     strong = None
@@ -486,6 +538,7 @@ def run_ours(args):
                                        "select+quantize+pack+dequant step",
                    "parallelism": f"weak shards of (layer, kv-head) units over {d.world} GPU(s)"},
         "phases": phases,
+        "select": select_times,
         "rank_ms": [round(r[0], 4) for r in head["per_rank"]],
         "roofline": roofline,
         "cpu_baseline": cpu,
