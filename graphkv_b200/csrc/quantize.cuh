@@ -24,7 +24,6 @@
 #pragma once
 
 #include <algorithm>
-#include <atomic>
 
 #include "gkv_params.cuh"
 
@@ -669,64 +668,54 @@ __device__ __forceinline__ TileRef tile_ref(const QuantParams& p, int t) {
   return r;
 }
 
-// Shared memory of a persistent quantize block: two staging buffers of one tile
-// (64 rows at a pitch of row bytes + 16), the token-axis exchange, and one
-// mbarrier per buffer.
+// Staging of a tile of one tensor with 16-byte asynchronous copies: thread =
+// (chunk c, rows r0, r0 + STEP, ...), so the lanes of a warp cover whole rows
+// (coalesced).  The rows' token indices are loaded one tile ahead, one per lane
+// (tile_tokens), and handed out with shuffles when the copies are issued
+// (stage_tile), so issuing never waits for a load.  Rows past the end of the
+// tier are zero-filled (token-axis groups quantize them as padding).
 template <typename T, int D>
-struct QSmem {
+struct StageMap {
   using G = QGeom<T, D>;
-  static constexpr size_t kBuf = G::kTileBytes;
-  static constexpr size_t kXch = (size_t)G::kWords * 2 * 2 * 4;
-  static constexpr size_t kBars = 2 * kBuf + kXch;  // offset of the two mbarriers
-  static constexpr size_t kBytes = kBars + 2 * sizeof(uint64_t);
+  static constexpr int STEP = kQThreads / G::kChunks;  // rows per pass of the block
+  static constexpr int LPR = G::kChunks;               // lanes per row within a pass
+  static constexpr int RPW = 32 / LPR;                 // rows of one pass held by a warp
+  static constexpr int NPASS = kQTile / STEP;          // passes
+  static_assert(LPR <= 32 && 32 % LPR == 0 && NPASS * RPW <= 32, "one index per lane");
 };
 
-// Token indices of rows `lane` and `lane + 32` of tile t (-1: no row; an index
-// outside [0, T) is reported and read as token 0).
-__device__ __forceinline__ int2 tile_rows(const QuantParams& p, const TileRef& tr) {
+template <typename T, int D>
+__device__ __forceinline__ int tile_tokens(const QuantParams& p, const TileRef& tr) {
+  using M = StageMap<T, D>;
   const int j0 = tr.k * kQTile;
   const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-  const int lane = threadIdx.x & 31;
-  int2 tok = make_int2(-1, -1);
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int r = lane + 32 * h;
-    if (r < rows) {
-      int t = p.idx[tr.tier][j0 + r];
-      if ((unsigned)t >= (unsigned)p.T) { raise_error(kErrBadIndex); t = 0; }
-      (h ? tok.y : tok.x) = t;
-    }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // lane l holds the index of row (l / RPW) * STEP + warp * RPW + l % RPW
+  const int lrow = (lane / M::RPW) * M::STEP + warp * M::RPW + lane % M::RPW;
+  int tok = 0;
+  if (lane < M::NPASS * M::RPW && lrow < rows) {
+    tok = p.idx[tr.tier][j0 + lrow];
+    if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); tok = 0; }
   }
   return tok;
 }
 
-// Warp 0 stages the rows of a tile into `buf`: one bulk copy (TMA, no
-// multicast) per row of this GPU's K or V, completing on `bar` by transaction
-// bytes; rows past the end of the tier are zero-filled (token-axis groups
-// quantize them as padding).
 template <typename T, int D>
-__device__ __forceinline__ void stage_rows(const T* base, int64_t st, int2 tok, uint8_t* buf, uint64_t* bar) {
+__device__ __forceinline__ void stage_tile(const QuantParams& p, const TileRef& tr, const T* base, int64_t st,
+                                           uint8_t* sx, int ltok) {
   using G = QGeom<T, D>;
-  const int lane = threadIdx.x & 31;
-  const unsigned live = __ballot_sync(kFull, tok.x >= 0) ;
-  const unsigned live2 = __ballot_sync(kFull, tok.y >= 0);
-  const uint32_t rows = __popc(live) + __popc(live2);
-  // generic-proxy accesses of this buffer (reads, the rotated rows' exchange)
-  // are ordered before the asynchronous copies that overwrite it
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  if (lane == 0) mbar_arrive_expect_tx(bar, rows * (uint32_t)G::kRowBytes);
-  __syncwarp();
+  using M = StageMap<T, D>;
+  const int j0 = tr.k * kQTile;
+  const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = threadIdx.x % M::LPR, b = lane / M::LPR;  // row of a pass: pass * STEP + warp * RPW + b
+  const uint8_t* src0 = reinterpret_cast<const uint8_t*>(base) + c * 16;
+  uint8_t* dst0 = sx + (warp * M::RPW + b) * G::kPitchB + c * 16;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int r = lane + 32 * h;
-    const int t = h ? tok.y : tok.x;
-    uint8_t* dst = buf + r * G::kPitchB;
-    if (t >= 0) {
-      bulk_load(dst, base + (int64_t)t * st, (uint32_t)G::kRowBytes, bar);
-    } else {
-#pragma unroll
-      for (int c = 0; c < G::kChunks; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0u, 0u, 0u, 0u);
-    }
+  for (int i = 0; i < M::NPASS; ++i) {
+    const int r = i * M::STEP + warp * M::RPW + b;
+    const int tok = __shfl_sync(kFull, ltok, i * M::RPW + b);
+    cp_async16(dst0 + i * M::STEP * G::kPitchB, src0 + (int64_t)tok * st * (int64_t)sizeof(T), r < rows ? 16u : 0u);
   }
 }
 
@@ -750,102 +739,53 @@ __device__ __forceinline__ int tile_role(const QuantParams& p, const TileRef& tr
   return d.axis == AXIS ? 2 : 0;                     // 2: quantize
 }
 
-// Persistent blocks over the tiles of one tensor (`tensor` 1: values, 0: keys),
-// tile t + gridDim.x after tile t.  Compiled per grouping axis (AXIS) and
-// rotation (ROT), so that each variant keeps only the registers it needs; a
-// launch covers the tiers that use its variant (the host zeroes the tile counts
-// of the others) and the retained rows when `copy_retained`.
-// Two staging buffers: while the block quantizes tile t from one, the rows of
-// its next tile arrive in the other (warp 0 issues one bulk copy per row, with
-// the rows' token indices loaded one tile earlier), so loads and arithmetic
-// overlap inside every block rather than only across blocks.  Waits on the
-// copies are bounded: on a timeout the block records kErrBarrierTimeout, waits
-// (bounded) for its copies in flight and stops.
+// One block per tile of one tensor (`tensor` 1: values, 0: keys).  Compiled per
+// grouping axis (AXIS) and rotation (ROT), so that each variant keeps only the
+// registers it needs; a launch covers the tiers that use its variant (the host
+// zeroes the tile counts of the others) and the retained rows when `copy_retained`.
+// Many small blocks per SM: while some wait for their rows, others compute.
 // INT2: the launch's rotated tiers are all packed int2 symmetric with groups of
 // 64 or 128 (16-bit rows of 128): only that coder is compiled, which keeps the
-// variant at 72 registers.
+// variant at 64 registers.
 template <typename T, int D, int AXIS, bool ROT, bool INT2 = false>
-__global__ void __launch_bounds__(kQThreads, sizeof(T) == 4 ? 3 : (INT2 || (ROT && AXIS == GKV_AXIS_CHANNEL) ? 5 : 6))
+__global__ void __launch_bounds__(kQThreads, INT2 ? 7 : sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 7)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 5 : 10)))
     quantize_tile_kernel(const __grid_constant__ QuantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = QGeom<T, D>;
-  using SM = QSmem<T, D>;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBars);
-  uint32_t* xch = reinterpret_cast<uint32_t*>(smem + 2 * SM::kBuf);
-  const int total = p.S * p.tiles_slice;
-  const int warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+  const TileRef tr = tile_ref(p, blockIdx.x);
+  const int role = tile_role<AXIS>(p, tr, tensor, copy_retained);
+  if (role == 0) return;
+  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
+  if (role == 2 && (d.rotation != 0) != ROT) return;  // not this variant's tier
+  const int gslice = p.slice_offset + tr.s;
+  int64_t st;
+  const T* base = tensor_base<T>(p, tr.s, tensor, st);
+  if (role == 1) {
+    copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
+    return;
   }
+  stage_tile<T, D>(p, tr, base, st, smem, tile_tokens<T, D>(p, tr));
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  int t = blockIdx.x;
-  bool armed[2] = {false, false};  // a buffer's copies are in flight
-  uint32_t parity[2] = {0u, 0u};
-  int2 next_rows = make_int2(-1, -1);
-  // prologue: stage tile t, load the indices of the tile after it
-  {
-    const TileRef tr = tile_ref(p, t);
-    if (tile_role<AXIS>(p, tr, tensor, copy_retained) == 2) {
-      armed[0] = true;
-      if (warp == 0) {
-        int64_t st;
-        const T* base = tensor_base<T>(p, tr.s, tensor, st);
-        stage_rows<T, D>(base, st, tile_rows(p, tr), smem, &bars[0]);
-      }
+  const int j0 = tr.k * kQTile;
+  if constexpr (AXIS == GKV_AXIS_TOKEN) {
+    if constexpr (ROT) {
+      rotate_rows_smem<T, D>(reinterpret_cast<T*>(smem), p.had_div, p.had_inv, threadIdx.x >> 5);
+      __syncthreads();
     }
-    if (warp == 0 && t + (int)gridDim.x < total) next_rows = tile_rows(p, tile_ref(p, t + gridDim.x));
-  }
-  for (int i = 0; t < total; ++i, t += gridDim.x) {
-    const int b = i & 1;
-    uint8_t* buf = smem + b * SM::kBuf;
-    // stage the next tile into the other buffer (free since the barrier that ended the last iteration)
-    const int tn = t + gridDim.x;
-    if (tn < total) {
-      const TileRef trn = tile_ref(p, tn);
-      armed[b ^ 1] = tile_role<AXIS>(p, trn, tensor, copy_retained) == 2;
-      if (armed[b ^ 1] && warp == 0) {
-        int64_t st;
-        const T* base = tensor_base<T>(p, trn.s, tensor, st);
-        stage_rows<T, D>(base, st, next_rows, smem + (b ^ 1) * SM::kBuf, &bars[b ^ 1]);
-      }
-      if (warp == 0 && tn + (int)gridDim.x < total) next_rows = tile_rows(p, tile_ref(p, tn + gridDim.x));
+    uint32_t* xch = reinterpret_cast<uint32_t*>(smem + G::kTileBytes);
+    if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, smem, gslice, j0, xch);
+    else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, smem, gslice, j0, xch);
+    else quant_tile_tokens_sb<T, D, 8>(d, smem, gslice, j0, xch);
+  } else {
+    const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
+    if constexpr (INT2) {
+      quant_channels<T, D, 64, 2, false, true>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv,
+                                               p.had_fused != 0);
+    } else {
+      quant_tile_channels<T, D, ROT>(d, smem, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv,
+                                     p.had_fused != 0);
     }
-    const TileRef tr = tile_ref(p, t);
-    const int role = tile_role<AXIS>(p, tr, tensor, copy_retained);
-    const int gslice = p.slice_offset + tr.s;
-    if (role == 1) {
-      int64_t st;
-      const T* base = tensor_base<T>(p, tr.s, tensor, st);
-      copy_retained_tile<T, D>(p, base, st, tensor ? p.ret_v : p.ret_k, gslice, tr.k);
-    } else if (role == 2) {
-      if (!block_wait(&bars[b], parity[b])) {
-        if (armed[b ^ 1]) block_wait(&bars[b ^ 1], parity[b ^ 1]);
-        return;
-      }
-      parity[b] ^= 1u;
-      const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-      const int j0 = tr.k * kQTile;
-      if constexpr (AXIS == GKV_AXIS_TOKEN) {
-        if constexpr (ROT) {
-          rotate_rows_smem<T, D>(reinterpret_cast<T*>(buf), p.had_div, p.had_inv, threadIdx.x >> 5);
-          __syncthreads();
-        }
-        if (d.sbits == 4) quant_tile_tokens_sb<T, D, 4>(d, buf, gslice, j0, xch);
-        else if (d.sbits == 2) quant_tile_tokens_sb<T, D, 2>(d, buf, gslice, j0, xch);
-        else quant_tile_tokens_sb<T, D, 8>(d, buf, gslice, j0, xch);
-      } else {
-        const int rows = min(kQTile, p.n_tier[tr.tier] - j0);
-        if constexpr (INT2) {
-          quant_channels<T, D, 64, 2, false, true>(d, buf, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv,
-                                                   p.had_fused != 0);
-        } else {
-          quant_tile_channels<T, D, ROT>(d, buf, gslice, j0, rows, threadIdx.x, p.had_div, p.had_inv,
-                                         p.had_fused != 0);
-        }
-      }
-    }
-    __syncthreads();  // the buffer of tile t is free for the tile after next
   }
 }
 
@@ -1026,19 +966,11 @@ static cudaError_t launch_variant(const QuantParams& p, int tensor, bool retaine
   const QuantParams q = tiers_only(p, retained, standard, cold);
   const int64_t tiles = (int64_t)q.S * q.tiles_slice;
   if (tiles == 0) return cudaSuccess;
-  const size_t sm = QSmem<T, D>::kBytes;
+  const size_t sm = QGeom<T, D>::kSmem;
   auto kern = quantize_tile_kernel<T, D, AXIS, ROT, INT2>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
-  static std::atomic<int> per_sm{0};  // resident blocks per SM of this variant, looked up once
-  int occ = per_sm.load(std::memory_order_relaxed);
-  if (occ == 0) {
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kQThreads, sm)) != cudaSuccess) return e;
-    occ = occ > 0 ? occ : 1;
-    per_sm.store(occ, std::memory_order_relaxed);
-  }
-  const int64_t grid = std::min<int64_t>(tiles, (int64_t)occ * device_sm_count());
-  kern<<<(unsigned)grid, kQThreads, sm, st>>>(q, tensor, retained ? 1 : 0);
+  kern<<<(unsigned)tiles, kQThreads, sm, st>>>(q, tensor, retained ? 1 : 0);
   return cudaGetLastError();
 }
 
