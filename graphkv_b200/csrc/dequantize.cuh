@@ -14,7 +14,6 @@
 #pragma once
 
 #include <algorithm>
-#include <atomic>
 
 #include "gkv_params.cuh"
 
@@ -510,164 +509,6 @@ __global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_
 }
 
 // ---------------------------------------------------------------------------
-// Keys of 16-bit caches (token-axis groups of SB-bit codes): persistent blocks,
-// tile t + gridDim.x after tile t, that load the next tile's code words, scales
-// and output row indices into registers before decoding the current tile.  The
-// decode waits on nothing but registers, and every thread keeps the loads of one
-// tile in flight while it decodes and stores the previous one (the one-tile-per-
-// block kernel stalls on these loads at the start of every tile).
-// Item = (column word w = two channels, run h of 32 rows), as in tok_decode.
-// ---------------------------------------------------------------------------
-template <int SB>
-struct KeyLoad {
-  uint32_t c0[SB], c1[SB];  // 32 codes of channels 2w and 2w + 1 (SB words each)
-  float s0, s1;
-  int z0, z1;
-  int tok;    // output row of tile row threadIdx.x (threads < 64); -1: none
-  bool live;  // this item's rows exist
-};
-
-template <typename T, int D, int SB>
-__device__ __forceinline__ void load_key_tile(const DequantParams& p, int t, int tensor, KeyLoad<SB>& L) {
-  using G = DGeom<T, D>;
-  constexpr int ITEMS = G::kWords * (kDTile / kDRows);
-  const DTileRef tr = dtile_ref(p, t);
-  L.live = false;
-  L.tok = -1;
-  if (tr.tier == 0) return;
-  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-  const int j0 = tr.k * kDTile;
-  const int rows = min(kDTile, p.n_tier[tr.tier] - j0);
-  if (threadIdx.x < kDTile && (int)threadIdx.x < rows) {
-    int tk = p.idx[tr.tier][j0 + threadIdx.x];
-    if ((unsigned)tk >= (unsigned)p.T) { raise_error(kErrBadIndex); tk = -1; }
-    L.tok = tk;
-  }
-  const int item = threadIdx.x;
-  const int h = item / G::kWords, w = item - h * G::kWords;
-  const int tok0 = j0 + h * kDRows;
-  if (item >= ITEMS || tok0 >= d.n_pad) return;
-  L.live = true;
-  const int64_t crow = (int64_t)tr.s * D + 2 * w;
-  load_codes<4 * SB>(d.codes + ((crow * d.n_pad + tok0) * SB) / 8, L.c0);
-  load_codes<4 * SB>(d.codes + (((crow + 1) * d.n_pad + tok0) * SB) / 8, L.c1);
-  const int64_t gi = crow * d.groups_row + (tok0 >> d.log2gs);
-  L.s0 = load_scale(d.scales, gi, d.scale_dtype);
-  L.s1 = load_scale(d.scales, gi + d.groups_row, d.scale_dtype);
-  L.z0 = load_zp(d, gi);
-  L.z1 = load_zp(d, gi + d.groups_row);
-}
-
-template <typename T, int D, int SB>
-__device__ __forceinline__ void process_key_tile(const DequantParams& p, int t, int tensor, const KeyLoad<SB>& L,
-                                                 uint8_t* tile, int* toks, int copy_retained) {
-  using G = DGeom<T, D>;
-  constexpr int EPC = 32 / SB;
-  const DTileRef tr = dtile_ref(p, t);
-  T* out = reinterpret_cast<T*>(tensor ? p.out_v : p.out_k) + (int64_t)tr.s * p.T * D;
-  if (tr.tier == 0) {
-    if (!copy_retained) return;
-    // retained rows: thread = (16-byte chunk, rows r0, r0 + STEP, ...), loads before stores
-    constexpr int VEC = 16 / (int)sizeof(T), CPR = D / VEC, STEP = kDThreads / CPR, N = kRetTile / STEP;
-    const int R = p.n_tier[0];
-    const int j0 = tr.k * kRetTile, rows = min(kRetTile, R - j0);
-    const T* src = reinterpret_cast<const T*>(tensor ? p.ret_v : p.ret_k) + ((int64_t)tr.s * R + j0) * D;
-    const int c = threadIdx.x % CPR, r0 = threadIdx.x / CPR;
-    uint4 v[N];
-    int to[N];
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      const int r = r0 + i * STEP;
-      to[i] = -1;
-      v[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (r < rows) {
-        to[i] = p.idx[0][j0 + r];
-        if ((unsigned)to[i] >= (unsigned)p.T) { raise_error(kErrBadIndex); to[i] = -1; }
-        v[i] = *reinterpret_cast<const uint4*>(src + r * D + c * VEC);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < N; ++i)
-      if (to[i] >= 0) *reinterpret_cast<uint4*>(out + (int64_t)to[i] * D + c * VEC) = v[i];
-    return;
-  }
-  const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
-  if (threadIdx.x < kDTile) toks[threadIdx.x] = L.tok;
-  if (L.live) {
-    const int item = threadIdx.x;
-    const int h = item / G::kWords, w = item - h * G::kWords;
-    uint32_t* col = reinterpret_cast<uint32_t*>(tile + (h * kDRows) * G::kPitchB) + w;
-    const Decoder d0 = make_decoder(d, L.s0, L.z0), d1 = make_decoder(d, L.s1, L.z1);
-    const uint64_t base2 = pk2(d0.base, d1.base), sc2 = pk2(d0.scale, d1.scale);
-    const uint32_t x0 = SB == 8 ? d0.xor_mask : 0u, x1 = SB == 8 ? d1.xor_mask : 0u;
-#pragma unroll
-    for (int q = 0; q < SB; ++q) {
-      uint32_t a[EPC], b[EPC];
-      word_codes<SB>(L.c0[q], a);
-      word_codes<SB>(L.c1[q], b);
-#pragma unroll
-      for (int e = 0; e < EPC; ++e)
-        col[(q * EPC + e) * G::kPitchW] = out_word<T>(decode_pair(a[e], b[e], x0, x1, base2, sc2));
-    }
-  }
-  __syncthreads();
-  const int rows = min(kDTile, p.n_tier[tr.tier] - tr.k * kDTile);
-  constexpr int CH = G::kRowBytes / 16, STEP = kDThreads / CH;
-  const int c = threadIdx.x % CH, r0 = threadIdx.x / CH;
-#pragma unroll
-  for (int i = 0; i < kDTile / STEP; ++i) {
-    const int r = r0 + i * STEP;
-    const int t_out = r < rows ? toks[r] : -1;
-    if (t_out >= 0)
-      reinterpret_cast<uint4*>(out + (int64_t)t_out * D)[c] = *reinterpret_cast<const uint4*>(tile + r * G::kPitchB + c * 16);
-  }
-  __syncthreads();  // tile and toks are rewritten by the next tile
-}
-
-template <typename T, int D, int SB>
-__global__ void __launch_bounds__(kDThreads, 6)
-    dequantize_keys_kernel(const __grid_constant__ DequantParams p, int tensor, int copy_retained) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  using G = DGeom<T, D>;
-  uint8_t* tile = smem;
-  int* toks = reinterpret_cast<int*>(smem + G::kTile);
-  const int total = p.S * p.tiles_slice;
-  const int step = gridDim.x;
-  KeyLoad<SB> a, b;
-  int t = blockIdx.x;
-  if (t < total) load_key_tile<T, D, SB>(p, t, tensor, a);
-  while (t < total) {
-    if (t + step < total) load_key_tile<T, D, SB>(p, t + step, tensor, b);
-    process_key_tile<T, D, SB>(p, t, tensor, a, tile, toks, copy_retained);
-    t += step;
-    if (t >= total) break;
-    if (t + step < total) load_key_tile<T, D, SB>(p, t + step, tensor, a);
-    process_key_tile<T, D, SB>(p, t, tensor, b, tile, toks, copy_retained);
-    t += step;
-  }
-}
-
-template <typename T, int D, int SB>
-static cudaError_t launch_keys_persistent(const DequantParams& q, int tensor, bool retained, cudaStream_t st) {
-  using G = DGeom<T, D>;
-  const int64_t tiles = (int64_t)q.S * q.tiles_slice;
-  const size_t sm = G::kTile + kDTile * sizeof(int);
-  auto kern = dequantize_keys_kernel<T, D, SB>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  if (e != cudaSuccess) return e;
-  static std::atomic<int> per_sm{0};  // resident blocks per SM, looked up once
-  int occ = per_sm.load(std::memory_order_relaxed);
-  if (occ == 0) {
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kDThreads, sm)) != cudaSuccess) return e;
-    occ = occ > 0 ? occ : 1;
-    per_sm.store(occ, std::memory_order_relaxed);
-  }
-  const int64_t grid = std::min<int64_t>(tiles, (int64_t)occ * device_sm_count());
-  kern<<<(unsigned)grid, kDThreads, sm, st>>>(q, tensor, retained ? 1 : 0);
-  return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
 // general path: warp per tier row (both K and V), element-wise decode
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float decode_element(const TensorDesc& d, int64_t e, int64_t gi) {
@@ -743,17 +584,6 @@ static cudaError_t launch_dq_variant(const DequantParams& p, int tensor, bool re
   const DequantParams q = tiers_only(p, retained, standard, cold);
   const int64_t tiles = (int64_t)q.S * q.tiles_slice;
   if (tiles == 0) return cudaSuccess;
-  if constexpr (AXIS == GKV_AXIS_TOKEN && !ROT && sizeof(T) == 2) {
-    // one code width over the launch's tiers: the persistent kernel with prefetched codes
-    const int sb_std = standard ? p.t[GKV_STD_K + tensor].sbits : 0;
-    const int sb_cold = cold ? p.t[GKV_COLD_K + tensor].sbits : 0;
-    const int sb = sb_std ? sb_std : sb_cold;
-    if (sb && (!sb_cold || sb_cold == sb)) {
-      if (sb == 4) return launch_keys_persistent<T, D, 4>(q, tensor, retained, st);
-      if (sb == 2) return launch_keys_persistent<T, D, 2>(q, tensor, retained, st);
-      return launch_keys_persistent<T, D, 8>(q, tensor, retained, st);
-    }
-  }
   const size_t sm = G::kTile + kDTile * sizeof(int);
   auto kern = dequantize_tile_kernel<T, D, AXIS, ROT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);

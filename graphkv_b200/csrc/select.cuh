@@ -31,6 +31,7 @@ constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSelCluster = 8;         // blocks of the selection cluster
 constexpr int kSelSmemTokens = 40960;  // tokens per block whose keys (4 B) and tier (1 B) fit in shared memory
+constexpr size_t kSelSmemLimit = 227 * 1024;  // shared memory of one block (static + dynamic)
 enum : uint8_t { kCand = 0, kRet = 1, kCold = 2 };
 
 struct SelectParams {
@@ -45,6 +46,8 @@ struct SelectParams {
   int* idx_ret;
   int* idx_std;
   int* idx_cold;
+  int heap_cap;        // entries of the shared-memory heap of the exact path (0: heap in the workspace)
+  int heap_offset;     // its byte offset in dynamic shared memory (8-byte aligned)
 };
 
 // Monotone key: larger score -> larger key; NaN above +inf (torch.topk ranks NaN
@@ -258,6 +261,100 @@ __device__ void heap_select_warp(int* q, int k, int n, const Key& key, Before be
   __syncwarp();
 }
 
+// The same heap with its keys and positions in shared memory (node i at index
+// i + 1 of each array, so the two children 2i + 1, 2i + 2 of a node sit in one
+// 8-byte word and load together).  Only the first k queue slots hold the result
+// of the heap select, so the evicted tops are not written back to the queue.
+__device__ void adjust_heap_smem(uint32_t* hk, int* hp, int hole, int len, int item, uint32_t item_key,
+                                 Before before) {
+  const int top = hole;
+  int child = hole;
+  while (child < (len - 1) / 2) {
+    child = 2 * (child + 1);
+    const uint2 kk = *reinterpret_cast<const uint2*>(hk + child);  // (left, right) keys
+    const int2 pp = *reinterpret_cast<const int2*>(hp + child);
+    uint32_t ck = kk.y;
+    int cp = pp.y;
+    if (before(kk.y, kk.x)) {
+      --child;
+      ck = kk.x;
+      cp = pp.x;
+    }
+    hk[hole + 1] = ck;
+    hp[hole + 1] = cp;
+    hole = child;
+  }
+  if ((len & 1) == 0 && child == (len - 2) / 2) {
+    child = 2 * (child + 1);
+    hk[hole + 1] = hk[child];
+    hp[hole + 1] = hp[child];
+    hole = child - 1;
+  }
+  int parent = (hole - 1) / 2;
+  while (hole > top && before(hk[parent + 1], item_key)) {
+    hk[hole + 1] = hk[parent + 1];
+    hp[hole + 1] = hp[parent + 1];
+    hole = parent;
+    parent = (hole - 1) / 2;
+  }
+  hk[hole + 1] = item_key;
+  hp[hole + 1] = item;
+}
+
+// __heap_select(0, k, n) by warp 0 over a shared-memory heap; the next 32
+// candidates are loaded while the replacements of the current 32 are replayed.
+template <class Key>
+__device__ void heap_select_warp_smem(int* q, int k, int n, const Key& key, Before before, uint32_t* hk, int* hp) {
+  const int lane = threadIdx.x & 31;
+  for (int i = lane; i < k; i += 32) {
+    const int it = q[i];
+    hk[i + 1] = key(it);
+    hp[i + 1] = it;
+  }
+  __syncwarp();
+  if (lane == 0 && k >= 2) {
+    for (int parent = (k - 2) / 2;; --parent) {
+      adjust_heap_smem(hk, hp, parent, k, hp[parent + 1], hk[parent + 1], before);
+      if (parent == 0) break;
+    }
+  }
+  __syncwarp();
+  uint32_t top = hk[1];
+  int item = 0;
+  uint32_t ki = 0u;
+  if (k + lane < n) {
+    item = q[k + lane];
+    ki = key(item);
+  }
+  for (int base = k; base < n; base += 32) {
+    const int i = base + lane;
+    const bool valid = i < n;
+    int item_n = 0;
+    uint32_t ki_n = 0u;
+    if (i + 32 < n) {
+      item_n = q[i + 32];
+      ki_n = key(item_n);
+    }
+    uint32_t hits = __ballot_sync(0xFFFFFFFFu, valid && before(ki, top));
+    while (hits) {
+      const int l = __ffs(hits) - 1;
+      hits &= hits - 1;
+      const uint32_t kl = __shfl_sync(0xFFFFFFFFu, ki, l);
+      const int il = __shfl_sync(0xFFFFFFFFu, item, l);
+      if (before(kl, top)) {
+        if (lane == 0) adjust_heap_smem(hk, hp, 0, k, il, kl, before);
+        __syncwarp();
+        top = hk[1];
+      }
+    }
+    item = item_n;
+    ki = ki_n;
+  }
+  __syncwarp();
+  for (int i = lane; i < k; i += 32) q[i] = hp[i + 1];
+  __syncwarp();
+}
+
 // __insertion_sort(first, last), one thread.
 template <class Key>
 __device__ void insertion_sort_serial(int* q, int first, int last, const Key& key, Before before) {
@@ -318,7 +415,16 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
   if (k > n) k = n;  // the count check reports the shortfall
   if (k <= 0) return;
   if ((int64_t)k * 64 <= n) {
-    if (warp == 0) heap_select_warp(q, k, n, key, before);
+    if (warp == 0) {
+      if (k <= p.heap_cap) {
+        extern __shared__ __align__(16) uint8_t sel_smem[];
+        uint32_t* hk = reinterpret_cast<uint32_t*>(sel_smem + p.heap_offset);
+        int* hp = reinterpret_cast<int*>(sel_smem + p.heap_offset + 4 * ((size_t)p.heap_cap + 2));
+        heap_select_warp_smem(q, k, n, key, before, hk, hp);
+      } else {
+        heap_select_warp(q, k, n, key, before);
+      }
+    }
   } else {
     const int nth = k - 1;
     if (threadIdx.x == 0) {
@@ -838,7 +944,18 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
   p.idx_std = idx_std;
   p.idx_cold = idx_cold;
   const int per = select_block_tokens(T);
-  const size_t sm = per <= kSelSmemTokens ? (size_t)per * 5 : 0;
+  size_t sm = per <= kSelSmemTokens ? (size_t)per * 5 : 0;
+  // room for the exact path's heap (a heap select needs k * 64 <= T)
+  int cap = 0;
+  for (const int k : {pol.keep_protect, pol.keep_outlier, pol.keep_cold})
+    if (k > 0 && (int64_t)k * 64 <= T) cap = k > cap ? k : cap;
+  p.heap_cap = 0;
+  p.heap_offset = (int)((sm + 15) & ~(size_t)15);
+  const size_t heap_bytes = 8 * ((size_t)cap + 2);
+  if (cap > 0 && p.heap_offset + heap_bytes + sizeof(SelShared) <= kSelSmemLimit) {
+    p.heap_cap = cap;
+    sm = p.heap_offset + heap_bytes;
+  }
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
   select_kernel<<<kSelCluster, kSelThreads, sm, st>>>(p);
