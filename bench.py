@@ -52,6 +52,7 @@ def parse_args():
     ap.add_argument("--strong-steps", type=int, default=12)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--append", type=int, default=1, help="time QuantizedKvCache.append (0: skip)")
     ap.add_argument("--layers", type=int, default=0, help="use only the first N layers (profiling case)")
     return ap.parse_args()
 
@@ -400,6 +401,47 @@ def selection_report(dev) -> dict:
     return out
 
 
+def append_report(d, w) -> dict:
+    """Device ms of QuantizedKvCache.append of 1 and of 1024 new tokens to the
+    whole compressed cache of this rank's units (the old tokens are dequantized
+    into the grown buffers and everything is requantized, as the reference's
+    append does)."""
+    import torch
+
+    import graphkv_b200 as g
+    from graphkv_b200.sharding import shard_units
+    from graphkv_b200.workloads import make_layer, make_scores
+
+    cfg = g.get_profile(w.profile).config
+    shard = shard_units(w.layers, w.heads, 1, 0)
+    pairs = [make_layer(w, l, device=str(d.dev), heads=range(h0, h1)) for (l, h0, h1) in shard]
+    scores = make_scores(w, device=str(d.dev))
+    cache = g.QuantizedKvCache.from_past_key_values(pairs, cfg, scores)
+    del pairs
+    out = {}
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(11)
+    for n in (1, 1024):
+        B, H, T, D = cache.layers[0].original_shape
+        new = [(torch.randn(B, H, n, D, generator=gen, device=d.dev).to(w.dtype),
+                torch.randn(B, H, n, D, generator=gen, device=d.dev).to(w.dtype)) for _ in cache.layers]
+        s_new = torch.cat([scores, torch.exp(2.0 * torch.randn(n, generator=gen, device=d.dev))])
+        for _ in range(2):
+            cache.append(new, cfg, s_new)
+        torch.cuda.synchronize(d.dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        reps = 5
+        for _ in range(reps):
+            cache.append(new, cfg, s_new)
+        b.record()
+        torch.cuda.synchronize(d.dev)
+        out[f"tokens_{n}_ms"] = round(a.elapsed_time(b) / reps, 3)
+    del cache
+    torch.cuda.empty_cache()
+    return out
+
+
 def phase_report(res, peak):
     """Max-over-ranks phase times and their roofline fractions (per-rank bytes)."""
     pr = res["per_rank"]
@@ -436,6 +478,7 @@ def run_ours(args):
     in_bytes_rank = head["in_bytes"]
 
     select_times = selection_report(d.dev) if d.rank == 0 else None
+    append_times = append_report(d, w) if d.rank == 0 and args.append else None
 
     # --- strong scaling of the 8 x 131k (60 GB) cache ---------------------------------
     strong = None
@@ -539,6 +582,7 @@ def run_ours(args):
                    "parallelism": f"weak shards of (layer, kv-head) units over {d.world} GPU(s)"},
         "phases": phases,
         "select": select_times,
+        "append": append_times,
         "rank_ms": [round(r[0], 4) for r in head["per_rank"]],
         "roofline": roofline,
         "cpu_baseline": cpu,

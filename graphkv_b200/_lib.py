@@ -40,7 +40,7 @@ class TensorSpec(ctypes.Structure):
 
 class Plan(ctypes.Structure):
     _fields_ = [("batch", c_i32), ("head_dim", c_i32), ("seq_len", c_i32), ("dtype", c_i32),
-                ("n_retained", c_i32), ("n_standard", c_i32), ("n_cold", c_i32), ("reserved0", c_i32),
+                ("n_retained", c_i32), ("n_standard", c_i32), ("n_cold", c_i32), ("out_seq_stride", c_i32),
                 ("idx_retained", c_ptr), ("idx_standard", c_ptr), ("idx_cold", c_ptr),
                 ("spec", TensorSpec * 4), ("hadamard_divisor", ctypes.c_float), ("reserved1", c_i32),
                 ("retained_k", c_ptr), ("retained_v", c_ptr),

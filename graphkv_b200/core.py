@@ -231,17 +231,9 @@ class QuantizedKvLayer:
 
     def append(self, new_keys: torch.Tensor, new_values: torch.Tensor, config: KvQuantConfig,
                importance_scores: torch.Tensor | None = None) -> "QuantizedKvLayer":
-        """Append tokens and requantize (core.py:325-348)."""
-        old_keys, old_values = self.dequantize()
-        if old_keys.shape[: self.seq_dim] != new_keys.shape[: self.seq_dim]:
-            raise ValueError("new_keys batch/head dimensions must match the cached layer.")
-        if old_keys.shape[self.seq_dim + 1:] != new_keys.shape[self.seq_dim + 1:]:
-            raise ValueError("new_keys head_dim dimensions must match the cached layer.")
-        if new_keys.shape != new_values.shape:
-            raise ValueError("new_keys and new_values must have the same shape.")
-        keys = torch.cat([old_keys, new_keys.to(old_keys.device)], dim=self.seq_dim)
-        values = torch.cat([old_values, new_values.to(old_values.device)], dim=self.seq_dim)
-        return quantize_kv_layer(keys, values, config, importance_scores=importance_scores)
+        """This layer with ``new_keys`` / ``new_values`` [B, H, n, D] appended,
+        requantized as the reference does (core.py:325-348)."""
+        return append_layers([self], [(new_keys, new_values)], config, importance_scores)[0]
 
 
 @dataclass
@@ -316,20 +308,8 @@ class QuantizedKvCache:
 
     def append(self, new_past_key_values: Sequence[tuple[torch.Tensor, torch.Tensor]], config: KvQuantConfig,
                importance_scores: Sequence[torch.Tensor] | torch.Tensor | None = None) -> "QuantizedKvCache":
-        """core.py:418-433: dequantize, concatenate, requantize (batched)."""
-        if len(new_past_key_values) != len(self.layers):
-            raise ValueError("new_past_key_values must have one (key, value) pair per cached layer.")
-        old = self.dequantize()
-        pairs = []
-        for (ok, ov), (nk, nv), layer in zip(old, new_past_key_values, self.layers):
-            if ok.shape[:2] != nk.shape[:2]:
-                raise ValueError("new_keys batch/head dimensions must match the cached layer.")
-            if ok.shape[3:] != nk.shape[3:]:
-                raise ValueError("new_keys head_dim dimensions must match the cached layer.")
-            if nk.shape != nv.shape:
-                raise ValueError("new_keys and new_values must have the same shape.")
-            pairs.append((torch.cat([ok, nk.to(ok.device)], dim=2), torch.cat([ov, nv.to(ov.device)], dim=2)))
-        return QuantizedKvCache.from_past_key_values(pairs, config, importance_scores)
+        """Every layer with its new tokens appended and requantized (core.py:418-433)."""
+        return QuantizedKvCache(append_layers(self.layers, new_past_key_values, config, importance_scores))
 
     @classmethod
     def from_hf_cache(cls, cache: object, config: KvQuantConfig,
@@ -988,9 +968,8 @@ def _dequantize_layers(layers: list[QuantizedKvLayer]) -> list:
     return out
 
 
-def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
-    """One launch for consecutive layers of one arena; returns [(K, V), ...]."""
-    lib = L.lib()
+def _run_plan(run: list[QuantizedKvLayer]):
+    """The C plan of consecutive layers of one arena; returns (plan, shape, dtype, device)."""
     first = run[0]
     B, H, T, D = first.original_shape
     qts = _layer_tensors(first)
@@ -1015,13 +994,28 @@ def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
         plan.codes[i] = t.q.data_ptr()
         plan.scales[i] = t.scales.data_ptr()
         plan.zero_points[i] = L.ptr(t.zero_points)
+    return plan, (B, H, T, D), dtype, dev
+
+
+def _dequantize_run_into(run: list[QuantizedKvLayer], outk: torch.Tensor, outv: torch.Tensor) -> None:
+    """Dequantize consecutive layers of one arena into the first T tokens of each
+    slice of ``outk`` / ``outv`` [L, B, H, T', D] (T' >= T, contiguous, on the
+    storage device): one launch, every output row written once."""
+    plan, (B, H, T, D), _, dev = _run_plan(run)
+    plan.out_seq_stride = outk.shape[3]
+    with torch.cuda.device(dev):
+        L.check(L.lib().gkv_dequantize(ctypes.byref(plan), len(run) * B * H, outk.data_ptr(), outv.data_ptr(),
+                                       None, 0, L.stream_handle(dev)))
+
+
+def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
+    """One launch for consecutive layers of one arena; returns [(K, V, device), ...]."""
+    _, (B, H, T, D), dtype, dev = _run_plan(run)
     nl = len(run)
     outk = torch.empty((nl, B, H, T, D), dtype=dtype, device=dev)
     outv = torch.empty((nl, B, H, T, D), dtype=dtype, device=dev)
-    with torch.cuda.device(dev):
-        L.check(lib.gkv_dequantize(ctypes.byref(plan), nl * B * H, outk.data_ptr(), outv.data_ptr(), None, 0,
-                                   L.stream_handle(dev)))
-    home = first.home_device
+    _dequantize_run_into(run, outk, outv)
+    home = run[0].home_device
     if home is not None and home.type == "cpu":
         hk = torch.empty(outk.shape, dtype=dtype, pin_memory=True)
         hv = torch.empty(outv.shape, dtype=dtype, pin_memory=True)
@@ -1029,6 +1023,80 @@ def _dequantize_run(run: list[QuantizedKvLayer]) -> list:
         hv.copy_(outv, non_blocking=True)
         outk, outv = hk, hv
     return [(outk[l], outv[l], dev) for l in range(nl)]
+
+
+def _check_append(layer: QuantizedKvLayer, new_keys: torch.Tensor, new_values: torch.Tensor) -> None:
+    old = tuple(layer.original_shape)
+    if old[:2] != tuple(new_keys.shape[:2]):
+        raise ValueError("new_keys batch/head dimensions must match the cached layer.")
+    if old[3:] != tuple(new_keys.shape[3:]):
+        raise ValueError("new_keys head_dim dimensions must match the cached layer.")
+    if new_keys.shape != new_values.shape:
+        raise ValueError("new_keys and new_values must have the same shape.")
+
+
+def _grown_pairs(layers: list[QuantizedKvLayer], new_pairs: list) -> list:
+    """(K, V) of every layer with its new tokens behind the old ones -- the
+    reference's ``cat(dequantize(old), new)`` (core.py:325-348).  Consecutive
+    layers of one arena with equally long appends are dequantized by one launch
+    straight into the grown [L, B, H, T + n, D] buffers, so no separate
+    concatenation pass runs."""
+    grown: list = [None] * len(layers)
+    i = 0
+    while i < len(layers):
+        lay = layers[i]
+        nk, nv = new_pairs[i]
+        if lay.passthrough_keys is not None and lay.passthrough_values is not None:
+            ok, ov = lay.passthrough_keys, lay.passthrough_values
+            grown[i] = (torch.cat([ok, nk.to(ok.device)], dim=2), torch.cat([ov, nv.to(ov.device)], dim=2))
+            i += 1
+            continue
+        j = i + 1
+        while (j < len(layers) and layers[j].passthrough_keys is None and _follows(layers[j - 1], layers[j])
+               and new_pairs[j][0].shape == nk.shape):
+            j += 1
+        run = layers[i:j]
+        _, (B, H, T, D), dtype, dev = _run_plan(run)
+        n = nk.shape[2]
+        outk = torch.empty((j - i, B, H, T + n, D), dtype=dtype, device=dev)
+        outv = torch.empty((j - i, B, H, T + n, D), dtype=dtype, device=dev)
+        if (T + n) * D * _dtype_element_size(dtype) % 16 == 0:
+            _dequantize_run_into(run, outk, outv)
+        else:  # output slices would not stay 16-byte aligned: dequantize, then place
+            for l, (k, v, _) in enumerate(_dequantize_run(run)):
+                outk[l, :, :, :T].copy_(k)
+                outv[l, :, :, :T].copy_(v)
+        for l in range(j - i):
+            outk[l, :, :, T:].copy_(new_pairs[i + l][0])
+            outv[l, :, :, T:].copy_(new_pairs[i + l][1])
+        for l in range(j - i):
+            grown[i + l] = (outk[l], outv[l])
+        i = j
+    return grown
+
+
+def append_layers(layers: list[QuantizedKvLayer], new_pairs, config: KvQuantConfig,
+                  importance_scores=None) -> list[QuantizedKvLayer]:
+    """Append new tokens to compressed layers and requantize (core.py:325-348,
+    418-433) with the result of the reference: its dequantized old tokens and
+    the new ones are requantized together, since every quantization group along
+    the tokens and every tier boundary can move when the cache grows.  The
+    dequantized old tokens go straight into the grown device buffers, and the
+    requantization is the batched quantize of ``from_past_key_values``.  The
+    layers keep the device their inputs came from."""
+    new_pairs = list(new_pairs)
+    if len(new_pairs) != len(layers):
+        raise ValueError("new_past_key_values must have one (key, value) pair per cached layer.")
+    for lay, (nk, nv) in zip(layers, new_pairs):
+        _check_append(lay, nk, nv)
+    grown = _grown_pairs(list(layers), new_pairs)
+    per_layer = [importance_scores if (importance_scores is None or isinstance(importance_scores, torch.Tensor))
+                 else importance_scores[i] for i in range(len(grown))]
+    out = _quantize_layers(grown, config, per_layer)
+    for old, new in zip(layers, out):
+        if old.home_device is not None and old.home_device.type == "cpu":
+            new.home_device = old.home_device
+    return out
 
 
 HOST_CHUNK_BYTES = 64 << 20  # K+V bytes per stage of the pipelined host round trip (at least one layer)

@@ -386,10 +386,15 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
   if (st != GKV_OK) return st;
   const gkv_plan& p = *plan;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.out_seq_stride != 0 && p.out_seq_stride < p.seq_len)
+    return fail(GKV_ERR_INVALID, "out_seq_stride must be 0 or >= seq_len");
+  if (p.out_seq_stride != 0 && ((int64_t)p.out_seq_stride * p.head_dim * elem_size(p.dtype)) % 16)
+    return fail(GKV_ERR_INVALID, "out_seq_stride rows must keep output slices 16-byte aligned");
   DequantParams q;
   q.T = p.seq_len;
   q.D = p.head_dim;
   q.S = n_slices;
+  q.out_T = p.out_seq_stride ? p.out_seq_stride : p.seq_len;
   q.idx[0] = p.idx_retained;
   q.idx[1] = p.idx_standard;
   q.idx[2] = p.idx_cold;

@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_
   if (tr.tier == 0 && !copy_retained) return;
   const TensorDesc& d = p.t[(tr.tier == 1 ? GKV_STD_K : GKV_COLD_K) + tensor];
   if (tr.tier != 0 && (d.axis != AXIS || (d.rotation != 0) != ROT)) return;
-  T* out = reinterpret_cast<T*>(tensor ? p.out_v : p.out_k) + (int64_t)tr.s * p.T * D;
+  T* out = reinterpret_cast<T*>(tensor ? p.out_v : p.out_k) + (int64_t)tr.s * p.out_T * D;
   if (tr.tier == 0) {
     // retained rows: thread = (16-byte chunk, rows r0, r0 + STEP, ...), loads before stores
     constexpr int VEC = 16 / (int)sizeof(T), CPR = D / VEC, STEP = kDThreads / CPR, N = kRetTile / STEP;
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(256) general_dequant_rows_kernel(const __grid_
   float* buf = gbuf + warp * D;
   for (int which = 0; which < 2; ++which) {
     const TensorDesc& d = p.t[(tier == 1 ? 0 : 2) + which];
-    T* out = reinterpret_cast<T*>(which ? p.out_v : p.out_k) + ((int64_t)s * p.T + tok) * D;
+    T* out = reinterpret_cast<T*>(which ? p.out_v : p.out_k) + ((int64_t)s * p.out_T + tok) * D;
     for (int c = lane; c < D; c += 32) {
       int64_t e, gi;
       if (d.axis == GKV_AXIS_TOKEN) {
@@ -572,7 +572,7 @@ __global__ void general_dequant_retained_kernel(const __grid_constant__ DequantP
   const int j = (int)(rj % R), s = (int)(rj / R);
   const int tok = p.idx[0][j];
   if ((unsigned)tok >= (unsigned)p.T) { raise_error(kErrBadIndex); return; }
-  const int64_t o = ((int64_t)s * p.T + tok) * p.D + c;
+  const int64_t o = ((int64_t)s * p.out_T + tok) * p.D + c;
   reinterpret_cast<T*>(p.out_k)[o] = reinterpret_cast<const T*>(p.ret_k)[i];
   reinterpret_cast<T*>(p.out_v)[o] = reinterpret_cast<const T*>(p.ret_v)[i];
 }

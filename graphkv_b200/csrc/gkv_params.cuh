@@ -94,12 +94,13 @@ int device_sm_count();  // host: SMs of the current device
 
 struct DequantParams {
   int T, D, S;
+  int out_T;         // tokens between two output slices (>= T)
   const int* idx[3];
   int n_tier[3];
   TensorDesc t[4];
   const void* ret_k;
   const void* ret_v;
-  void* out_k;       // [S, T, D]
+  void* out_k;       // [S, out_T, D]
   void* out_v;
   float had_div, had_inv;
   int had_fused;     // as in QuantParams

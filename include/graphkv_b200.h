@@ -88,7 +88,8 @@ typedef struct gkv_plan {
   int32_t n_retained;  /* R  */
   int32_t n_standard;  /* Tc */
   int32_t n_cold;      /* Tl */
-  int32_t reserved0;
+  int32_t out_seq_stride; /* gkv_dequantize: tokens between two output slices (0: seq_len) --
+                             lets a dequantize write into a longer [S, stride, D] buffer */
   const int32_t* idx_retained; /* [R]  ascending token positions */
   const int32_t* idx_standard; /* [Tc] */
   const int32_t* idx_cold;     /* [Tl] */
@@ -203,8 +204,9 @@ int32_t gkv_quantize(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n
                      void* workspace, size_t workspace_bytes, gkv_stream_t stream);
 
 /* Unpack + dequantize every tier of n_slices slices and scatter the rows, with
- * the retained rows, into k_out / v_out ([S, T, D] contiguous, dtype of the
- * plan); every output row is written exactly once.  Replaces
+ * the retained rows, into k_out / v_out ([S, T, D], or [S, out_seq_stride, D]
+ * whose first T rows of each slice are written, dtype of the plan); every
+ * output row is written exactly once.  Replaces
  * QuantizedKvLayer.dequantize (core.py:265-307), QuantizedTensor.dequantize
  * (core.py:153-173) and _unpack_lowbit (core.py:993-1007); over layers,
  * QuantizedKvCache.dequantize (core.py:371-372). */
