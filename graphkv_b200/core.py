@@ -1002,7 +1002,7 @@ def _dequantize_run_into(run: list[QuantizedKvLayer], outk: torch.Tensor, outv: 
     slice of ``outk`` / ``outv`` [L, B, H, T', D] (T' >= T, contiguous, on the
     storage device): one launch, every output row written once."""
     plan, (B, H, T, D), _, dev = _run_plan(run)
-    plan.out_seq_stride = outk.shape[3]
+    plan.out_seq_stride = outk.shape[3] if outk.shape[3] != T else 0
     with torch.cuda.device(dev):
         L.check(L.lib().gkv_dequantize(ctypes.byref(plan), len(run) * B * H, outk.data_ptr(), outv.data_ptr(),
                                        None, 0, L.stream_handle(dev)))
@@ -1060,12 +1060,7 @@ def _grown_pairs(layers: list[QuantizedKvLayer], new_pairs: list) -> list:
         n = nk.shape[2]
         outk = torch.empty((j - i, B, H, T + n, D), dtype=dtype, device=dev)
         outv = torch.empty((j - i, B, H, T + n, D), dtype=dtype, device=dev)
-        if (T + n) * D * _dtype_element_size(dtype) % 16 == 0:
-            _dequantize_run_into(run, outk, outv)
-        else:  # output slices would not stay 16-byte aligned: dequantize, then place
-            for l, (k, v, _) in enumerate(_dequantize_run(run)):
-                outk[l, :, :, :T].copy_(k)
-                outv[l, :, :, :T].copy_(v)
+        _dequantize_run_into(run, outk, outv)
         for l in range(j - i):
             outk[l, :, :, T:].copy_(new_pairs[i + l][0])
             outv[l, :, :, T:].copy_(new_pairs[i + l][1])

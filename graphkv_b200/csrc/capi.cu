@@ -381,15 +381,16 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
   (void)workspace_bytes;
   if (!plan || !k_out || !v_out || n_slices < 1) return fail(GKV_ERR_INVALID, "plan/outputs missing");
   Resolved r;
-  const bool out_aligned = aligned16(k_out) && aligned16(v_out);
+  // the tile kernels store 16-byte vectors: every output slice must start 16-byte aligned
+  const int64_t out_T = plan && plan->out_seq_stride ? plan->out_seq_stride : (plan ? plan->seq_len : 0);
+  const bool out_aligned = aligned16(k_out) && aligned16(v_out) && plan &&
+                           (out_T * plan->head_dim * elem_size(plan->dtype)) % 16 == 0;
   int st = resolve_plan(plan, n_slices, false, nullptr, 0, out_aligned, r);
   if (st != GKV_OK) return st;
   const gkv_plan& p = *plan;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.out_seq_stride != 0 && p.out_seq_stride < p.seq_len)
     return fail(GKV_ERR_INVALID, "out_seq_stride must be 0 or >= seq_len");
-  if (p.out_seq_stride != 0 && ((int64_t)p.out_seq_stride * p.head_dim * elem_size(p.dtype)) % 16)
-    return fail(GKV_ERR_INVALID, "out_seq_stride rows must keep output slices 16-byte aligned");
   DequantParams q;
   q.T = p.seq_len;
   q.D = p.head_dim;
