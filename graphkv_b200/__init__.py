@@ -11,6 +11,7 @@ from .core import (
     QuantizedKvLayer,
     QuantizedTensor,
     attention_from_kv,
+    attention_from_quantized,
     attention_report,
     build_retention_mask,
     chunk_scores_to_token_scores,
@@ -63,6 +64,7 @@ __all__ = [
     "QuantizedKvLayer",
     "QuantizedTensor",
     "attention_from_kv",
+    "attention_from_quantized",
     "attention_report",
     "build_candidate_bank",
     "build_fact_bank",

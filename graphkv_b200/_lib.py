@@ -72,6 +72,8 @@ _PROTOTYPES = {
     "gkv_quantize": (c_i32, [ctypes.POINTER(Plan), ctypes.POINTER(LayerIn), c_i32, c_ptr, ctypes.c_size_t, c_ptr]),
     "gkv_dequantize_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Plan), c_i32]),
     "gkv_dequantize": (c_i32, [ctypes.POINTER(Plan), c_i32, c_ptr, c_ptr, c_ptr, ctypes.c_size_t, c_ptr]),
+    "gkv_attention_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Plan), c_i32, c_i32]),
+    "gkv_attention": (c_i32, [ctypes.POINTER(Plan), c_i32, c_ptr, c_i32, c_ptr, c_ptr, ctypes.c_size_t, c_ptr]),
 }
 
 _lock = threading.Lock()

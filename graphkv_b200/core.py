@@ -1236,5 +1236,37 @@ def attention_report(query: torch.Tensor, original_keys: torch.Tensor, original_
     }
 
 
+def attention_from_quantized(query: torch.Tensor, quantized_layer: QuantizedKvLayer) -> torch.Tensor:
+    """fp32 softmax(q k^T / sqrt(d)) v of [B, H, Q, D] queries (Q <= 16) over a
+    compressed layer, read from its packed codes: the output of
+    ``attention_from_kv(query, *quantized_layer.dequantize())[0]`` (core.py:800-820)
+    without writing the dequantized keys and values.  The rows attended over are
+    bit-identical to the dequantized cache's; the fp32 sums run in another order.
+    Layers the attention kernels do not cover (passthrough layers, keys grouped
+    along channels, head dims other than 64 / 128) are dequantized first."""
+    if query.ndim != 4:
+        raise ValueError("query, keys, and values must be rank-4 tensors.")
+    B, H, T, D = quantized_layer.original_shape
+    if tuple(query.shape[:2]) != (B, H) or query.shape[-1] != D:
+        raise ValueError("query and KV batch/head/head_dim dimensions must match.")
+    Q = query.shape[2]
+    if quantized_layer.passthrough_keys is not None or Q > 16:
+        keys, values = quantized_layer.dequantize()
+        return attention_from_kv(query.to(keys.device), keys, values)[0]
+    plan, _, _, dev = _run_plan([quantized_layer])
+    lib = L.lib()
+    ws_bytes = int(lib.gkv_attention_workspace_bytes(ctypes.byref(plan), B * H, Q))
+    if ws_bytes == 0:
+        keys, values = quantized_layer.dequantize()
+        return attention_from_kv(query.to(keys.device), keys, values)[0]
+    q = query.to(device=dev, dtype=torch.float32).contiguous()
+    out = torch.empty((B, H, Q, D), dtype=torch.float32, device=dev)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        L.check(lib.gkv_attention(ctypes.byref(plan), B * H, q.data_ptr(), Q, out.data_ptr(), ws.data_ptr(),
+                                  ws_bytes, L.stream_handle(dev)))
+    return out
+
+
 def _flat_cosine(a: torch.Tensor, b: torch.Tensor) -> float:
     return float(F.cosine_similarity(a.float().flatten(), b.float().flatten(), dim=0).cpu())

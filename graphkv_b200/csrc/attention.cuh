@@ -1,0 +1,172 @@
+// Attention of queries over a compressed layer, reading the packed codes directly
+// (the consumer of the compressed cache; the reference computes the same result as
+// softmax(q k^T / sqrt(D)) v over the dequantized cache, core.py:800-820).
+//
+// One block of 128 threads per tile of 64 rows of one tier of one (batch, head)
+// slice -- the dequantizer's tiles: retained rows, then standard, then cold.  The
+// block decodes the tile's key and value rows into shared memory with the
+// dequantizer's own decoders, so the rows it attends over are bit-identical to the
+// dequantized cache's, and writes, per query, the tile's softmax partials: the
+// largest logit m, the sum l of exp(logit - m) and o = sum exp(logit - m) v.  A
+// second kernel merges the partials of a slice's tiles (rescaled to the overall
+// largest logit) into the output.  Only the summation order differs from the
+// reference's fp32 matmul / softmax / matmul.
+#pragma once
+
+#include "dequantize.cuh"
+
+namespace gkv {
+
+constexpr int kAttnMaxQueries = 16;
+
+struct AttnParams {
+  DequantParams d;     // tiles, tiers and tensors of the layer (out_k / out_v unused)
+  const float* q;      // [S, Q, D] fp32
+  int Q;
+  float inv_sqrt_d;    // 1 / sqrt(D)
+  float* part;         // [S, tiles_slice, Q, D + 2]: m, l, o[D]
+  float* out;          // [S, Q, D] fp32
+};
+
+template <typename T, int D>
+struct AGeom {
+  using G = DGeom<T, D>;
+  static constexpr size_t kTile = G::kTile;                       // one decoded [64][D] tile
+  static constexpr size_t kQ = (size_t)kAttnMaxQueries * D * 4;   // queries
+  static constexpr size_t kBytes = 2 * kTile + kQ + kDTile * 4 + 64 + kDTile * 4;
+};
+
+// Retained rows j0 .. j0 + rows of one tensor into a [64][D] tile (16-byte vectors).
+template <typename T, int D>
+__device__ __forceinline__ void load_retained_rows(const void* ret, int R, int s, int j0, int rows, uint8_t* tile) {
+  using G = DGeom<T, D>;
+  constexpr int CH = G::kRowBytes / 16;
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(ret) + ((int64_t)s * R + j0) * G::kRowBytes;
+  for (int i = threadIdx.x; i < rows * CH; i += kDThreads) {
+    const int r = i / CH, c = i - r * CH;
+    *reinterpret_cast<uint4*>(tile + r * G::kPitchB + c * 16) =
+        *reinterpret_cast<const uint4*>(src + (int64_t)r * G::kRowBytes + c * 16);
+  }
+}
+
+template <typename T, int D, bool VROT>
+__global__ void __launch_bounds__(kDThreads, 4) attend_tile_kernel(const __grid_constant__ AttnParams a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  using G = DGeom<T, D>;
+  using A = AGeom<T, D>;
+  const DequantParams& p = a.d;
+  uint8_t* tk = smem;
+  uint8_t* tv = smem + A::kTile;
+  float* qs = reinterpret_cast<float*>(smem + 2 * A::kTile);
+  float* prob = reinterpret_cast<float*>(smem + 2 * A::kTile + A::kQ);
+  float* red = prob + kDTile;  // 16 floats of reductions
+  const DTileRef tr = dtile_ref(p, blockIdx.x);
+  const int s = tr.s;
+  const int j0 = tr.k * kDTile;
+  const int rows = min(kDTile, p.n_tier[tr.tier] - j0);
+  // queries of this slice
+  for (int i = threadIdx.x; i < a.Q * D; i += kDThreads) qs[i] = a.q[(int64_t)s * a.Q * D + i];
+  // key and value rows of the tile
+  if (tr.tier == 0) {
+    load_retained_rows<T, D>(p.ret_k, p.n_tier[0], s, j0, rows, tk);
+    load_retained_rows<T, D>(p.ret_v, p.n_tier[0], s, j0, rows, tv);
+  } else {
+    const TensorDesc& dk = p.t[tr.tier == 1 ? GKV_STD_K : GKV_COLD_K];
+    const TensorDesc& dv = p.t[tr.tier == 1 ? GKV_STD_V : GKV_COLD_V];
+    if (dk.sbits == 4) tok_decode<T, D, 4>(dk, s, j0, tk);
+    else if (dk.sbits == 2) tok_decode<T, D, 2>(dk, s, j0, tk);
+    else tok_decode<T, D, 8>(dk, s, j0, tk);
+    constexpr int RUN = G::kRun;
+    if (dv.rotation) {
+      if constexpr (VROT) chan_decode_any<T, D, (RUN / 2 >= 32 && D / (RUN / 2) <= 4) ? RUN / 2 : RUN, true>(
+          p, dv, s, j0, rows, tv);
+    } else if (dv.gs < RUN) {
+      if constexpr (RUN / 2 >= 32 && D / (RUN / 2) <= 4) chan_decode_any<T, D, RUN / 2, false>(p, dv, s, j0, rows, tv);
+    } else {
+      chan_decode_any<T, D, RUN, false>(p, dv, s, j0, rows, tv);
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = threadIdx.x >> 1, half = threadIdx.x & 1;  // two threads per tile row
+  constexpr int HD = D / 2;
+  float* part = a.part + ((int64_t)s * p.tiles_slice + (blockIdx.x - s * p.tiles_slice)) * a.Q * (D + 2);
+  for (int qi = 0; qi < a.Q; ++qi) {
+    const float* q = qs + qi * D;
+    // logit of row r: q . k_r / sqrt(D)
+    float dot = 0.f;
+    const T* krow = reinterpret_cast<const T*>(tk + r * G::kPitchB) + half * HD;
+#pragma unroll 8
+    for (int c = 0; c < HD; ++c) dot = __fmaf_rn(q[half * HD + c], Elem<T>::to_f32(krow[c]), dot);
+    dot += __shfl_xor_sync(kFull, dot, 1);
+    const float logit = r < rows ? dot * a.inv_sqrt_d : -INFINITY;
+    float m = logit;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float e = r < rows ? expf(logit - m) : 0.f;
+    if (half == 0) prob[r] = e;
+    float l = half == 0 ? e : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
+    __syncthreads();  // prob complete; red reads done
+    if (lane == 0) red[4 + warp] = l;
+    __syncthreads();
+    // o[c] = sum_r prob[r] v_r[c]
+    for (int c = threadIdx.x; c < D; c += kDThreads) {
+      float acc = 0.f;
+      for (int rr = 0; rr < rows; ++rr)
+        acc = __fmaf_rn(prob[rr], Elem<T>::to_f32(reinterpret_cast<const T*>(tv + rr * G::kPitchB)[c]), acc);
+      part[qi * (D + 2) + 2 + c] = acc;
+    }
+    if (threadIdx.x == 0) {
+      part[qi * (D + 2)] = m;
+      part[qi * (D + 2) + 1] = red[4] + red[5] + red[6] + red[7];
+    }
+    __syncthreads();  // red / prob reused by the next query
+  }
+}
+
+// Merge the tiles' partials of one (slice, query): block of D threads.
+__global__ void attend_combine_kernel(const __grid_constant__ AttnParams a) {
+  const int sq = blockIdx.x;  // slice * Q + query
+  const int s = sq / a.Q, qi = sq - s * a.Q;
+  const int D = a.d.D, n = a.d.tiles_slice;
+  const float* part = a.part + (int64_t)s * n * a.Q * (D + 2) + qi * (D + 2);
+  const int64_t stride = (int64_t)a.Q * (D + 2);
+  float M = -INFINITY;
+  for (int j = 0; j < n; ++j) M = fmaxf(M, part[j * stride]);
+  float L = 0.f, o = 0.f;
+  const int c = threadIdx.x;
+  for (int j = 0; j < n; ++j) {
+    const float w = expf(part[j * stride] - M);
+    L = __fmaf_rn(w, part[j * stride + 1], L);
+    if (c < D) o = __fmaf_rn(w, part[j * stride + 2 + c], o);
+  }
+  if (c < D) a.out[(int64_t)sq * D + c] = o / L;
+}
+
+template <typename T, int D>
+static cudaError_t launch_attention_t(const AttnParams& a, cudaStream_t st) {
+  const size_t sm = AGeom<T, D>::kBytes;
+  const bool vrot = (a.d.tiles[1] && a.d.t[GKV_STD_V].rotation) || (a.d.tiles[2] && a.d.t[GKV_COLD_V].rotation);
+  auto kern = vrot ? attend_tile_kernel<T, D, true> : attend_tile_kernel<T, D, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  kern<<<(unsigned)((int64_t)a.d.S * a.d.tiles_slice), kDThreads, sm, st>>>(a);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  attend_combine_kernel<<<(unsigned)(a.d.S * a.Q), D, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnParams& a, int dtype, cudaStream_t st) {
+  if (dtype == GKV_BF16) return a.d.D == 64 ? launch_attention_t<__nv_bfloat16, 64>(a, st)
+                                            : launch_attention_t<__nv_bfloat16, 128>(a, st);
+  if (dtype == GKV_F16) return a.d.D == 64 ? launch_attention_t<__half, 64>(a, st)
+                                           : launch_attention_t<__half, 128>(a, st);
+  return a.d.D == 64 ? launch_attention_t<float, 64>(a, st) : launch_attention_t<float, 128>(a, st);
+}
+
+}  // namespace gkv

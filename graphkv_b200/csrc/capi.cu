@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <string>
 
+#include "attention.cuh"
 #include "dequantize.cuh"
 #include "gkv_params.cuh"
 #include "quantize.cuh"
@@ -425,6 +426,88 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
       return cuda_fail(e, "general dequantize kernel");
   }
   return GKV_OK;
+}
+
+namespace {
+
+// Tiles per slice of a dequant / attention call (retained, standard, cold).
+void tile_counts(const Resolved& r, int* tiles) {
+  tiles[0] = r.fast[0] ? (int)ceil_div(r.n[0], kRetTile) : 0;
+  for (int k = 1; k <= 2; ++k) tiles[k] = r.fast[k] ? (int)ceil_div(r.n[k], r.tt) : 0;
+}
+
+// The attention kernels cover layers whose every non-empty tier takes the tile
+// path, with keys grouped along tokens (not rotated) and values along channels.
+int resolve_attention(const gkv_plan* plan, int32_t n_slices, int32_t n_queries, Resolved& r) {
+  if (!plan) return fail(GKV_ERR_INVALID, "plan is NULL");
+  if (n_slices < 1 || n_queries < 1) return fail(GKV_ERR_INVALID, "n_slices and n_queries must be >= 1");
+  if (n_queries > kAttnMaxQueries)
+    return fail(GKV_ERR_TOO_LARGE, "at most " + std::to_string(kAttnMaxQueries) + " queries per slice");
+  const int st = resolve_plan(plan, n_slices, false, nullptr, 0, true, r);
+  if (st != GKV_OK) return st;
+  const gkv_plan& p = *plan;
+  if (p.head_dim != 64 && p.head_dim != 128) return fail(GKV_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
+  for (int tier = 0; tier <= 2; ++tier)
+    if (r.n[tier] > 0 && !r.fast[tier]) return fail(GKV_ERR_UNSUPPORTED, "attention: a tier outside the tile path");
+  for (int tier = 1; tier <= 2; ++tier) {
+    if (r.n[tier] == 0) continue;
+    const TensorDesc& k = r.t[tier == 1 ? GKV_STD_K : GKV_COLD_K];
+    const TensorDesc& v = r.t[tier == 1 ? GKV_STD_V : GKV_COLD_V];
+    if (k.axis != GKV_AXIS_TOKEN || k.rotation || v.axis != GKV_AXIS_CHANNEL)
+      return fail(GKV_ERR_UNSUPPORTED, "attention: keys grouped along tokens and values along channels only");
+  }
+  return GKV_OK;
+}
+
+}  // namespace
+
+size_t gkv_attention_workspace_bytes(const gkv_plan* plan, int32_t n_slices, int32_t n_queries) {
+  Resolved r;
+  if (resolve_attention(plan, n_slices, n_queries, r) != GKV_OK) return 0;
+  int tiles[3];
+  tile_counts(r, tiles);
+  return (size_t)n_slices * (tiles[0] + tiles[1] + tiles[2]) * n_queries * (plan->head_dim + 2) * sizeof(float);
+}
+
+int32_t gkv_attention(const gkv_plan* plan, int32_t n_slices, const float* queries, int32_t n_queries, float* out,
+                      void* workspace, size_t workspace_bytes, gkv_stream_t stream) {
+  if (!queries || !out) return fail(GKV_ERR_INVALID, "queries / out missing");
+  Resolved r;
+  int st = resolve_attention(plan, n_slices, n_queries, r);
+  if (st != GKV_OK) return st;
+  const gkv_plan& p = *plan;
+  AttnParams a;
+  DequantParams& q = a.d;
+  q.T = p.seq_len;
+  q.D = p.head_dim;
+  q.S = n_slices;
+  q.out_T = p.seq_len;
+  q.idx[0] = p.idx_retained;
+  q.idx[1] = p.idx_standard;
+  q.idx[2] = p.idx_cold;
+  for (int k = 0; k < 3; ++k) q.n_tier[k] = r.n[k];
+  for (int i = 0; i < 4; ++i) q.t[i] = r.t[i];
+  q.ret_k = p.retained_k;
+  q.ret_v = p.retained_v;
+  q.out_k = q.out_v = nullptr;
+  q.had_div = p.hadamard_divisor;
+  q.had_inv = p.hadamard_divisor > 0.f ? 1.0f / p.hadamard_divisor : 0.f;
+  q.had_fused = (p.head_dim == 64 || p.head_dim == 128) &&
+                p.hadamard_divisor == (float)std::sqrt((double)p.head_dim);
+  q.tt = r.tt;
+  tile_counts(r, q.tiles);
+  q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
+  q.tile_div = make_fastdiv((uint32_t)(q.tiles_slice > 0 ? q.tiles_slice : 1));
+  const size_t need = (size_t)n_slices * q.tiles_slice * n_queries * (p.head_dim + 2) * sizeof(float);
+  if (!workspace || workspace_bytes < need)
+    return fail(GKV_ERR_WORKSPACE, "attention workspace too small: need " + std::to_string(need) + " bytes");
+  a.q = queries;
+  a.Q = n_queries;
+  a.inv_sqrt_d = (float)(1.0 / std::sqrt((double)p.head_dim));
+  a.part = static_cast<float*>(workspace);
+  a.out = out;
+  cudaError_t e = launch_attention(a, p.dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GKV_OK : cuda_fail(e, "attention kernels");
 }
 
 }  // extern "C"

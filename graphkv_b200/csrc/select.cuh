@@ -261,9 +261,13 @@ __device__ void heap_select_warp(int* q, int k, int n, const Key& key, Before be
   __syncwarp();
 }
 
+// Entries of each array of the shared-memory heap: nodes at 1 .. cap, rounded up
+// to an even count so that the second array also starts 8-byte aligned.
+__host__ __device__ constexpr size_t heap_words(int cap) { return ((size_t)cap + 3) & ~(size_t)1; }
+
 // The same heap with its keys and positions in shared memory (node i at index
 // i + 1 of each array, so the two children 2i + 1, 2i + 2 of a node sit in one
-// 8-byte word and load together).  Only the first k queue slots hold the result
+// 8-byte word and load together; both arrays start 8-byte aligned).  Only the first k queue slots hold the result
 // of the heap select, so the evicted tops are not written back to the queue.
 __device__ void adjust_heap_smem(uint32_t* hk, int* hp, int hole, int len, int item, uint32_t item_key,
                                  Before before) {
@@ -419,7 +423,7 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       if (k <= p.heap_cap) {
         extern __shared__ __align__(16) uint8_t sel_smem[];
         uint32_t* hk = reinterpret_cast<uint32_t*>(sel_smem + p.heap_offset);
-        int* hp = reinterpret_cast<int*>(sel_smem + p.heap_offset + 4 * ((size_t)p.heap_cap + 2));
+        int* hp = reinterpret_cast<int*>(sel_smem + p.heap_offset + 4 * heap_words(p.heap_cap));
         heap_select_warp_smem(q, k, n, key, before, hk, hp);
       } else {
         heap_select_warp(q, k, n, key, before);
@@ -951,7 +955,7 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
     if (k > 0 && (int64_t)k * 64 <= T) cap = k > cap ? k : cap;
   p.heap_cap = 0;
   p.heap_offset = (int)((sm + 15) & ~(size_t)15);
-  const size_t heap_bytes = 8 * ((size_t)cap + 2);
+  const size_t heap_bytes = 8 * heap_words(cap);
   if (cap > 0 && p.heap_offset + heap_bytes + sizeof(SelShared) <= kSelSmemLimit) {
     p.heap_cap = cap;
     sm = p.heap_offset + heap_bytes;

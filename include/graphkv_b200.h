@@ -214,6 +214,20 @@ size_t gkv_dequantize_workspace_bytes(const gkv_plan* plan, int32_t n_slices);
 int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void* v_out,
                        void* workspace, size_t workspace_bytes, gkv_stream_t stream);
 
+/* Attention of n_queries fp32 queries per slice ([S, n_queries, D], S =
+ * batch * kv-heads) over a compressed layer, reading the packed codes directly:
+ * out[s, i, :] = softmax(q_i k^T / sqrt(D)) v over the slice's dequantized keys
+ * and values, without writing them out.  The reference computes this as
+ * attention_from_kv over QuantizedKvLayer.dequantize() (core.py:800-820,
+ * 265-307); the rows attended over are bit-identical to the dequantized
+ * cache's, only the fp32 summation order differs.  Supported: head_dim 64 or
+ * 128, every tier on the tile path, keys grouped along tokens (not rotated),
+ * values along channels; otherwise GKV_ERR_UNSUPPORTED.  At most 16 queries.
+ * workspace: gkv_attention_workspace_bytes(...) bytes (per-tile partials). */
+size_t gkv_attention_workspace_bytes(const gkv_plan* plan, int32_t n_slices, int32_t n_queries);
+int32_t gkv_attention(const gkv_plan* plan, int32_t n_slices, const float* queries, int32_t n_queries, float* out,
+                      void* workspace, size_t workspace_bytes, gkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
