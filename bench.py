@@ -402,10 +402,11 @@ def selection_report(dev) -> dict:
 
 
 def append_report(d, w) -> dict:
-    """Device ms of QuantizedKvCache.append of 1 and of 1024 new tokens to the
-    whole compressed cache of this rank's units (the old tokens are dequantized
-    into the grown buffers and everything is requantized, as the reference's
-    append does)."""
+    """On the whole compressed cache: device ms of one decode step of attention
+    read from the packed codes (against dequantize + fp32 attention), and of
+    QuantizedKvCache.append of 1 and of 1024 new tokens (the old tokens are
+    dequantized into the grown buffers and everything is requantized, as the
+    reference's append does)."""
     import torch
 
     import graphkv_b200 as g
@@ -421,6 +422,32 @@ def append_report(d, w) -> dict:
     out = {}
     gen = torch.Generator(device=d.dev)
     gen.manual_seed(11)
+    # one decode step of attention (1 query per kv-head) over every layer: read from
+    # the packed codes, against dequantize + fp32 attention
+    B, H, T, D = cache.layers[0].original_shape
+    queries = [torch.randn(B, H, 1, D, generator=gen, device=d.dev) for _ in cache.layers]
+
+    def fused():
+        for q, lay in zip(queries, cache.layers):
+            g.attention_from_quantized(q, lay)
+
+    def unfused():
+        for q, lay in zip(queries, cache.layers):
+            k, v = lay.dequantize()
+            g.attention_from_kv(q, k, v)
+
+    for name, fn in (("fused_ms", fused), ("dequantize_then_attend_ms", unfused)):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(d.dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(5):
+            fn()
+        b.record()
+        torch.cuda.synchronize(d.dev)
+        out.setdefault("decode_attention", {})[name] = round(a.elapsed_time(b) / 5, 3)
+    out["decode_attention"]["compressed_bytes"] = cache.memory_bytes()
     for n in (1, 1024):
         B, H, T, D = cache.layers[0].original_shape
         new = [(torch.randn(B, H, n, D, generator=gen, device=d.dev).to(w.dtype),
@@ -582,7 +609,7 @@ def run_ours(args):
                    "parallelism": f"weak shards of (layer, kv-head) units over {d.world} GPU(s)"},
         "phases": phases,
         "select": select_times,
-        "append": append_times,
+        "append_and_attention": append_times,
         "rank_ms": [round(r[0], 4) for r in head["per_rank"]],
         "roofline": roofline,
         "cpu_baseline": cpu,

@@ -129,23 +129,59 @@ __global__ void __launch_bounds__(kDThreads, 4) attend_tile_kernel(const __grid_
   }
 }
 
-// Merge the tiles' partials of one (slice, query): block of D threads.
-__global__ void attend_combine_kernel(const __grid_constant__ AttnParams a) {
+// Merge the tiles' partials of one (slice, query), one block of 256 threads:
+// the largest logit over the tiles, each tile's weight exp(m_j - M) (kept in
+// shared memory), the weighted sum of the l_j, and the weighted sum of the o_j
+// with the tiles split over the block's two halves (128 channels each).
+constexpr int kCombineThreads = 256;
+constexpr int kCombineSmemTiles = 8192;  // weights kept in shared memory up to this many tiles
+
+__device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(kFull, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < kCombineThreads / 32; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  return r;
+}
+
+__global__ void __launch_bounds__(kCombineThreads) attend_combine_kernel(const __grid_constant__ AttnParams a) {
+  __shared__ float wts[kCombineSmemTiles];
+  __shared__ float red[kCombineThreads / 32];
+  __shared__ float half_o[2][128];
   const int sq = blockIdx.x;  // slice * Q + query
   const int s = sq / a.Q, qi = sq - s * a.Q;
   const int D = a.d.D, n = a.d.tiles_slice;
   const float* part = a.part + (int64_t)s * n * a.Q * (D + 2) + qi * (D + 2);
   const int64_t stride = (int64_t)a.Q * (D + 2);
-  float M = -INFINITY;
-  for (int j = 0; j < n; ++j) M = fmaxf(M, part[j * stride]);
-  float L = 0.f, o = 0.f;
-  const int c = threadIdx.x;
-  for (int j = 0; j < n; ++j) {
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < n; j += kCombineThreads) m = fmaxf(m, part[j * stride]);
+  const float M = block_reduce(m, red, true);
+  float l = 0.f;
+  for (int j = threadIdx.x; j < n; j += kCombineThreads) {
     const float w = expf(part[j * stride] - M);
-    L = __fmaf_rn(w, part[j * stride + 1], L);
-    if (c < D) o = __fmaf_rn(w, part[j * stride + 2 + c], o);
+    if (j < kCombineSmemTiles) wts[j] = w;
+    l = __fmaf_rn(w, part[j * stride + 1], l);
   }
-  if (c < D) a.out[(int64_t)sq * D + c] = o / L;
+  const float L = block_reduce(l, red, false);  // its barriers also publish wts
+  const int c = threadIdx.x & 127, h = threadIdx.x >> 7;
+  float o = 0.f;
+  if (c < D) {
+#pragma unroll 4
+    for (int j = h; j < n; j += 2) {
+      const float w = j < kCombineSmemTiles ? wts[j] : expf(part[j * stride] - M);
+      o = __fmaf_rn(w, part[j * stride + 2 + c], o);
+    }
+  }
+  half_o[h][c] = o;
+  __syncthreads();
+  if (h == 0 && c < D) a.out[(int64_t)sq * D + c] = (half_o[0][c] + half_o[1][c]) / L;
 }
 
 template <typename T, int D>
@@ -157,7 +193,7 @@ static cudaError_t launch_attention_t(const AttnParams& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   kern<<<(unsigned)((int64_t)a.d.S * a.d.tiles_slice), kDThreads, sm, st>>>(a);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  attend_combine_kernel<<<(unsigned)(a.d.S * a.Q), D, 0, st>>>(a);
+  attend_combine_kernel<<<(unsigned)(a.d.S * a.Q), kCombineThreads, 0, st>>>(a);
   return cudaGetLastError();
 }
 
