@@ -15,7 +15,6 @@ namespace gkv {
 // ---------------------------------------------------------------------------
 enum DeviceError : int {
   kErrNone = 0,
-  kErrBarrierTimeout = 1,   // a bulk copy did not complete within the spin bound
   kErrSelectCount = 2,      // selection produced list lengths different from the plan
   kErrBadIndex = 3,         // an index list entry outside [0, T)
 };
@@ -211,26 +210,6 @@ struct FastCoder {
   uint32_t flip;  // per-byte XOR applied to unpacked symmetric codes (0x80808080) or 0
 };
 
-template <bool AFF>
-__device__ __forceinline__ FastCoder fast_coder(const GroupCoder& g, bool packed, int bits) {
-  FastCoder c;
-  c.scale = g.scale;
-  c.inv = g.inv;
-  c.zp = g.zp;
-  c.hi = g.hi;
-  if (AFF) {
-    c.magic = kMagic;
-    c.flip = 0u;
-  } else if (packed) {
-    c.magic = kMagic + (float)(1 << (bits - 1));
-    c.flip = 0u;
-  } else {
-    c.magic = kMagic + 128.f;
-    c.flip = 0x80808080u;
-  }
-  return c;
-}
-
 // sum over the first `cnt` element slots of a word of bits(kMagic) << (SB * i), mod 2^32
 template <int SB>
 __host__ __device__ constexpr uint32_t magic_sum(int cnt) {
@@ -243,37 +222,6 @@ __host__ __device__ constexpr uint32_t magic_sum(int cnt) {
 template <int SB>
 __host__ __device__ constexpr uint32_t slot_mask(int cnt) {
   return cnt * SB >= 32 ? 0xFFFFFFFFu : ((1u << (cnt * SB)) - 1u);
-}
-
-template <int SB, bool AFF, int N>
-__device__ __forceinline__ void encode_run(const float* x, const FastCoder& c, uint32_t* w) {
-  static_assert(N % 2 == 0, "pairs");
-  constexpr int EPW = 32 / SB;  // elements per 32-bit word
-  constexpr int NW = (N * SB + 31) / 32;
-  const uint64_t inv2 = pk2(c.inv, c.inv), nsc2 = pk2(-c.scale, -c.scale);
-  const uint64_t mg2 = pk2(c.magic, c.magic), zp2 = pk2(c.zp, c.zp);
-#pragma unroll
-  for (int q = 0; q < NW; ++q) {
-    const int first = q * EPW;
-    const int cnt = (N - first) < EPW ? (N - first) : EPW;
-    uint32_t acc = 0;
-#pragma unroll
-    for (int j = EPW / 2 - 1; j >= 0; --j) {
-      if (2 * j >= cnt) continue;
-      const int e = first + 2 * j;
-      const uint64_t x2 = pk2(x[e], x[e + 1]);
-      const uint64_t q0 = mul2(x2, inv2);
-      uint64_t a2 = fma2(fma2(q0, nsc2, x2), inv2, q0);
-      if (AFF) {
-        a2 = add2(a2, zp2);
-        a2 = pk2(fminf(fmaxf(lo2(a2), 0.f), c.hi), fminf(fmaxf(hi2(a2), 0.f), c.hi));
-      }
-      const uint64_t t2 = add2(a2, mg2);
-      acc = acc * (1u << SB) + hi32(t2);
-      acc = acc * (1u << SB) + lo32(t2);
-    }
-    w[q] = (acc - magic_sum<SB>(cnt)) ^ (c.flip & slot_mask<SB>(cnt));
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -541,74 +489,16 @@ __device__ __forceinline__ T hadamard_scale(float y, float divisor, float inv_di
 }
 
 // ---------------------------------------------------------------------------
-// asynchronous bulk copies (TMA, non-tensor form) with an mbarrier
+// asynchronous 16-byte copies into shared memory
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte aligned),
-// completion signalled on `bar` as transaction bytes.
-__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst_smem)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
 }
 
 // 16-byte asynchronous global -> shared copy; src_bytes == 0 writes zeros
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src), "r"(src_bytes)
                : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-
-// Bounded wait on phase `parity`.  Every thread of the block must call it; returns
-// false on every thread when any thread of the block gave up (error recorded).
-constexpr uint32_t kSpinLimit = 1u << 22;
-
-__device__ __forceinline__ bool block_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t n = 0;
-  bool ok = false;
-  while (n < kSpinLimit) {
-    if (mbar_try_wait(bar, parity)) { ok = true; break; }
-    ++n;
-  }
-  const int failed = __syncthreads_or(ok ? 0 : 1);
-  if (failed) {
-    raise_error(kErrBarrierTimeout);
-    // give the copies in flight a second bounded chance to land before the
-    // block's shared memory is released
-    for (uint32_t m = 0; m < kSpinLimit && !mbar_try_wait(bar, parity); ++m) {}
-    __syncthreads();
-    return false;
-  }
-  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -665,14 +555,6 @@ __device__ __forceinline__ void word_codes(uint32_t w, uint32_t (&out)[32 / SB])
 #pragma unroll
       for (int j = 0; j < 4; ++j) out[4 * k + j] = with_magic(m[j], k);
   }
-}
-
-__device__ __forceinline__ void bar_half(int half) {
-  asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
-}
-// named barrier of the 64 threads of one half of a 128-thread block
-__device__ __forceinline__ void bar_half64(int half) {
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + half) : "memory");
 }
 
 // ---------------------------------------------------------------------------

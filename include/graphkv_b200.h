@@ -13,9 +13,10 @@
  *    every entry point returns without synchronising.
  *  - Return value: GKV_OK (0) or a negative gkv_status; gkv_last_error()
  *    returns a message for the calling thread's last failure.
- *  - Kernels that wait on asynchronous copies do so with bounded spins; when a
- *    bound is hit they record a code in a per-device error word and return.
- *    gkv_device_error() reads and clears that word (it synchronises the device).
+ *  - Kernels record problems they find in the data (an index list entry outside
+ *    [0, T): 3; selection counts that differ from the plan: 2) in a per-device
+ *    error word and carry on without the faulty access; gkv_device_error()
+ *    reads and clears that word (it synchronises the device).
  *
  * Terms
  *  - slice: one (layer, batch row, kv-head) matrix [T, D] of keys or values.
