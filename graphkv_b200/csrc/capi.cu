@@ -530,8 +530,8 @@ namespace {
 constexpr int kStaticSelectMaxTokens = GKV_STATIC_SELECT_MAX_TOKENS;
 constexpr int kMaxDevices = 64;
 
-// Selection workspace for kStaticSelectMaxTokens tokens (13 MiB: tier bytes plus
-// the three int32 tables of the exact tie path).  Every GPU that loads this
+// Selection workspace for kStaticSelectMaxTokens tokens (13 MiB and 256 bytes:
+// tier bytes plus the three 4-byte tables of the exact tie path).  Every GPU that loads this
 // library holds it until the process exits.  In host code `g_select_scratch`
 // only names a host-side handle of the symbol; the device address comes from
 // cudaGetSymbolAddress below.

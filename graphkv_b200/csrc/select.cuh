@@ -16,7 +16,7 @@
 // run by block 0 over the tier bytes in global memory.  A final ordered pass
 // compacts the three ascending index lists, each block at the offsets of the
 // blocks before it.  Workspace: one tier byte per token, then the candidate queue
-// and the two partition stop tables (int32).
+// (positions and keys) and the partition stop tables (int32).
 #pragma once
 
 #include <cooperative_groups.h>
@@ -40,14 +40,14 @@ struct SelectParams {
   int T, sink, tail, keep_protect, keep_outlier, keep_cold;
   int n_ret, n_std, n_cold;
   uint8_t* tier;  // workspace: tier bytes (blocks of more than kSelSmemTokens tokens, exact path)
-  int* queue;     // workspace [T]: candidate queue of the exact tie path
-  int* stop_l;    // workspace [T]: left stops of a partition, by rank
-  int* stop_r;    // workspace [T]: right stops of a partition, by rank
+  int* queue;       // workspace [T]: candidate positions of the exact tie path
+  uint32_t* qkey;   // workspace [T]: their order keys
+  int* stops;       // workspace [T + 1]: stop tables of a partition (or the heap nodes)
   int* idx_ret;
   int* idx_std;
   int* idx_cold;
-  int heap_cap;        // entries of the shared-memory heap of the exact path (0: heap in the workspace)
-  int heap_offset;     // its byte offset in dynamic shared memory (8-byte aligned)
+  int heap_cap;        // heap nodes the shared memory holds for the exact path (0: heap in the workspace)
+  int heap_offset;     // their byte offset in dynamic shared memory (16-byte aligned)
 };
 
 // Monotone key: larger score -> larger key; NaN above +inf (torch.topk ranks NaN
@@ -147,9 +147,10 @@ __device__ __forceinline__ uint32_t key_at(const SelState<SMEM>& st, const float
 // Which of several equal values lands there follows the libstdc++ algorithms
 // (GCC bits/stl_heap.h, bits/stl_algo.h), restated here over order keys:
 //  - heap select: heapify the first k slots, then each later element that
-//    compares before the heap top replaces it (__adjust_heap + __push_heap);
-//    serial in one thread, the scan for replacement candidates warp-parallel
-//    (an element that does not beat the top cannot beat a later top);
+//    compares before the heap top replaces it (__adjust_heap + __push_heap,
+//    restated as one top-down pass); the replacements are serial in one thread,
+//    the scan for them warp-parallel (an element that does not beat the top
+//    cannot beat a later top);
 //  - introselect: median-of-three pivot moved to `first`, unguarded Hoare
 //    partition, continue on the side holding nth; heap select when the depth
 //    limit 2*floor(log2 n) runs out; insertion sort of the last <= 3 slots.
@@ -163,239 +164,216 @@ __device__ __forceinline__ uint32_t key_at(const SelState<SMEM>& st, const float
 //    slot, the M-th right stop.
 // ---------------------------------------------------------------------------
 
-template <bool SMEM>
-struct KeyOf {
-  const SelState<SMEM>& st;
-  const float* src;
-  __device__ __forceinline__ uint32_t operator()(int pos) const { return key_at<SMEM>(st, src, pos); }
-};
-
 struct Before {
   bool largest;
   __device__ __forceinline__ bool operator()(uint32_t a, uint32_t b) const { return largest ? a > b : a < b; }
 };
 
-// __adjust_heap followed by __push_heap on the heap q[first, first + len).
-template <class Key>
-__device__ void adjust_heap(int* q, int first, int hole, int len, int item, uint32_t item_key, const Key& key,
-                            Before before) {
-  const int top = hole;
-  int child = hole;
-  while (child < (len - 1) / 2) {
-    child = 2 * (child + 1);
-    if (before(key(q[first + child]), key(q[first + child - 1]))) --child;
-    q[first + hole] = q[first + child];
-    hole = child;
+// The candidate queue of the exact path: positions q[i] and their order keys
+// qk[i], moved together (so no pass gathers keys through positions).
+struct Queue {
+  int* q;
+  uint32_t* qk;
+  __device__ __forceinline__ void swap(int i, int j) const {
+    const int t = q[i];
+    q[i] = q[j];
+    q[j] = t;
+    const uint32_t u = qk[i];
+    qk[i] = qk[j];
+    qk[j] = u;
   }
-  if ((len & 1) == 0 && child == (len - 2) / 2) {
-    child = 2 * (child + 1);
-    q[first + hole] = q[first + child - 1];
-    hole = child - 1;
+};
+
+// Heap nodes {key, position}; node i of a heap lives at nd[i + 1], so the two
+// children 2i + 1, 2i + 2 of a node share one 16-byte word and its four
+// grandchildren 4i + 3 .. 4i + 6 two more.  Entries beyond the heap's length
+// (up to index len + 3) are read but never used.
+//
+// sift_down(h, x): libstdc++'s __adjust_heap(first, h, len, x) followed by
+// __push_heap, restated top-down.  __adjust_heap moves the hole from h to a leaf
+// along the path of chosen children (the right child unless comp(right, left))
+// and __push_heap moves x back up while comp(parent, x).  Along that path no
+// parent compares before its child (heap order), so the nodes that compare
+// before x form a tail of the path, which __push_heap restores to where they
+// were: walking down and stopping at the first chosen child that compares
+// before x leaves the same heap.  The loads of the next level's pair of
+// children are issued one level ahead.  Returns the key at the root afterwards.
+__host__ __device__ constexpr size_t heap_node_bytes(int cap) { return 8 * ((size_t)cap + 8); }
+
+__device__ __forceinline__ uint32_t sift_down(uint2* nd, int h, int len, uint2 x, Before before) {
+  const int h0 = h;
+  uint32_t root = x.x;
+  int l = 2 * h + 1;
+  uint4 c = make_uint4(0u, 0u, 0u, 0u);
+  if (l < len) c = *reinterpret_cast<const uint4*>(nd + l + 1);
+  while (l < len) {
+    const int gl = 2 * l + 1;  // first grandchild
+    uint4 g0 = make_uint4(0u, 0u, 0u, 0u), g1 = g0;
+    if (gl < len) {
+      g0 = *reinterpret_cast<const uint4*>(nd + gl + 1);
+      g1 = *reinterpret_cast<const uint4*>(nd + gl + 3);
+    }
+    const bool right = l + 1 < len && !before(c.z, c.x);
+    const uint2 ch = right ? make_uint2(c.z, c.w) : make_uint2(c.x, c.y);
+    if (before(ch.x, x.x)) break;
+    nd[h + 1] = ch;
+    if (h == h0) root = ch.x;
+    h = right ? l + 1 : l;
+    l = 2 * h + 1;
+    c = right ? g1 : g0;
   }
-  int parent = (hole - 1) / 2;
-  while (hole > top && before(key(q[first + parent]), item_key)) {
-    q[first + hole] = q[first + parent];
-    hole = parent;
-    parent = (hole - 1) / 2;
-  }
-  q[first + hole] = item;
+  nd[h + 1] = x;
+  return root;
 }
 
-template <class Key>
-__device__ void make_heap(int* q, int first, int len, const Key& key, Before before) {
+// std::make_heap over nodes 0 .. len - 1, one thread.
+__device__ void make_heap_nodes(uint2* nd, int len, Before before) {
   if (len < 2) return;
   for (int parent = (len - 2) / 2;; --parent) {
-    const int item = q[first + parent];
-    adjust_heap(q, first, parent, len, item, key(item), key, before);
+    sift_down(nd, parent, len, nd[parent + 1], before);
     if (parent == 0) break;
   }
 }
 
-// __heap_select(first, middle, last), one thread.
-template <class Key>
-__device__ void heap_select_serial(int* q, int first, int middle, int last, const Key& key, Before before) {
-  const int len = middle - first;
-  make_heap(q, first, len, key, before);
-  uint32_t top = key(q[first]);
-  for (int i = middle; i < last; ++i) {
-    const int item = q[i];
-    const uint32_t k = key(item);
-    if (before(k, top)) {
-      q[i] = q[first];
-      adjust_heap(q, first, 0, len, item, k, key, before);
-      top = key(q[first]);
-    }
-  }
-}
-
-// __heap_select(0, k, n) by warp 0: lanes test 32 slots at a time against the
-// heap top; lane 0 replays the replacements in slot order.
-template <class Key>
-__device__ void heap_select_warp(int* q, int k, int n, const Key& key, Before before) {
+// __heap_select(0, k, n) by one warp over the queue: the first k entries form
+// the heap (nodes in `nd`, at least k + 4 entries, 16-byte aligned); lanes test
+// 256 later entries at a time against the heap top (an entry that does not beat
+// the top cannot beat a later one) and lane 0 replays the replacements in queue
+// order.  The first k queue entries receive the result; the evicted entries
+// are not written back (nothing reads past the first k).
+__device__ void heap_select_warp(const Queue& Q, int k, int n, Before before, uint2* nd) {
   const int lane = threadIdx.x & 31;
-  if (lane == 0) make_heap(q, 0, k, key, before);
+  for (int i = lane; i < k; i += 32) nd[i + 1] = make_uint2(Q.qk[i], (uint32_t)Q.q[i]);
   __syncwarp();
-  uint32_t top = __shfl_sync(0xFFFFFFFFu, lane == 0 ? key(q[0]) : 0u, 0);
-  for (int base = k; base < n; base += 32) {
-    const int i = base + lane;
-    const int item = i < n ? q[i] : 0;
-    const uint32_t ki = i < n ? key(item) : 0u;
-    uint32_t hits = __ballot_sync(0xFFFFFFFFu, i < n && before(ki, top));
-    while (hits) {
-      const int l = __ffs(hits) - 1;
-      hits &= hits - 1;
-      const uint32_t kl = __shfl_sync(0xFFFFFFFFu, ki, l);
-      const int il = __shfl_sync(0xFFFFFFFFu, item, l);
-      if (before(kl, top)) {
-        uint32_t nt = 0;
-        if (lane == 0) {
-          q[base + l] = q[0];
-          adjust_heap(q, 0, 0, k, il, kl, key, before);
-          nt = key(q[0]);
+  if (lane == 0) make_heap_nodes(nd, k, before);
+  __syncwarp();
+  uint32_t top = nd[1].x;
+  constexpr int B = 8;  // 32-entry slices per batch
+  for (int base = k; base < n; base += 32 * B) {
+    uint32_t kk[B];
+    int pp[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int i = base + 32 * j + lane;
+      kk[j] = i < n ? Q.qk[i] : 0u;
+      pp[j] = i < n ? Q.q[i] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int i = base + 32 * j + lane;
+      uint32_t hits = __ballot_sync(0xFFFFFFFFu, i < n && before(kk[j], top));
+      while (hits) {
+        const int l = __ffs(hits) - 1;
+        hits &= hits - 1;
+        const uint32_t kl = __shfl_sync(0xFFFFFFFFu, kk[j], l);
+        const int il = __shfl_sync(0xFFFFFFFFu, pp[j], l);
+        if (before(kl, top)) {
+          uint32_t nt = 0u;
+          if (lane == 0) nt = sift_down(nd, 0, k, make_uint2(kl, (uint32_t)il), before);
+          top = __shfl_sync(0xFFFFFFFFu, nt, 0);
         }
-        __syncwarp();
-        top = __shfl_sync(0xFFFFFFFFu, nt, 0);
       }
     }
   }
   __syncwarp();
+  for (int i = lane; i < k; i += 32) {
+    const uint2 v = nd[i + 1];
+    Q.qk[i] = v.x;
+    Q.q[i] = (int)v.y;
+  }
+  __syncwarp();
 }
 
-// Entries of each array of the shared-memory heap: nodes at 1 .. cap, rounded up
-// to an even count so that the second array also starts 8-byte aligned.
-__host__ __device__ constexpr size_t heap_words(int cap) { return ((size_t)cap + 3) & ~(size_t)1; }
-
-// The same heap with its keys and positions in shared memory (node i at index
-// i + 1 of each array, so the two children 2i + 1, 2i + 2 of a node sit in one
-// 8-byte word and load together; both arrays start 8-byte aligned).  Only the first k queue slots hold the result
-// of the heap select, so the evicted tops are not written back to the queue.
-__device__ void adjust_heap_smem(uint32_t* hk, int* hp, int hole, int len, int item, uint32_t item_key,
-                                 Before before) {
+// __adjust_heap followed by __push_heap on the queue's heap [first, first + len),
+// one thread (the introselect's depth-limit fallback).
+__device__ void adjust_heap_queue(const Queue& Q, int first, int hole, int len, int item, uint32_t item_key,
+                                  Before before) {
+  int* q = Q.q + first;
+  uint32_t* qk = Q.qk + first;
   const int top = hole;
   int child = hole;
   while (child < (len - 1) / 2) {
     child = 2 * (child + 1);
-    const uint2 kk = *reinterpret_cast<const uint2*>(hk + child);  // (left, right) keys
-    const int2 pp = *reinterpret_cast<const int2*>(hp + child);
-    uint32_t ck = kk.y;
-    int cp = pp.y;
-    if (before(kk.y, kk.x)) {
-      --child;
-      ck = kk.x;
-      cp = pp.x;
-    }
-    hk[hole + 1] = ck;
-    hp[hole + 1] = cp;
+    if (before(qk[child], qk[child - 1])) --child;
+    q[hole] = q[child];
+    qk[hole] = qk[child];
     hole = child;
   }
   if ((len & 1) == 0 && child == (len - 2) / 2) {
     child = 2 * (child + 1);
-    hk[hole + 1] = hk[child];
-    hp[hole + 1] = hp[child];
+    q[hole] = q[child - 1];
+    qk[hole] = qk[child - 1];
     hole = child - 1;
   }
   int parent = (hole - 1) / 2;
-  while (hole > top && before(hk[parent + 1], item_key)) {
-    hk[hole + 1] = hk[parent + 1];
-    hp[hole + 1] = hp[parent + 1];
+  while (hole > top && before(qk[parent], item_key)) {
+    q[hole] = q[parent];
+    qk[hole] = qk[parent];
     hole = parent;
     parent = (hole - 1) / 2;
   }
-  hk[hole + 1] = item_key;
-  hp[hole + 1] = item;
+  q[hole] = item;
+  qk[hole] = item_key;
 }
 
-// __heap_select(0, k, n) by warp 0 over a shared-memory heap; the next 32
-// candidates are loaded while the replacements of the current 32 are replayed.
-template <class Key>
-__device__ void heap_select_warp_smem(int* q, int k, int n, const Key& key, Before before, uint32_t* hk, int* hp) {
-  const int lane = threadIdx.x & 31;
-  for (int i = lane; i < k; i += 32) {
-    const int it = q[i];
-    hk[i + 1] = key(it);
-    hp[i + 1] = it;
-  }
-  __syncwarp();
-  if (lane == 0 && k >= 2) {
-    for (int parent = (k - 2) / 2;; --parent) {
-      adjust_heap_smem(hk, hp, parent, k, hp[parent + 1], hk[parent + 1], before);
+// __heap_select(first, middle, last) in place, one thread.
+__device__ void heap_select_serial(const Queue& Q, int first, int middle, int last, Before before) {
+  const int len = middle - first;
+  if (len >= 2)
+    for (int parent = (len - 2) / 2;; --parent) {
+      adjust_heap_queue(Q, first, parent, len, Q.q[first + parent], Q.qk[first + parent], before);
       if (parent == 0) break;
     }
-  }
-  __syncwarp();
-  uint32_t top = hk[1];
-  int item = 0;
-  uint32_t ki = 0u;
-  if (k + lane < n) {
-    item = q[k + lane];
-    ki = key(item);
-  }
-  for (int base = k; base < n; base += 32) {
-    const int i = base + lane;
-    const bool valid = i < n;
-    int item_n = 0;
-    uint32_t ki_n = 0u;
-    if (i + 32 < n) {
-      item_n = q[i + 32];
-      ki_n = key(item_n);
+  for (int i = middle; i < last; ++i) {
+    const int item = Q.q[i];
+    const uint32_t k = Q.qk[i];
+    if (before(k, Q.qk[first])) {
+      Q.q[i] = Q.q[first];
+      Q.qk[i] = Q.qk[first];
+      adjust_heap_queue(Q, first, 0, len, item, k, before);
     }
-    uint32_t hits = __ballot_sync(0xFFFFFFFFu, valid && before(ki, top));
-    while (hits) {
-      const int l = __ffs(hits) - 1;
-      hits &= hits - 1;
-      const uint32_t kl = __shfl_sync(0xFFFFFFFFu, ki, l);
-      const int il = __shfl_sync(0xFFFFFFFFu, item, l);
-      if (before(kl, top)) {
-        if (lane == 0) adjust_heap_smem(hk, hp, 0, k, il, kl, before);
-        __syncwarp();
-        top = hk[1];
-      }
-    }
-    item = item_n;
-    ki = ki_n;
   }
-  __syncwarp();
-  for (int i = lane; i < k; i += 32) q[i] = hp[i + 1];
-  __syncwarp();
 }
 
 // __insertion_sort(first, last), one thread.
-template <class Key>
-__device__ void insertion_sort_serial(int* q, int first, int last, const Key& key, Before before) {
+__device__ void insertion_sort_serial(const Queue& Q, int first, int last, Before before) {
   for (int i = first + 1; i < last; ++i) {
-    const int item = q[i];
-    const uint32_t k = key(item);
-    if (before(k, key(q[first]))) {
-      for (int j = i; j > first; --j) q[j] = q[j - 1];
-      q[first] = item;
+    const int item = Q.q[i];
+    const uint32_t k = Q.qk[i];
+    int j = i;
+    if (before(k, Q.qk[first])) {
+      for (; j > first; --j) {
+        Q.q[j] = Q.q[j - 1];
+        Q.qk[j] = Q.qk[j - 1];
+      }
     } else {
-      int j = i;
-      while (before(k, key(q[j - 1]))) {
-        q[j] = q[j - 1];
+      while (before(k, Q.qk[j - 1])) {
+        Q.q[j] = Q.q[j - 1];
+        Q.qk[j] = Q.qk[j - 1];
         --j;
       }
-      q[j] = item;
     }
+    Q.q[j] = item;
+    Q.qk[j] = k;
   }
 }
 
-// Contiguous piece of [lo, hi) for warp w (multiples of 32 slots).
+// Contiguous piece of [lo, hi) for warp w (multiples of 128 slots).
 __device__ __forceinline__ Chunk range_chunk(int lo, int hi, int w) {
   const int len = hi - lo;
-  const int per = ((len + kSelWarps - 1) / kSelWarps + 31) & ~31;
+  const int per = ((len + kSelWarps - 1) / kSelWarps + 127) & ~127;
   const int b = min(hi, lo + w * per);
   return {b, min(hi, b + per)};
 }
 
 // Mark the k candidates torch.topk would choose, by one block over all T tokens
 // (st: tier bytes of [0, T)).  The candidates are compacted into the queue in
-// position order first.
+// position order first, with their keys beside them.
 template <bool SMEM>
 __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, const float* src, int k, bool largest,
                              uint8_t mark, SelShared& sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int* const q = p.queue;
-  const KeyOf<SMEM> key{st, src};
+  const Queue Q{p.queue, p.qkey};
   const Before before{largest};
   // queue of candidates in position order
   const Chunk ch = warp_chunk(0, p.T, warp);
@@ -411,7 +389,11 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
     const int t = b + lane;
     const bool c = t < ch.end && st.tier[t] == kCand;
     const uint32_t bal = __ballot_sync(0xFFFFFFFFu, c);
-    if (c) q[off + __popc(bal & ((1u << lane) - 1u))] = t;
+    if (c) {
+      const uint32_t pos = off + __popc(bal & ((1u << lane) - 1u));
+      Q.q[pos] = t;
+      Q.qk[pos] = key_at<SMEM>(st, src, t);
+    }
     off += __popc(bal);
   }
   const int n = (int)(sh.warp_off[0][kSelWarps - 1] + sh.warp_cnt[0][kSelWarps - 1]);
@@ -420,14 +402,10 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
   if (k <= 0) return;
   if ((int64_t)k * 64 <= n) {
     if (warp == 0) {
-      if (k <= p.heap_cap) {
-        extern __shared__ __align__(16) uint8_t sel_smem[];
-        uint32_t* hk = reinterpret_cast<uint32_t*>(sel_smem + p.heap_offset);
-        int* hp = reinterpret_cast<int*>(sel_smem + p.heap_offset + 4 * heap_words(p.heap_cap));
-        heap_select_warp_smem(q, k, n, key, before, hk, hp);
-      } else {
-        heap_select_warp(q, k, n, key, before);
-      }
+      extern __shared__ __align__(16) uint8_t sel_smem[];
+      uint2* nd = k <= p.heap_cap ? reinterpret_cast<uint2*>(sel_smem + p.heap_offset)
+                                  : reinterpret_cast<uint2*>(p.stops);  // k * 64 <= T: room for k + 4 nodes
+      heap_select_warp(Q, k, n, before, nd);
     }
   } else {
     const int nth = k - 1;
@@ -444,10 +422,8 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       if (done || last - first <= 3) break;
       if (depth == 0) {
         if (threadIdx.x == 0) {
-          heap_select_serial(q, first, nth + 1, last, key, before);
-          const int t = q[first];
-          q[first] = q[nth];
-          q[nth] = t;
+          heap_select_serial(Q, first, nth + 1, last, before);
+          Q.swap(first, nth);
           sh.done = 2;
         }
         break;
@@ -455,34 +431,48 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       if (threadIdx.x == 0) {
         sh.depth = depth - 1;
         const int a = first + 1, b = first + (last - first) / 2, c = last - 1;
-        const uint32_t ka = key(q[a]), kb = key(q[b]), kc = key(q[c]);
+        const uint32_t ka = Q.qk[a], kb = Q.qk[b], kc = Q.qk[c];
         int m;
-        if (before(ka, kb)) m = before(kb, kc) ? b : (before(ka, kc) ? c : a);
-        else if (before(ka, kc)) m = a;
-        else if (before(kb, kc)) m = c;
-        else m = b;
-        const int t = q[first];
-        q[first] = q[m];
-        q[m] = t;
-        sh.pivot = key(q[first]);
+        uint32_t km;
+        if (before(ka, kb)) {
+          if (before(kb, kc)) m = b, km = kb;
+          else if (before(ka, kc)) m = c, km = kc;
+          else m = a, km = ka;
+        } else if (before(ka, kc)) {
+          m = a, km = ka;
+        } else if (before(kb, kc)) {
+          m = c, km = kc;
+        } else {
+          m = b, km = kb;
+        }
+        Q.swap(first, m);
+        sh.pivot = km;
         sh.pairs = 0;
       }
       __syncthreads();
       const uint32_t piv = sh.pivot;
       const int lo = first + 1, hi = last;
+      // Stop tables: at most (hi - lo) / 2 swaps, so left stops of rank <= H and
+      // right stops of rank < H are all that is read; they share one region.
+      const int H = (hi - lo) / 2;
+      int* const stop_l = p.stops;
+      int* const stop_r = p.stops + H + 1;
       const Chunk rc = range_chunk(lo, hi, warp);
       // pass 1: left / right stops per warp piece
       uint32_t nl = 0, nr = 0;
-      for (int b = rc.begin; b < rc.end; b += 32) {
-        const int i = b + lane;
-        bool ls = false, rs = false;
-        if (i < rc.end) {
-          const uint32_t kk = key(q[i]);
-          ls = !before(kk, piv);
-          rs = !before(piv, kk);
+      for (int b = rc.begin; b < rc.end; b += 128) {
+        uint32_t kk[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = b + 32 * j + lane;
+          kk[j] = i < rc.end ? Q.qk[i] : 0u;
         }
-        nl += __popc(__ballot_sync(0xFFFFFFFFu, ls));
-        nr += __popc(__ballot_sync(0xFFFFFFFFu, rs));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool valid = b + 32 * j + lane < rc.end;
+          nl += __popc(__ballot_sync(0xFFFFFFFFu, valid && !before(kk[j], piv)));
+          nr += __popc(__ballot_sync(0xFFFFFFFFu, valid && !before(piv, kk[j])));
+        }
       }
       if (lane == 0) {
         sh.warp_cnt[0][warp] = nl;
@@ -494,23 +484,29 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       // pass 2: ranks, stop tables and the swap count
       uint32_t left_before = sh.warp_off[0][warp], right_before = sh.warp_off[1][warp];
       int best = 0;
-      for (int b = rc.begin; b < rc.end; b += 32) {
-        const int i = b + lane;
-        bool ls = false, rs = false;
-        if (i < rc.end) {
-          const uint32_t kk = key(q[i]);
-          ls = !before(kk, piv);
-          rs = !before(piv, kk);
+      const uint32_t below = (1u << lane) - 1u;
+      for (int b = rc.begin; b < rc.end; b += 128) {
+        uint32_t kk[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = b + 32 * j + lane;
+          kk[j] = i < rc.end ? Q.qk[i] : 0u;
         }
-        const uint32_t bl = __ballot_sync(0xFFFFFFFFu, ls), br = __ballot_sync(0xFFFFFFFFu, rs);
-        const uint32_t below = (1u << lane) - 1u;
-        const int lrank = (int)(left_before + __popc(bl & below));     // left stops in [lo, i)
-        const int rbefore = (int)(right_before + __popc(br & below));  // right stops in [lo, i)
-        if (ls) p.stop_l[lrank] = i;
-        if (rs) p.stop_r[total_r - 1 - rbefore] = i;
-        if (i < rc.end) best = max(best, min(lrank, total_r - rbefore));  // cut just before slot i
-        left_before += __popc(bl);
-        right_before += __popc(br);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = b + 32 * j + lane;
+          const bool valid = i < rc.end;
+          const bool ls = valid && !before(kk[j], piv), rs = valid && !before(piv, kk[j]);
+          const uint32_t bl = __ballot_sync(0xFFFFFFFFu, ls), br = __ballot_sync(0xFFFFFFFFu, rs);
+          const int lrank = (int)(left_before + __popc(bl & below));     // left stops in [lo, i)
+          const int rbefore = (int)(right_before + __popc(br & below));  // right stops in [lo, i)
+          const int ri = total_r - 1 - rbefore;
+          if (ls && lrank <= H) stop_l[lrank] = i;
+          if (rs && ri < H) stop_r[ri] = i;
+          if (valid) best = max(best, min(lrank, total_r - rbefore));  // cut just before slot i
+          left_before += __popc(bl);
+          right_before += __popc(br);
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
@@ -518,16 +514,11 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       __syncthreads();
       const int pairs = sh.pairs;
       // pass 3: the swaps (disjoint slot pairs)
-      for (int m = threadIdx.x; m < pairs; m += kSelThreads) {
-        const int i = p.stop_l[m], j = p.stop_r[m];
-        const int t = q[i];
-        q[i] = q[j];
-        q[j] = t;
-      }
+      for (int m = threadIdx.x; m < pairs; m += kSelThreads) Q.swap(stop_l[m], stop_r[m]);
       if (threadIdx.x == 0) {
         int cut = -1;
-        if (pairs >= 1 && !(pairs < total_l && p.stop_l[pairs] < p.stop_r[pairs - 1])) cut = p.stop_r[pairs - 1];
-        else if (pairs < total_l) cut = p.stop_l[pairs];
+        if (pairs >= 1 && !(pairs < total_l && stop_l[pairs] < stop_r[pairs - 1])) cut = stop_r[pairs - 1];
+        else if (pairs < total_l) cut = stop_l[pairs];
         if (cut < 0) {  // unreachable: the median of three guards the left scan
           raise_error(kErrSelectCount);
           sh.done = 1;
@@ -540,10 +531,10 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       __syncthreads();
     }
     __syncthreads();
-    if (threadIdx.x == 0 && sh.done == 0) insertion_sort_serial(q, sh.first, sh.last, key, before);
+    if (threadIdx.x == 0 && sh.done == 0) insertion_sort_serial(Q, sh.first, sh.last, before);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < k; i += kSelThreads) st.tier[q[i]] = mark;
+  for (int i = threadIdx.x; i < k; i += kSelThreads) st.tier[Q.q[i]] = mark;
   __syncthreads();
 }
 
@@ -918,10 +909,13 @@ __global__ void outlier_kernel(const gkv_layer_in L, int B, int T, int D, float*
 
 }  // namespace
 
-// Workspace of the select kernel: tier bytes [T], then queue, left and right stop
-// tables (int32 [T] each), every region 256-byte aligned.
+// Workspace of the select kernel: tier bytes [T], then the queue's positions and
+// keys (4 bytes [T] each) and the stop tables (int32 [T + 1]), every region
+// 256-byte aligned.
 constexpr size_t select_region(int T) { return ((size_t)T * 4 + 255) & ~(size_t)255; }
-constexpr size_t select_workspace(int T) { return (((size_t)T + 255) & ~(size_t)255) + 3 * select_region(T); }
+constexpr size_t select_workspace(int T) {
+  return (((size_t)T + 255) & ~(size_t)255) + 2 * select_region(T) + select_region(T + 1);
+}
 
 cudaError_t launch_select(const float* scores, const float* outlier, const gkv_select_policy& pol, int* idx_ret,
                           int* idx_std, int* idx_cold, uint8_t* workspace, cudaStream_t st) {
@@ -942,8 +936,8 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
   p.tier = w;
   w += ((size_t)T + 255) & ~(size_t)255;
   p.queue = reinterpret_cast<int*>(w);
-  p.stop_l = reinterpret_cast<int*>(w + select_region(T));
-  p.stop_r = reinterpret_cast<int*>(w + 2 * select_region(T));
+  p.qkey = reinterpret_cast<uint32_t*>(w + select_region(T));
+  p.stops = reinterpret_cast<int*>(w + 2 * select_region(T));
   p.idx_ret = idx_ret;
   p.idx_std = idx_std;
   p.idx_cold = idx_cold;
@@ -955,7 +949,7 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
     if (k > 0 && (int64_t)k * 64 <= T) cap = k > cap ? k : cap;
   p.heap_cap = 0;
   p.heap_offset = (int)((sm + 15) & ~(size_t)15);
-  const size_t heap_bytes = 8 * heap_words(cap);
+  const size_t heap_bytes = heap_node_bytes(cap);
   if (cap > 0 && p.heap_offset + heap_bytes + sizeof(SelShared) <= kSelSmemLimit) {
     p.heap_cap = cap;
     sm = p.heap_offset + heap_bytes;

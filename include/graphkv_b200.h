@@ -160,7 +160,7 @@ int32_t gkv_select_tiers(const float* scores, const float* outlier_scores, const
  * device-wide synchronisation.
  *  - Limit: seq_len <= GKV_STATIC_SELECT_MAX_TOKENS; larger sizes return
  *    GKV_ERR_TOO_LARGE without launching anything.
- *  - The scratch is a 13 MiB device array inside the library (the selection
+ *  - The scratch is a 13 MiB (+256 B) device array inside the library (the selection
  *    workspace of GKV_STATIC_SELECT_MAX_TOKENS tokens); every GPU that loads
  *    the library keeps it until the process exits.
  *  - The first call on a device looks up the array's device address

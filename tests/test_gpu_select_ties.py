@@ -85,6 +85,9 @@ CASES = [
     (10000, "graphkv", {"semantic_protection_ratio": 0.3, "low_priority_ratio": 0.01}, "levels5"),
     (60000, "graphkv", {"semantic_protection_ratio": 0.5, "long_low_priority_ratio": 0.005}, "levels20"),
     (8192, "graphkv", {"min_protected_tokens": 5000}, "levels3"),
+    # shared-memory variant whose heap (4497 nodes) does not fit beside the block's
+    # tokens: the heap select keeps its nodes in the workspace
+    (300000, "graphkv", {"semantic_protection_ratio": 0.015}, "levels200"),
 ]
 
 
