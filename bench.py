@@ -447,6 +447,31 @@ def append_report(d, w) -> dict:
         b.record()
         torch.cuda.synchronize(d.dev)
         out.setdefault("decode_attention", {})[name] = round(a.elapsed_time(b) / 5, 3)
+    # the same 28 layer calls replayed from a CUDA graph: the kernels' device time
+    # without the Python calls between them
+    try:
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(d.dev)
+        side.wait_stream(torch.cuda.current_stream(d.dev))
+        with torch.cuda.stream(side):
+            fused()
+            torch.cuda.synchronize(d.dev)
+            with torch.cuda.graph(graph, stream=side):
+                fused()
+        torch.cuda.current_stream(d.dev).wait_stream(side)
+        graph.replay()
+        torch.cuda.synchronize(d.dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(20):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(d.dev)
+        out["decode_attention"]["fused_graph_ms"] = round(a.elapsed_time(b) / 20, 4)
+        del graph
+    except RuntimeError as e:  # capture unsupported here: report why
+        out["decode_attention"]["fused_graph_ms"] = None
+        out["decode_attention"]["graph_note"] = str(e)[:120]
     out["decode_attention"]["compressed_bytes"] = cache.memory_bytes()
     for n in (1, 1024):
         B, H, T, D = cache.layers[0].original_shape

@@ -119,7 +119,7 @@ class QuantizedTensor:
             plan.codes[slot] = self.q.data_ptr()
             plan.scales[slot] = self.scales.data_ptr()
             plan.zero_points[slot] = L.ptr(self.zero_points)
-        plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+        plan.hadamard_divisor = sqrt(D)  # the c_float field rounds it to fp32, as torch does
         out = torch.empty((2, B, H, n, D), dtype=self.original_dtype, device=dev)
         with torch.cuda.device(dev):
             L.check(lib.gkv_dequantize(ctypes.byref(plan), B * H, out[0].data_ptr(), out[1].data_ptr(), None, 0,
@@ -731,7 +731,7 @@ class _GroupRun:
         plan.idx_retained = self.idx_ret.data_ptr()
         plan.idx_standard = self.idx_std.data_ptr()
         plan.idx_cold = self.idx_cold.data_ptr()
-        plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+        plan.hadamard_divisor = sqrt(D)  # the c_float field rounds it to fp32, as torch does
         plan.retained_k, plan.retained_v = ar.ptr(h_ret[0]), ar.ptr(h_ret[1])
         for i, p in enumerate(plans):
             if p is None:
@@ -985,7 +985,7 @@ def _run_plan(run: list[QuantizedKvLayer]):
     plan.idx_retained = first.retained_indices.data_ptr()
     plan.idx_standard = first.compressed_indices.data_ptr()
     plan.idx_cold = lp.data_ptr() if lp is not None else 0
-    plan.hadamard_divisor = float(torch.tensor(sqrt(D), dtype=torch.float32))
+    plan.hadamard_divisor = sqrt(D)  # the c_float field rounds it to fp32, as torch does
     plan.retained_k, plan.retained_v = first.retained_keys.data_ptr(), first.retained_values.data_ptr()
     for i, t in enumerate(qts):
         if t is None:

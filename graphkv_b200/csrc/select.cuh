@@ -46,8 +46,7 @@ struct SelectParams {
   int* idx_ret;
   int* idx_std;
   int* idx_cold;
-  int heap_cap;        // heap nodes the shared memory holds for the exact path (0: heap in the workspace)
-  int heap_offset;     // their byte offset in dynamic shared memory (16-byte aligned)
+  int smem_bytes;      // dynamic shared memory of each block (the exact path's scratch in block 0)
 };
 
 // Monotone key: larger score -> larger key; NaN above +inf (torch.topk ranks NaN
@@ -168,6 +167,12 @@ struct Before {
   bool largest;
   __device__ __forceinline__ bool operator()(uint32_t a, uint32_t b) const { return largest ? a > b : a < b; }
 };
+// The same order with the direction fixed at compile time (the heap select's
+// serial sifts).
+template <bool LARGEST>
+struct BeforeC {
+  __device__ __forceinline__ bool operator()(uint32_t a, uint32_t b) const { return LARGEST ? a > b : a < b; }
+};
 
 // The candidate queue of the exact path: positions q[i] and their order keys
 // qk[i], moved together (so no pass gathers keys through positions).
@@ -183,6 +188,14 @@ struct Queue {
     qk[j] = u;
   }
 };
+
+// Contiguous piece of [lo, hi) for warp w (multiples of 128 slots).
+__device__ __forceinline__ Chunk range_chunk(int lo, int hi, int w) {
+  const int len = hi - lo;
+  const int per = ((len + kSelWarps - 1) / kSelWarps + 127) & ~127;
+  const int b = min(hi, lo + w * per);
+  return {b, min(hi, b + per)};
+}
 
 // Heap nodes {key, position}; node i of a heap lives at nd[i + 1], so the two
 // children 2i + 1, 2i + 2 of a node share one 16-byte word and its four
@@ -200,88 +213,155 @@ struct Queue {
 // children are issued one level ahead.  Returns the key at the root afterwards.
 __host__ __device__ constexpr size_t heap_node_bytes(int cap) { return 8 * ((size_t)cap + 8); }
 
-__device__ __forceinline__ uint32_t sift_down(uint2* nd, int h, int len, uint2 x, Before before) {
+template <class Cmp>
+__device__ __forceinline__ uint32_t sift_down(uint2* nd, int h, int len, uint2 x, Cmp before) {
+  // A uniform number of levels (the depth below h), with the moves predicated
+  // and the loads unconditional (node pair 0 stands in past the heap's end), so
+  // no branch waits on a loaded key; the next pair of children is loaded one
+  // level ahead.
   const int h0 = h;
   uint32_t root = x.x;
+  const int levels = (31 - __clz(len)) - (31 - __clz(h0 + 1));
+  bool go = true;
   int l = 2 * h + 1;
-  uint4 c = make_uint4(0u, 0u, 0u, 0u);
-  if (l < len) c = *reinterpret_cast<const uint4*>(nd + l + 1);
-  while (l < len) {
+  uint4 c = *reinterpret_cast<const uint4*>(nd + (l < len ? l + 1 : 0));
+  for (int it = 0; it < levels; ++it) {
     const int gl = 2 * l + 1;  // first grandchild
-    uint4 g0 = make_uint4(0u, 0u, 0u, 0u), g1 = g0;
-    if (gl < len) {
-      g0 = *reinterpret_cast<const uint4*>(nd + gl + 1);
-      g1 = *reinterpret_cast<const uint4*>(nd + gl + 3);
-    }
+    const bool gok = gl < len;
+    const uint4 g0 = *reinterpret_cast<const uint4*>(nd + (gok ? gl + 1 : 0));
+    const uint4 g1 = *reinterpret_cast<const uint4*>(nd + (gok ? gl + 3 : 0));
+    const bool has = go && l < len;
     const bool right = l + 1 < len && !before(c.z, c.x);
     const uint2 ch = right ? make_uint2(c.z, c.w) : make_uint2(c.x, c.y);
-    if (before(ch.x, x.x)) break;
-    nd[h + 1] = ch;
-    if (h == h0) root = ch.x;
-    h = right ? l + 1 : l;
-    l = 2 * h + 1;
+    go = has && !before(ch.x, x.x);
+    if (go) nd[h + 1] = ch;
+    root = (go && h == h0) ? ch.x : root;
+    h = go ? (right ? l + 1 : l) : h;
+    l = go ? 2 * h + 1 : l;
     c = right ? g1 : g0;
   }
   nd[h + 1] = x;
   return root;
 }
 
-// std::make_heap over nodes 0 .. len - 1, one thread.
-__device__ void make_heap_nodes(uint2* nd, int len, Before before) {
+// std::make_heap over nodes 0 .. len - 1 by one warp.  libstdc++ sifts the
+// parents from (len - 2) / 2 down to 0; the parents of one depth have disjoint
+// subtrees and all deeper parents come first, so each depth is sifted by the
+// lanes at once.
+template <class Cmp>
+__device__ __forceinline__ void make_heap_warp(uint2* nd, int len, Cmp before) {
+  const int lane = threadIdx.x & 31;
   if (len < 2) return;
-  for (int parent = (len - 2) / 2;; --parent) {
-    sift_down(nd, parent, len, nd[parent + 1], before);
-    if (parent == 0) break;
+  const int last_parent = (len - 2) / 2;
+  for (int d = 31 - __clz(last_parent + 1); d >= 0; --d) {
+    const int lo = (1 << d) - 1, hi = min(2 * lo, last_parent);  // parents of depth d
+    for (int parent = hi - lane; parent >= lo; parent -= 32) sift_down(nd, parent, len, nd[parent + 1], before);
+    __syncwarp();
   }
 }
 
-// __heap_select(0, k, n) by one warp over the queue: the first k entries form
-// the heap (nodes in `nd`, at least k + 4 entries, 16-byte aligned); lanes test
-// 256 later entries at a time against the heap top (an entry that does not beat
-// the top cannot beat a later one) and lane 0 replays the replacements in queue
-// order.  The first k queue entries receive the result; the evicted entries
-// are not written back (nothing reads past the first k).
-__device__ void heap_select_warp(const Queue& Q, int k, int n, Before before, uint2* nd) {
+// Replacements of the heap select for the candidates list[0 .. m) (queue order),
+// by one warp: candidate x replaces the top when it compares before it
+// (__pop_heap + __adjust_heap).  The lanes test 32 candidates at a time against
+// the top; lane 0 replays the replacements among them in order, re-testing each
+// against its current top.  Returns the top.
+template <class Cmp>
+__device__ __forceinline__ uint32_t heap_replay(uint2* nd, int len, const uint2* list, int m, uint32_t top,
+                                                Cmp before) {
   const int lane = threadIdx.x & 31;
-  for (int i = lane; i < k; i += 32) nd[i + 1] = make_uint2(Q.qk[i], (uint32_t)Q.q[i]);
-  __syncwarp();
-  if (lane == 0) make_heap_nodes(nd, k, before);
-  __syncwarp();
-  uint32_t top = nd[1].x;
-  constexpr int B = 8;  // 32-entry slices per batch
-  for (int base = k; base < n; base += 32 * B) {
-    uint32_t kk[B];
-    int pp[B];
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      const int i = base + 32 * j + lane;
-      kk[j] = i < n ? Q.qk[i] : 0u;
-      pp[j] = i < n ? Q.q[i] : 0;
-    }
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      const int i = base + 32 * j + lane;
-      uint32_t hits = __ballot_sync(0xFFFFFFFFu, i < n && before(kk[j], top));
-      while (hits) {
-        const int l = __ffs(hits) - 1;
-        hits &= hits - 1;
-        const uint32_t kl = __shfl_sync(0xFFFFFFFFu, kk[j], l);
-        const int il = __shfl_sync(0xFFFFFFFFu, pp[j], l);
-        if (before(kl, top)) {
-          uint32_t nt = 0u;
-          if (lane == 0) nt = sift_down(nd, 0, k, make_uint2(kl, (uint32_t)il), before);
-          top = __shfl_sync(0xFFFFFFFFu, nt, 0);
+  for (int base = 0; base < m; base += 32) {
+    const int e = base + lane;
+    const uint2 ce = e < m ? list[e] : make_uint2(0u, 0u);
+    uint32_t hits = __ballot_sync(0xFFFFFFFFu, e < m && before(ce.x, top));
+    if (hits) {
+      if (lane == 0) {
+        while (hits) {
+          const int f = __ffs(hits) - 1;
+          hits &= hits - 1;
+          const uint2 x = list[base + f];
+          if (before(x.x, top)) top = sift_down(nd, 0, len, x, before);
         }
       }
+      top = __shfl_sync(0xFFFFFFFFu, top, 0);
     }
   }
   __syncwarp();
-  for (int i = lane; i < k; i += 32) {
-    const uint2 v = nd[i + 1];
-    Q.qk[i] = v.x;
-    Q.q[i] = (int)v.y;
+  return top;
+}
+
+// __heap_select(0, k, n) over the queue by the whole block.  The heap's nodes
+// live in `nd` (at least k + 8 entries, 16-byte aligned); the queue after the
+// first k entries is taken in windows of at most `lcap` entries: the block
+// copies the entries of a window that compare before the current top (the top
+// only moves on, so no other entry of the window can replace it) into `list`,
+// in queue order, and warp 0 replays them.  The first k queue entries receive
+// the result; the evicted entries are not written back (nothing reads past the
+// first k).
+template <class Cmp>
+__device__ __forceinline__ void heap_select_block(const Queue& Q, int k, int n, Cmp before, uint2* nd, uint2* list,
+                                                  int lcap,
+                                  SelShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    for (int i = lane; i < k; i += 32) nd[i + 1] = make_uint2(Q.qk[i], (uint32_t)Q.q[i]);
+    __syncwarp();
+    make_heap_warp(nd, k, before);
+    if (lane == 0) sh.pivot = nd[1].x;
   }
-  __syncwarp();
+  __syncthreads();
+  for (int lo = k; lo < n; lo += lcap) {
+    const int hi = min(n, lo + lcap);
+    const uint32_t top = sh.pivot;
+    const Chunk rc = range_chunk(lo, hi, warp);
+    uint32_t cnt = 0;
+    for (int b = rc.begin; b < rc.end; b += 128) {
+      uint32_t kk[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = b + 32 * j + lane;
+        kk[j] = i < rc.end ? Q.qk[i] : 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        cnt += __popc(__ballot_sync(0xFFFFFFFFu, b + 32 * j + lane < rc.end && before(kk[j], top)));
+    }
+    if (lane == 0) sh.warp_cnt[0][warp] = cnt;
+    scan_warp_counts(sh, 1);
+    uint32_t off = sh.warp_off[0][warp];
+    const uint32_t below = (1u << lane) - 1u;
+    for (int b = rc.begin; b < rc.end; b += 128) {
+      uint32_t kk[4];
+      int pp[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = b + 32 * j + lane;
+        kk[j] = i < rc.end ? Q.qk[i] : 0u;
+        pp[j] = i < rc.end ? Q.q[i] : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool hit = b + 32 * j + lane < rc.end && before(kk[j], top);
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, hit);
+        if (hit) list[off + __popc(bal & below)] = make_uint2(kk[j], (uint32_t)pp[j]);
+        off += __popc(bal);
+      }
+    }
+    const int m = (int)(sh.warp_off[0][kSelWarps - 1] + sh.warp_cnt[0][kSelWarps - 1]);
+    __syncthreads();
+    if (warp == 0) {
+      const uint32_t t = heap_replay(nd, k, list, m, top, before);
+      if (lane == 0) sh.pivot = t;
+    }
+    __syncthreads();
+  }
+  if (warp == 0) {
+    for (int i = lane; i < k; i += 32) {
+      const uint2 v = nd[i + 1];
+      Q.qk[i] = v.x;
+      Q.q[i] = (int)v.y;
+    }
+  }
+  __syncthreads();
 }
 
 // __adjust_heap followed by __push_heap on the queue's heap [first, first + len),
@@ -358,12 +438,22 @@ __device__ void insertion_sort_serial(const Queue& Q, int first, int last, Befor
   }
 }
 
-// Contiguous piece of [lo, hi) for warp w (multiples of 128 slots).
-__device__ __forceinline__ Chunk range_chunk(int lo, int hi, int w) {
-  const int len = hi - lo;
-  const int per = ((len + kSelWarps - 1) / kSelWarps + 127) & ~127;
-  const int b = min(hi, lo + w * per);
-  return {b, min(hi, b + per)};
+
+// Candidates (tier byte kCand) among tokens t0 .. t0 + 15 below `end`, as a bit
+// mask (bit i: token t0 + i); t0 is a multiple of 16.
+__device__ __forceinline__ uint32_t cand_mask16(const uint8_t* tier, int t0, int end) {
+  uint32_t w[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
+  if (t0 + 16 <= end) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tier + t0);
+    w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+  } else {
+    for (int i = 0; i < 16 && t0 + i < end; ++i)
+      w[i >> 2] = (w[i >> 2] & ~(0xFFu << (8 * (i & 3)))) | ((uint32_t)tier[t0 + i] << (8 * (i & 3)));
+  }
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m |= (((w[i >> 2] >> (8 * (i & 3))) & 0xFFu) == kCand ? 1u : 0u) << i;
+  return m;
 }
 
 // Mark the k candidates torch.topk would choose, by one block over all T tokens
@@ -375,40 +465,72 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const Queue Q{p.queue, p.qkey};
   const Before before{largest};
-  // queue of candidates in position order
-  const Chunk ch = warp_chunk(0, p.T, warp);
+  // queue of candidates in position order: 16 tokens per lane per step (one
+  // 16-byte load of tier bytes), the lanes' counts scanned across the warp
+  const Chunk ch = warp_chunk(0, p.T, warp);  // starts at a multiple of 128
   uint32_t cnt = 0;
-  for (int b = ch.begin; b < ch.end; b += 32) {
-    const int t = b + lane;
-    cnt += __popc(__ballot_sync(0xFFFFFFFFu, t < ch.end && st.tier[t] == kCand));
-  }
+  for (int b = ch.begin; b < ch.end; b += 512) cnt += __popc(cand_mask16(st.tier, b + 16 * lane, ch.end));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
   if (lane == 0) sh.warp_cnt[0][warp] = cnt;
   scan_warp_counts(sh, 1);
   uint32_t off = sh.warp_off[0][warp];
-  for (int b = ch.begin; b < ch.end; b += 32) {
-    const int t = b + lane;
-    const bool c = t < ch.end && st.tier[t] == kCand;
-    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, c);
-    if (c) {
-      const uint32_t pos = off + __popc(bal & ((1u << lane) - 1u));
-      Q.q[pos] = t;
-      Q.qk[pos] = key_at<SMEM>(st, src, t);
+  const uint32_t below = (1u << lane) - 1u;
+  for (int b = ch.begin; b < ch.end; b += 128) {  // coalesced stores: 32 tokens per ballot
+    uint8_t tb[4];
+    float sc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = b + 32 * j + lane;
+      tb[j] = t < ch.end ? st.tier[t] : (uint8_t)0xFF;
+      sc[j] = tb[j] == kCand ? src[t] : 0.f;
     }
-    off += __popc(bal);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool c = tb[j] == kCand;
+      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, c);
+      if (c) {
+        const uint32_t pos = off + __popc(bal & below);
+        Q.q[pos] = b + 32 * j + lane;
+        Q.qk[pos] = order_key(sc[j]);
+      }
+      off += __popc(bal);
+    }
   }
   const int n = (int)(sh.warp_off[0][kSelWarps - 1] + sh.warp_cnt[0][kSelWarps - 1]);
   __syncthreads();
   if (k > n) k = n;  // the count check reports the shortfall
   if (k <= 0) return;
   if ((int64_t)k * 64 <= n) {
-    if (warp == 0) {
-      extern __shared__ __align__(16) uint8_t sel_smem[];
-      uint2* nd = k <= p.heap_cap ? reinterpret_cast<uint2*>(sel_smem + p.heap_offset)
-                                  : reinterpret_cast<uint2*>(p.stops);  // k * 64 <= T: room for k + 4 nodes
-      heap_select_warp(Q, k, n, before, nd);
+    // Scratch: this block's dynamic shared memory (its own tokens' tier bytes
+    // are in the workspace meanwhile; the caller restores its keys).  The heap
+    // nodes go there when they leave room for a window of 4096 entries, else
+    // into the stop table (k * 64 <= T: room for k + 8 nodes).
+    extern __shared__ __align__(16) uint8_t sel_smem[];
+    const size_t nb = heap_node_bytes(k);
+    // (each call inlined with its nodes' memory space known to the compiler)
+    if (nb + 8 * 4096 <= (size_t)p.smem_bytes) {
+      uint2* const nd = reinterpret_cast<uint2*>(sel_smem);
+      uint2* const list = reinterpret_cast<uint2*>(sel_smem + nb);
+      const int lcap = (int)((p.smem_bytes - nb) / 8);
+      if (largest) heap_select_block(Q, k, n, BeforeC<true>{}, nd, list, lcap, sh);
+      else heap_select_block(Q, k, n, BeforeC<false>{}, nd, list, lcap, sh);
+    } else {
+      uint2* const nd = reinterpret_cast<uint2*>(p.stops);
+      uint2* const list = reinterpret_cast<uint2*>(sel_smem);
+      const int lcap = p.smem_bytes / 8;
+      if (largest) heap_select_block(Q, k, n, BeforeC<true>{}, nd, list, lcap, sh);
+      else heap_select_block(Q, k, n, BeforeC<false>{}, nd, list, lcap, sh);
     }
   } else {
     const int nth = k - 1;
+    // Working copy: the queue in the workspace until the remaining range (with
+    // its stop table, 12 bytes an entry) fits this block's shared memory, then
+    // there (indices unchanged), copied back at the end.
+    extern __shared__ __align__(16) uint8_t sel_smem[];
+    Queue W = Q;
+    int* stops = p.stops;
+    int moved_first = 0, moved_last = 0;
     if (threadIdx.x == 0) {
       sh.first = 0;
       sh.last = n;
@@ -420,10 +542,24 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       const int first = sh.first, last = sh.last, done = sh.done, depth = sh.depth;
       __syncthreads();  // every thread has read the loop state before thread 0 updates it
       if (done || last - first <= 3) break;
+      if (moved_last == 0 && (size_t)(last - first) * 12 + 16 <= (size_t)p.smem_bytes) {
+        const int R = last - first;
+        int* qs = reinterpret_cast<int*>(sel_smem);
+        uint32_t* ks = reinterpret_cast<uint32_t*>(sel_smem + 4 * (size_t)R);
+        for (int i = threadIdx.x; i < R; i += kSelThreads) {
+          qs[i] = Q.q[first + i];
+          ks[i] = Q.qk[first + i];
+        }
+        W = Queue{qs - first, ks - first};
+        stops = reinterpret_cast<int*>(sel_smem + 8 * (size_t)R);
+        moved_first = first;
+        moved_last = last;
+        __syncthreads();
+      }
       if (depth == 0) {
         if (threadIdx.x == 0) {
-          heap_select_serial(Q, first, nth + 1, last, before);
-          Q.swap(first, nth);
+          heap_select_serial(W, first, nth + 1, last, before);
+          W.swap(first, nth);
           sh.done = 2;
         }
         break;
@@ -431,7 +567,7 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       if (threadIdx.x == 0) {
         sh.depth = depth - 1;
         const int a = first + 1, b = first + (last - first) / 2, c = last - 1;
-        const uint32_t ka = Q.qk[a], kb = Q.qk[b], kc = Q.qk[c];
+        const uint32_t ka = W.qk[a], kb = W.qk[b], kc = W.qk[c];
         int m;
         uint32_t km;
         if (before(ka, kb)) {
@@ -445,7 +581,7 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
         } else {
           m = b, km = kb;
         }
-        Q.swap(first, m);
+        W.swap(first, m);
         sh.pivot = km;
         sh.pairs = 0;
       }
@@ -455,8 +591,8 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       // Stop tables: at most (hi - lo) / 2 swaps, so left stops of rank <= H and
       // right stops of rank < H are all that is read; they share one region.
       const int H = (hi - lo) / 2;
-      int* const stop_l = p.stops;
-      int* const stop_r = p.stops + H + 1;
+      int* const stop_l = stops;
+      int* const stop_r = stops + H + 1;
       const Chunk rc = range_chunk(lo, hi, warp);
       // pass 1: left / right stops per warp piece
       uint32_t nl = 0, nr = 0;
@@ -465,7 +601,7 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int i = b + 32 * j + lane;
-          kk[j] = i < rc.end ? Q.qk[i] : 0u;
+          kk[j] = i < rc.end ? W.qk[i] : 0u;
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -490,7 +626,7 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int i = b + 32 * j + lane;
-          kk[j] = i < rc.end ? Q.qk[i] : 0u;
+          kk[j] = i < rc.end ? W.qk[i] : 0u;
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -514,7 +650,28 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       __syncthreads();
       const int pairs = sh.pairs;
       // pass 3: the swaps (disjoint slot pairs)
-      for (int m = threadIdx.x; m < pairs; m += kSelThreads) Q.swap(stop_l[m], stop_r[m]);
+      for (int m0 = threadIdx.x; m0 < pairs; m0 += 4 * kSelThreads) {  // four swaps in flight
+        int li[4], ri[4], a[4], b[4];
+        uint32_t ka[4], kb[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int m = m0 + u * kSelThreads;
+          li[u] = m < pairs ? stop_l[m] : -1;
+          ri[u] = m < pairs ? stop_r[m] : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (li[u] >= 0) {
+            a[u] = W.q[li[u]], b[u] = W.q[ri[u]];
+            ka[u] = W.qk[li[u]], kb[u] = W.qk[ri[u]];
+          }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (li[u] >= 0) {
+            W.q[li[u]] = b[u], W.q[ri[u]] = a[u];
+            W.qk[li[u]] = kb[u], W.qk[ri[u]] = ka[u];
+          }
+      }
       if (threadIdx.x == 0) {
         int cut = -1;
         if (pairs >= 1 && !(pairs < total_l && stop_l[pairs] < stop_r[pairs - 1])) cut = stop_r[pairs - 1];
@@ -531,7 +688,12 @@ __device__ void select_exact(const SelectParams& p, const SelState<SMEM>& st, co
       __syncthreads();
     }
     __syncthreads();
-    if (threadIdx.x == 0 && sh.done == 0) insertion_sort_serial(Q, sh.first, sh.last, before);
+    if (threadIdx.x == 0 && sh.done == 0) insertion_sort_serial(W, sh.first, sh.last, before);
+    __syncthreads();
+    for (int i = moved_first + (int)threadIdx.x; i < moved_last; i += kSelThreads) {
+      Q.q[i] = W.q[i];
+      Q.qk[i] = W.qk[i];
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < k; i += kSelThreads) st.tier[Q.q[i]] = mark;
@@ -706,6 +868,9 @@ __device__ void exact_on_block0(const SelectParams& p, const SelState<SMEM>& st,
   if (cg::this_cluster().block_rank() == 0) {
     const SelState<false> all{nullptr, p.tier, 0, p.T};
     select_exact<false>(p, all, src ? src : p.scores, k, largest, mark, sh);
+    if (SMEM && p.scores)  // the exact path used the cached keys' shared memory as scratch
+      for (int t = st.base + (int)threadIdx.x; t < st.end; t += kSelThreads)
+        st.keys[t - st.base] = order_key(p.scores[t]);
   }
   cluster_sync();
   if (SMEM) {
@@ -941,19 +1106,14 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
   p.idx_ret = idx_ret;
   p.idx_std = idx_std;
   p.idx_cold = idx_cold;
-  const int per = select_block_tokens(T);
-  size_t sm = per <= kSelSmemTokens ? (size_t)per * 5 : 0;
-  // room for the exact path's heap (a heap select needs k * 64 <= T)
-  int cap = 0;
-  for (const int k : {pol.keep_protect, pol.keep_outlier, pol.keep_cold})
-    if (k > 0 && (int64_t)k * 64 <= T) cap = k > cap ? k : cap;
-  p.heap_cap = 0;
-  p.heap_offset = (int)((sm + 15) & ~(size_t)15);
-  const size_t heap_bytes = heap_node_bytes(cap);
-  if (cap > 0 && p.heap_offset + heap_bytes + sizeof(SelShared) <= kSelSmemLimit) {
-    p.heap_cap = cap;
-    sm = p.heap_offset + heap_bytes;
-  }
+  // Nearly all the shared memory a block may have: the blocks' own tokens (at
+  // most kSelSmemTokens * 5 bytes) and, in block 0, the exact path's scratch.
+  // The static part is rounded up to 1 KB (the compiler pads it, and the
+  // dynamic part starts aligned after it).  One block per SM either way.
+  constexpr size_t kStatic = (sizeof(SelShared) + 1023) & ~(size_t)1023;
+  constexpr size_t sm = kSelSmemLimit - kStatic;
+  static_assert(sm >= (size_t)kSelSmemTokens * 5, "select smem");
+  p.smem_bytes = (int)sm;
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
   select_kernel<<<kSelCluster, kSelThreads, sm, st>>>(p);
