@@ -9,8 +9,9 @@
 // dequantized cache's, and writes, per query, the tile's softmax partials: the
 // largest logit m, the sum l of exp(logit - m) and o = sum exp(logit - m) v.  A
 // second kernel merges the partials of a slice's tiles (rescaled to the overall
-// largest logit) into the output.  Only the summation order differs from the
-// reference's fp32 matmul / softmax / matmul.
+// largest logit) into the output, in two stages when a slice has many tiles.
+// Only the summation order differs from the reference's fp32 matmul / softmax /
+// matmul.
 #pragma once
 
 #include "dequantize.cuh"
@@ -25,15 +26,19 @@ struct AttnParams {
   int Q;
   float inv_sqrt_d;    // 1 / sqrt(D)
   float* part;         // [S, tiles_slice, Q, D + 2]: m, l, o[D]
+  float* part2;        // [S, merge groups, Q, D + 2]: the first merge stage's partials
   float* out;          // [S, Q, D] fp32
 };
 
+// Shared memory of a tile block: the decoded key and value tiles, the queries
+// (Q x D fp32, 16-byte aligned size), then the tile's probabilities and 16
+// floats of reductions.
 template <typename T, int D>
 struct AGeom {
   using G = DGeom<T, D>;
-  static constexpr size_t kTile = G::kTile;                       // one decoded [64][D] tile
-  static constexpr size_t kQ = (size_t)kAttnMaxQueries * D * 4;   // queries
-  static constexpr size_t kBytes = 2 * kTile + kQ + kDTile * 4 + 64 + kDTile * 4;
+  static constexpr size_t kTile = G::kTile;  // one decoded [64][D] tile
+  static __host__ __device__ size_t q_bytes(int Q) { return ((size_t)Q * D * 4 + 15) & ~(size_t)15; }
+  static __host__ __device__ size_t bytes(int Q) { return 2 * kTile + q_bytes(Q) + kDTile * 4 + 64; }
 };
 
 // Retained rows j0 .. j0 + rows of one tensor into a [64][D] tile (16-byte vectors).
@@ -50,7 +55,7 @@ __device__ __forceinline__ void load_retained_rows(const void* ret, int R, int s
 }
 
 template <typename T, int D, bool VROT>
-__global__ void __launch_bounds__(kDThreads, 4) attend_tile_kernel(const __grid_constant__ AttnParams a) {
+__global__ void __launch_bounds__(kDThreads, 6) attend_tile_kernel(const __grid_constant__ AttnParams a) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = DGeom<T, D>;
   using A = AGeom<T, D>;
@@ -58,7 +63,7 @@ __global__ void __launch_bounds__(kDThreads, 4) attend_tile_kernel(const __grid_
   uint8_t* tk = smem;
   uint8_t* tv = smem + A::kTile;
   float* qs = reinterpret_cast<float*>(smem + 2 * A::kTile);
-  float* prob = reinterpret_cast<float*>(smem + 2 * A::kTile + A::kQ);
+  float* prob = reinterpret_cast<float*>(smem + 2 * A::kTile + A::q_bytes(a.Q));
   float* red = prob + kDTile;  // 16 floats of reductions
   const DTileRef tr = dtile_ref(p, blockIdx.x);
   const int s = tr.s;
@@ -129,12 +134,16 @@ __global__ void __launch_bounds__(kDThreads, 4) attend_tile_kernel(const __grid_
   }
 }
 
-// Merge the tiles' partials of one (slice, query), one block of 256 threads:
-// the largest logit over the tiles, each tile's weight exp(m_j - M) (kept in
-// shared memory), the weighted sum of the l_j, and the weighted sum of the o_j
-// with the tiles split over the block's two halves (128 channels each).
+// Merge softmax partials (m, l, o[D]) in groups: one block of 256 threads per
+// (slice, query, group of entries): the largest logit M over the group, each
+// entry's weight exp(m_j - M) (kept in shared memory), L = sum of the weighted
+// l_j and o = sum of the weighted o_j, with the entries split over the block's
+// two halves (128 channels each).  FINAL (one group per slice): writes o / L;
+// otherwise writes the group's own partial (M, L, o).  Partials are laid out
+// [S][n][Q][D + 2].
 constexpr int kCombineThreads = 256;
-constexpr int kCombineSmemTiles = 8192;  // weights kept in shared memory up to this many tiles
+constexpr int kCombineSmemTiles = 8192;  // weights kept in shared memory up to this many entries
+constexpr int kMergeGroup = 16;          // entries per block of the first merge stage
 
 __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -151,15 +160,18 @@ __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) 
   return r;
 }
 
-__global__ void __launch_bounds__(kCombineThreads) attend_combine_kernel(const __grid_constant__ AttnParams a) {
+template <bool FINAL>
+__global__ void __launch_bounds__(kCombineThreads) attend_merge_kernel(const float* in, int n_in, int group, int Q,
+                                                                         int D, float* out) {
   __shared__ float wts[kCombineSmemTiles];
   __shared__ float red[kCombineThreads / 32];
   __shared__ float half_o[2][128];
-  const int sq = blockIdx.x;  // slice * Q + query
-  const int s = sq / a.Q, qi = sq - s * a.Q;
-  const int D = a.d.D, n = a.d.tiles_slice;
-  const float* part = a.part + (int64_t)s * n * a.Q * (D + 2) + qi * (D + 2);
-  const int64_t stride = (int64_t)a.Q * (D + 2);
+  const int ng = (n_in + group - 1) / group;
+  const int sq = blockIdx.x / ng, g = blockIdx.x - sq * ng;  // (slice * Q + query, group)
+  const int s = sq / Q, qi = sq - s * Q;
+  const int j0 = g * group, n = min(n_in, j0 + group) - j0;
+  const int64_t stride = (int64_t)Q * (D + 2);
+  const float* part = in + ((int64_t)s * n_in + j0) * stride + (int64_t)qi * (D + 2);
   float m = -INFINITY;
   for (int j = threadIdx.x; j < n; j += kCombineThreads) m = fmaxf(m, part[j * stride]);
   const float M = block_reduce(m, red, true);
@@ -181,19 +193,44 @@ __global__ void __launch_bounds__(kCombineThreads) attend_combine_kernel(const _
   }
   half_o[h][c] = o;
   __syncthreads();
-  if (h == 0 && c < D) a.out[(int64_t)sq * D + c] = (half_o[0][c] + half_o[1][c]) / L;
+  if (h == 0 && c < D) {
+    const float sum = half_o[0][c] + half_o[1][c];
+    if constexpr (FINAL) {
+      out[(int64_t)sq * D + c] = sum / L;
+    } else {
+      float* dst = out + ((int64_t)s * ng + g) * stride + (int64_t)qi * (D + 2);
+      if (c == 0) {
+        dst[0] = M;
+        dst[1] = L;
+      }
+      dst[2 + c] = sum;
+    }
+  }
+}
+
+// Entries of the first merge stage's output per slice (0: one stage).
+__host__ __device__ inline int merge_groups(int tiles_slice) {
+  return tiles_slice > 2 * kMergeGroup ? (tiles_slice + kMergeGroup - 1) / kMergeGroup : 0;
 }
 
 template <typename T, int D>
 static cudaError_t launch_attention_t(const AttnParams& a, cudaStream_t st) {
-  const size_t sm = AGeom<T, D>::kBytes;
+  const size_t sm = AGeom<T, D>::bytes(a.Q);
   const bool vrot = (a.d.tiles[1] && a.d.t[GKV_STD_V].rotation) || (a.d.tiles[2] && a.d.t[GKV_COLD_V].rotation);
   auto kern = vrot ? attend_tile_kernel<T, D, true> : attend_tile_kernel<T, D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
   kern<<<(unsigned)((int64_t)a.d.S * a.d.tiles_slice), kDThreads, sm, st>>>(a);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  attend_combine_kernel<<<(unsigned)(a.d.S * a.Q), kCombineThreads, 0, st>>>(a);
+  const int n = a.d.tiles_slice, ng = merge_groups(n);
+  if (ng > 0) {  // groups of kMergeGroup tiles, then their ng partials
+    attend_merge_kernel<false><<<(unsigned)((int64_t)a.d.S * a.Q * ng), kCombineThreads, 0, st>>>(
+        a.part, n, kMergeGroup, a.Q, D, a.part2);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    attend_merge_kernel<true><<<(unsigned)(a.d.S * a.Q), kCombineThreads, 0, st>>>(a.part2, ng, ng, a.Q, D, a.out);
+  } else {
+    attend_merge_kernel<true><<<(unsigned)(a.d.S * a.Q), kCombineThreads, 0, st>>>(a.part, n, n, a.Q, D, a.out);
+  }
   return cudaGetLastError();
 }
 

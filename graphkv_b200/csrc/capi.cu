@@ -461,12 +461,19 @@ int resolve_attention(const gkv_plan* plan, int32_t n_slices, int32_t n_queries,
 
 }  // namespace
 
+// Softmax partials of every tile, then those of the first merge stage's groups.
+static size_t attention_workspace(int n_slices, int tiles_slice, int n_queries, int head_dim) {
+  const size_t entry = (size_t)n_queries * (head_dim + 2) * sizeof(float);
+  return (size_t)n_slices * (tiles_slice + merge_groups(tiles_slice)) * entry;
+}
+
 size_t gkv_attention_workspace_bytes(const gkv_plan* plan, int32_t n_slices, int32_t n_queries) {
   Resolved r;
   if (resolve_attention(plan, n_slices, n_queries, r) != GKV_OK) return 0;
   int tiles[3];
   tile_counts(r, tiles);
-  return (size_t)n_slices * (tiles[0] + tiles[1] + tiles[2]) * n_queries * (plan->head_dim + 2) * sizeof(float);
+  const int n = tiles[0] + tiles[1] + tiles[2];
+  return attention_workspace(n_slices, n, n_queries, plan->head_dim);
 }
 
 int32_t gkv_attention(const gkv_plan* plan, int32_t n_slices, const float* queries, int32_t n_queries, float* out,
@@ -498,13 +505,14 @@ int32_t gkv_attention(const gkv_plan* plan, int32_t n_slices, const float* queri
   tile_counts(r, q.tiles);
   q.tiles_slice = q.tiles[0] + q.tiles[1] + q.tiles[2];
   q.tile_div = make_fastdiv((uint32_t)(q.tiles_slice > 0 ? q.tiles_slice : 1));
-  const size_t need = (size_t)n_slices * q.tiles_slice * n_queries * (p.head_dim + 2) * sizeof(float);
+  const size_t need = attention_workspace(n_slices, q.tiles_slice, n_queries, p.head_dim);
   if (!workspace || workspace_bytes < need)
     return fail(GKV_ERR_WORKSPACE, "attention workspace too small: need " + std::to_string(need) + " bytes");
   a.q = queries;
   a.Q = n_queries;
   a.inv_sqrt_d = (float)(1.0 / std::sqrt((double)p.head_dim));
   a.part = static_cast<float*>(workspace);
+  a.part2 = a.part + (size_t)n_slices * q.tiles_slice * n_queries * (p.head_dim + 2);
   a.out = out;
   cudaError_t e = launch_attention(a, p.dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? GKV_OK : cuda_fail(e, "attention kernels");

@@ -224,7 +224,7 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
  * cache's, only the fp32 summation order differs.  Supported: head_dim 64 or
  * 128, every tier on the tile path, keys grouped along tokens (not rotated),
  * values along channels; otherwise GKV_ERR_UNSUPPORTED.  At most 16 queries.
- * workspace: gkv_attention_workspace_bytes(...) bytes (per-tile partials). */
+ * workspace: gkv_attention_workspace_bytes(...) bytes (softmax partials per tile and per merge group). */
 size_t gkv_attention_workspace_bytes(const gkv_plan* plan, int32_t n_slices, int32_t n_queries);
 int32_t gkv_attention(const gkv_plan* plan, int32_t n_slices, const float* queries, int32_t n_queries, float* out,
                       void* workspace, size_t workspace_bytes, gkv_stream_t stream);
