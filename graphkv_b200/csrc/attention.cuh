@@ -31,14 +31,14 @@ struct AttnParams {
 };
 
 // Shared memory of a tile block: the decoded key and value tiles, the queries
-// (Q x D fp32, 16-byte aligned size), then the tile's probabilities and 16
-// floats of reductions.
+// (Q x D fp32, 16-byte aligned size), then the tile's probabilities, 16 floats
+// of reductions and D floats of partial value sums.
 template <typename T, int D>
 struct AGeom {
   using G = DGeom<T, D>;
   static constexpr size_t kTile = G::kTile;  // one decoded [64][D] tile
   static __host__ __device__ size_t q_bytes(int Q) { return ((size_t)Q * D * 4 + 15) & ~(size_t)15; }
-  static __host__ __device__ size_t bytes(int Q) { return 2 * kTile + q_bytes(Q) + kDTile * 4 + 64; }
+  static __host__ __device__ size_t bytes(int Q) { return 2 * kTile + q_bytes(Q) + kDTile * 4 + 64 + D * 4; }
 };
 
 // Retained rows j0 .. j0 + rows of one tensor into a [64][D] tile (16-byte vectors).
@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(kDThreads, 6) attend_tile_kernel(const __grid_
   uint8_t* tv = smem + A::kTile;
   float* qs = reinterpret_cast<float*>(smem + 2 * A::kTile);
   float* prob = reinterpret_cast<float*>(smem + 2 * A::kTile + A::q_bytes(a.Q));
-  float* red = prob + kDTile;  // 16 floats of reductions
+  float* red = prob + kDTile;  // 16 floats of reductions, then D floats of partial sums
   const DTileRef tr = dtile_ref(p, blockIdx.x);
   const int s = tr.s;
   const int j0 = tr.k * kDTile;
@@ -100,9 +100,28 @@ __global__ void __launch_bounds__(kDThreads, 6) attend_tile_kernel(const __grid_
     const float* q = qs + qi * D;
     // logit of row r: q . k_r / sqrt(D)
     float dot = 0.f;
-    const T* krow = reinterpret_cast<const T*>(tk + r * G::kPitchB) + half * HD;
+    if constexpr (sizeof(T) == 2) {  // 8 elements per 16-byte load
+      using W = Word16<T>;
+      const uint4* krow = reinterpret_cast<const uint4*>(tk + r * G::kPitchB + half * HD * 2);
+      const float4* qh = reinterpret_cast<const float4*>(q + half * HD);
+#pragma unroll 4
+      for (int c8 = 0; c8 < HD / 8; ++c8) {
+        const uint4 w = krow[c8];
+        const float4 qa = qh[2 * c8], qb = qh[2 * c8 + 1];
+        dot = __fmaf_rn(qa.x, W::lo(w.x), dot);
+        dot = __fmaf_rn(qa.y, W::hi(w.x), dot);
+        dot = __fmaf_rn(qa.z, W::lo(w.y), dot);
+        dot = __fmaf_rn(qa.w, W::hi(w.y), dot);
+        dot = __fmaf_rn(qb.x, W::lo(w.z), dot);
+        dot = __fmaf_rn(qb.y, W::hi(w.z), dot);
+        dot = __fmaf_rn(qb.z, W::lo(w.w), dot);
+        dot = __fmaf_rn(qb.w, W::hi(w.w), dot);
+      }
+    } else {
+      const T* krow = reinterpret_cast<const T*>(tk + r * G::kPitchB) + half * HD;
 #pragma unroll 8
-    for (int c = 0; c < HD; ++c) dot = __fmaf_rn(q[half * HD + c], Elem<T>::to_f32(krow[c]), dot);
+      for (int c = 0; c < HD; ++c) dot = __fmaf_rn(q[half * HD + c], Elem<T>::to_f32(krow[c]), dot);
+    }
     dot += __shfl_xor_sync(kFull, dot, 1);
     const float logit = r < rows ? dot * a.inv_sqrt_d : -INFINITY;
     float m = logit;
@@ -120,11 +139,37 @@ __global__ void __launch_bounds__(kDThreads, 6) attend_tile_kernel(const __grid_
     if (lane == 0) red[4 + warp] = l;
     __syncthreads();
     // o[c] = sum_r prob[r] v_r[c]
-    for (int c = threadIdx.x; c < D; c += kDThreads) {
-      float acc = 0.f;
-      for (int rr = 0; rr < rows; ++rr)
-        acc = __fmaf_rn(prob[rr], Elem<T>::to_f32(reinterpret_cast<const T*>(tv + rr * G::kPitchB)[c]), acc);
-      part[qi * (D + 2) + 2 + c] = acc;
+    if constexpr (sizeof(T) == 2 && D == 128) {
+      // thread: channels 2p, 2p + 1 over rows 32h .. 32h + 31 (p = tid % 64,
+      // h = tid / 64); the two halves of the rows are added through shared memory
+      using W = Word16<T>;
+      const int pc = threadIdx.x & 63, h = threadIdx.x >> 6;
+      float a0 = 0.f, a1 = 0.f;
+      const int r0 = 32 * h, r1 = min(rows, r0 + 32);
+#pragma unroll 4
+      for (int rr = r0; rr < r1; ++rr) {
+        const float pr = prob[rr];
+        const uint32_t w = reinterpret_cast<const uint32_t*>(tv + rr * G::kPitchB)[pc];
+        a0 = __fmaf_rn(pr, W::lo(w), a0);
+        a1 = __fmaf_rn(pr, W::hi(w), a1);
+      }
+      float* oh = red + 16;  // D floats
+      if (h == 1) {
+        oh[2 * pc] = a0;
+        oh[2 * pc + 1] = a1;
+      }
+      __syncthreads();
+      if (h == 0) {
+        part[qi * (D + 2) + 2 + 2 * pc] = a0 + oh[2 * pc];
+        part[qi * (D + 2) + 3 + 2 * pc] = a1 + oh[2 * pc + 1];
+      }
+    } else {
+      for (int c = threadIdx.x; c < D; c += kDThreads) {
+        float acc = 0.f;
+        for (int rr = 0; rr < rows; ++rr)
+          acc = __fmaf_rn(prob[rr], Elem<T>::to_f32(reinterpret_cast<const T*>(tv + rr * G::kPitchB)[c]), acc);
+        part[qi * (D + 2) + 2 + c] = acc;
+      }
     }
     if (threadIdx.x == 0) {
       part[qi * (D + 2)] = m;

@@ -152,8 +152,8 @@ def test_quantize_hf_cache_takes_the_pipeline_for_pinned_host_caches(monkeypatch
 def test_tensors_on_another_gpu_than_the_current_one():
     """Every call runs on the GPU that holds its tensors, whichever GPU is
     current: cache on cuda:1 with cuda:0 current gives the same bytes as on cuda:0."""
-    cache0 = _small_cache(T=4096, layers=2)
-    scores = torch.exp(torch.randn(4, 4096, generator=torch.Generator().manual_seed(2)))
+    cache0 = _small_cache(T=16384, layers=2)  # long enough for a cold tier
+    scores = torch.exp(torch.randn(4, 16384, generator=torch.Generator().manual_seed(2)))
     torch.cuda.set_device(0)
     ref = g.quantize_hf_cache(cache0, "graphkv", importance_scores=scores.cuda(0), output="compressed")
     cache1 = tuple((k.to("cuda:1"), v.to("cuda:1")) for k, v in cache0)
@@ -163,6 +163,7 @@ def test_tensors_on_another_gpu_than_the_current_one():
         assert lb.compressed_keys.q.device == torch.device("cuda:1")
         assert torch.equal(la.retained_indices.cpu(), lb.retained_indices.cpu())
         assert torch.equal(la.compressed_keys.q.cpu(), lb.compressed_keys.q.cpu())
+        assert la.low_priority_compressed_values is not None
         assert torch.equal(la.low_priority_compressed_values.q.cpu(), lb.low_priority_compressed_values.q.cpu())
     for (ka, va), (kb, vb) in zip(ref.dequantize(), other.dequantize()):
         assert kb.device == torch.device("cuda:1")
