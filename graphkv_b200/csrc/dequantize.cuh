@@ -441,7 +441,7 @@ __device__ __forceinline__ void chan_decode_any(const DequantParams& p, const Te
 // the general path); a launch covers the tiers that use its variant, and the
 // retained rows when `copy_retained`.
 template <typename T, int D, int AXIS, bool ROT>
-__global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 10)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 6 : 10)))
+__global__ void __launch_bounds__(kDThreads, sizeof(T) == 4 ? (AXIS == GKV_AXIS_TOKEN ? 7 : (ROT ? 5 : 10)) : (AXIS == GKV_AXIS_TOKEN ? 8 : (ROT ? 7 : 10)))
     dequantize_tile_kernel(const __grid_constant__ DequantParams p, int tensor, int copy_retained) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = DGeom<T, D>;

@@ -19,6 +19,8 @@
 // (positions and keys) and the partition stop tables (int32).
 #pragma once
 
+#include <algorithm>
+
 #include <cooperative_groups.h>
 
 #include "gkv_common.cuh"
@@ -32,6 +34,8 @@ constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSelCluster = 8;         // blocks of the selection cluster
 constexpr int kSelSmemTokens = 40960;  // tokens per block whose keys (4 B) and tier (1 B) fit in shared memory
 constexpr size_t kSelSmemLimit = 227 * 1024;  // shared memory of one block (static + dynamic)
+constexpr size_t kSelExactSmem = 48 * 1024;   // least dynamic shared memory (the exact path's scratch)
+constexpr int kSelWindow = 4096;              // heap select: queue entries filtered per window
 enum : uint8_t { kCand = 0, kRet = 1, kCold = 2 };
 
 struct SelectParams {
@@ -291,7 +295,7 @@ __device__ __forceinline__ uint32_t heap_replay(uint2* nd, int len, const uint2*
 
 // __heap_select(0, k, n) over the queue by the whole block.  The heap's nodes
 // live in `nd` (at least k + 8 entries, 16-byte aligned); the queue after the
-// first k entries is taken in windows of at most `lcap` entries: the block
+// first k entries is taken in windows of at most `lcap` (and kSelWindow) entries: the block
 // copies the entries of a window that compare before the current top (the top
 // only moves on, so no other entry of the window can replace it) into `list`,
 // in queue order, and warp 0 replays them.  The first k queue entries receive
@@ -309,6 +313,9 @@ __device__ __forceinline__ void heap_select_block(const Queue& Q, int k, int n, 
     if (lane == 0) sh.pivot = nd[1].x;
   }
   __syncthreads();
+  // Short windows keep the filter's top close to the replay's, so fewer entries
+  // reach the list.
+  lcap = min(lcap, kSelWindow);
   for (int lo = k; lo < n; lo += lcap) {
     const int hi = min(n, lo + lcap);
     const uint32_t top = sh.pivot;
@@ -1106,13 +1113,13 @@ cudaError_t launch_select(const float* scores, const float* outlier, const gkv_s
   p.idx_ret = idx_ret;
   p.idx_std = idx_std;
   p.idx_cold = idx_cold;
-  // Nearly all the shared memory a block may have: the blocks' own tokens (at
-  // most kSelSmemTokens * 5 bytes) and, in block 0, the exact path's scratch.
-  // The static part is rounded up to 1 KB (the compiler pads it, and the
-  // dynamic part starts aligned after it).  One block per SM either way.
+  // The blocks' own tokens (kSelSmemTokens * 5 bytes at most, below the limit
+  // with the static part rounded up to 1 KB), and at least kSelExactSmem for the
+  // exact path's scratch in block 0 (its tokens' space included).
   constexpr size_t kStatic = (sizeof(SelShared) + 1023) & ~(size_t)1023;
-  constexpr size_t sm = kSelSmemLimit - kStatic;
-  static_assert(sm >= (size_t)kSelSmemTokens * 5, "select smem");
+  static_assert(kSelSmemLimit - kStatic >= (size_t)kSelSmemTokens * 5, "select smem");
+  const int per = select_block_tokens(T);
+  const size_t sm = std::max(per <= kSelSmemTokens ? (size_t)per * 5 : (size_t)0, kSelExactSmem);
   p.smem_bytes = (int)sm;
   cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
