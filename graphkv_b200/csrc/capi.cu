@@ -3,6 +3,7 @@
 // kernels, workspace layout, and launches.  Nothing here allocates device memory.
 // The library is one translation unit: the kernel sources are included below.
 #include <atomic>
+#include <mutex>
 #include <cmath>
 #include <cstdio>
 #include <string>
@@ -56,6 +57,66 @@ bool tile_instantiated(int esize, int D, int TT) {
 }
 
 const int kTierOf[4] = {1, 1, 2, 2};
+
+// A second stream per device on which the rotated value tiles are quantized and
+// dequantized beside the key and plain value tiles of the caller's stream: the
+// rotated kernels are bound by instruction issue and the others by memory, so
+// they share the SMs well (measured on the 32k cache: quantize 0.539 -> 0.522 ms,
+// dequant 0.518 -> 0.509 ms).  The helper stream starts after the caller's
+// earlier work (fork event) and the caller's stream continues after the
+// helper's kernels (join event).  The lock keeps one call's fork ... join
+// sequence together when host threads overlap, so the helper holds only that
+// call's kernels between its two events.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mutex;
+SideStream g_side[64];
+constexpr int64_t kSideMinTiles = 8192;  // calls with fewer tiles stay on one stream
+
+class SideStreamCall {
+ public:
+  // use: false runs everything on `st` (small calls, where the two event waits
+  // cost more than the overlap gains).
+  SideStreamCall(cudaStream_t st, bool use) : st_(st), lock_(g_side_mutex, std::defer_lock) {
+    if (!use) return;
+    lock_.lock();
+    int dev = 0;
+    if ((err_ = cudaGetDevice(&dev)) != cudaSuccess) return;
+    if (dev < 0 || dev >= 64) {
+      err_ = cudaErrorInvalidDevice;
+      return;
+    }
+    SideStream& ss = g_side[dev];
+    if (!ss.s) {
+      if ((err_ = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking)) != cudaSuccess) return;
+      if ((err_ = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming)) != cudaSuccess) return;
+      if ((err_ = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming)) != cudaSuccess) return;
+    }
+    if ((err_ = cudaEventRecord(ss.fork, st)) != cudaSuccess) return;
+    if ((err_ = cudaStreamWaitEvent(ss.s, ss.fork, 0)) != cudaSuccess) return;
+    side_ = &ss;
+  }
+  cudaStream_t side() const { return side_ ? side_->s : st_; }
+  cudaError_t error() const { return err_; }
+  // The caller's stream waits for the helper's kernels (also after a failed launch).
+  cudaError_t join() {
+    if (!side_ || joined_) return cudaSuccess;
+    joined_ = true;
+    cudaError_t e = cudaEventRecord(side_->join, side_->s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st_, side_->join, 0);
+    return e;
+  }
+  ~SideStreamCall() { join(); }
+
+ private:
+  cudaStream_t st_;
+  std::unique_lock<std::mutex> lock_;
+  SideStream* side_ = nullptr;
+  cudaError_t err_ = cudaSuccess;
+  bool joined_ = false;
+};
 
 struct Resolved {
   TensorDesc t[4];
@@ -355,8 +416,14 @@ int32_t gkv_quantize(const gkv_plan* plan, const gkv_layer_in* layers, int32_t n
     q.layer_div = uniform ? make_fastdiv((uint32_t)(p.batch * q.layers[0].heads)) : FastDiv{0u, 0u, 0, 0};
     q.head_div = make_fastdiv((uint32_t)q.layers[0].heads);
     cudaError_t e = cudaSuccess;
-    if (q.tiles_slice > 0 && (e = launch_quantize_tiles(q, p.dtype, s)) != cudaSuccess)
-      return cuda_fail(e, "quantize tile kernel");
+    if (q.tiles_slice > 0) {
+      SideStreamCall side(s, (int64_t)q.S * q.tiles_slice >= kSideMinTiles);
+      if ((e = side.error()) != cudaSuccess) return cuda_fail(e, "side stream");
+      e = launch_quantize_tiles(q, p.dtype, s, side.side());
+      const cudaError_t ej = side.join();
+      if (e != cudaSuccess) return cuda_fail(e, "quantize tile kernel");
+      if (ej != cudaSuccess) return cuda_fail(ej, "side stream join");
+    }
     if (!r.fast[0] && r.n[0] > 0 && (e = launch_retained_general(q, p.dtype, s)) != cudaSuccess)
       return cuda_fail(e, "retained copy kernel");
     for (int i = 0; i < 4; ++i) {
@@ -416,8 +483,14 @@ int32_t gkv_dequantize(const gkv_plan* plan, int32_t n_slices, void* k_out, void
   q.had_fused = (p.head_dim == 64 || p.head_dim == 128) &&
                 p.hadamard_divisor == (float)std::sqrt((double)p.head_dim);
   cudaError_t e;
-  if (q.tiles_slice > 0 && (e = launch_dequantize_tiles(q, p.dtype, s)) != cudaSuccess)
-    return cuda_fail(e, "dequantize tile kernel");
+  if (q.tiles_slice > 0) {
+    SideStreamCall side(s, (int64_t)q.S * q.tiles_slice >= kSideMinTiles);
+    if ((e = side.error()) != cudaSuccess) return cuda_fail(e, "side stream");
+    e = launch_dequantize_tiles(q, p.dtype, s, side.side());
+    const cudaError_t ej = side.join();
+    if (e != cudaSuccess) return cuda_fail(e, "dequantize tile kernel");
+    if (ej != cudaSuccess) return cuda_fail(ej, "side stream join");
+  }
   if (!r.fast[0] && r.n[0] > 0 && (e = launch_dequantize_retained_general(q, p.dtype, s)) != cudaSuccess)
     return cuda_fail(e, "retained scatter kernel");
   for (int tier = 1; tier <= 2; ++tier) {
@@ -530,7 +603,6 @@ int32_t gkv_attention(const gkv_plan* plan, int32_t n_slices, const float* queri
 // own pool, or a latency-critical path where cudaMalloc's implicit device-wide
 // synchronisation is not acceptable).
 // ---------------------------------------------------------------------------
-#include <mutex>
 
 namespace gkv {
 namespace {

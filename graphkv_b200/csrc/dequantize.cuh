@@ -593,7 +593,7 @@ static cudaError_t launch_dq_variant(const DequantParams& p, int tensor, bool re
 }
 
 template <typename T, int D>
-static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st) {
+static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st, cudaStream_t st_rot) {
   if ((int64_t)p.S * p.tiles_slice == 0) return cudaSuccess;
   for (int tensor = 0; tensor < 2; ++tensor) {
     const int v1 = p.tiles[1] ? tier_variant(p.t[GKV_STD_K + tensor]) : -1;
@@ -607,7 +607,7 @@ static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st) {
       switch (v) {
         case 0: e = launch_dq_variant<T, D, GKV_AXIS_TOKEN, false>(p, tensor, ret_here, standard, cold, st); break;
         case 2: e = launch_dq_variant<T, D, GKV_AXIS_CHANNEL, false>(p, tensor, ret_here, standard, cold, st); break;
-        case 3: e = launch_dq_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st); break;
+        case 3: e = launch_dq_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st_rot); break;
         default: e = cudaErrorInvalidConfiguration; break;  // rotated token axis: general path only
       }
       if (e != cudaSuccess) return e;
@@ -618,16 +618,18 @@ static cudaError_t launch_dq_tile(const DequantParams& p, cudaStream_t st) {
 }
 
 template <typename T>
-static cudaError_t launch_dq_tile_d(const DequantParams& p, cudaStream_t st) {
-  if (p.D == 64) return launch_dq_tile<T, 64>(p, st);
-  if (p.D == 128) return launch_dq_tile<T, 128>(p, st);
+static cudaError_t launch_dq_tile_d(const DequantParams& p, cudaStream_t st, cudaStream_t st_rot) {
+  if (p.D == 64) return launch_dq_tile<T, 64>(p, st, st_rot);
+  if (p.D == 128) return launch_dq_tile<T, 128>(p, st, st_rot);
   return cudaErrorInvalidConfiguration;
 }
 
-cudaError_t launch_dequantize_tiles(const DequantParams& p, int dtype, cudaStream_t st) {
-  if (dtype == GKV_BF16) return launch_dq_tile_d<__nv_bfloat16>(p, st);
-  if (dtype == GKV_F16) return launch_dq_tile_d<__half>(p, st);
-  return launch_dq_tile_d<float>(p, st);
+// Rotated-tier launches on st_rot, the others on st (the caller orders the two
+// streams).
+cudaError_t launch_dequantize_tiles(const DequantParams& p, int dtype, cudaStream_t st, cudaStream_t st_rot) {
+  if (dtype == GKV_BF16) return launch_dq_tile_d<__nv_bfloat16>(p, st, st_rot);
+  if (dtype == GKV_F16) return launch_dq_tile_d<__half>(p, st, st_rot);
+  return launch_dq_tile_d<float>(p, st, st_rot);
 }
 
 template <typename T>

@@ -975,7 +975,7 @@ static cudaError_t launch_variant(const QuantParams& p, int tensor, bool retaine
 }
 
 template <typename T, int D>
-static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
+static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st, cudaStream_t st_rot) {
   if ((int64_t)p.S * p.tiles_slice == 0) return cudaSuccess;
   for (int tensor = 0; tensor < 2; ++tensor) {
     const int v1 = p.tiles[1] ? tier_variant(p.t[GKV_STD_K + tensor]) : -1;
@@ -995,11 +995,11 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
                             (!cold || int2_rot_tensor(p.t[GKV_COLD_K + tensor], sizeof(T), D));
           if constexpr (sizeof(T) == 2 && D == 128) {
             if (int2) {
-              e = launch_variant<T, D, GKV_AXIS_CHANNEL, true, true>(p, tensor, ret_here, standard, cold, st);
+              e = launch_variant<T, D, GKV_AXIS_CHANNEL, true, true>(p, tensor, ret_here, standard, cold, st_rot);
               break;
             }
           }
-          e = launch_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st);
+          e = launch_variant<T, D, GKV_AXIS_CHANNEL, true>(p, tensor, ret_here, standard, cold, st_rot);
           break;
         }
       }
@@ -1011,16 +1011,18 @@ static cudaError_t launch_tile(const QuantParams& p, cudaStream_t st) {
 }
 
 template <typename T>
-static cudaError_t launch_tile_d(const QuantParams& p, cudaStream_t st) {
-  if (p.D == 64) return launch_tile<T, 64>(p, st);
-  if (p.D == 128) return launch_tile<T, 128>(p, st);
+static cudaError_t launch_tile_d(const QuantParams& p, cudaStream_t st, cudaStream_t st_rot) {
+  if (p.D == 64) return launch_tile<T, 64>(p, st, st_rot);
+  if (p.D == 128) return launch_tile<T, 128>(p, st, st_rot);
   return cudaErrorInvalidConfiguration;
 }
 
-cudaError_t launch_quantize_tiles(const QuantParams& p, int dtype, cudaStream_t st) {
-  if (dtype == GKV_BF16) return launch_tile_d<__nv_bfloat16>(p, st);
-  if (dtype == GKV_F16) return launch_tile_d<__half>(p, st);
-  return launch_tile_d<float>(p, st);
+// Rotated-tier launches on st_rot, the others on st (the caller orders the two
+// streams).
+cudaError_t launch_quantize_tiles(const QuantParams& p, int dtype, cudaStream_t st, cudaStream_t st_rot) {
+  if (dtype == GKV_BF16) return launch_tile_d<__nv_bfloat16>(p, st, st_rot);
+  if (dtype == GKV_F16) return launch_tile_d<__half>(p, st, st_rot);
+  return launch_tile_d<float>(p, st, st_rot);
 }
 
 template <typename T>

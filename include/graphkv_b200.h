@@ -9,8 +9,12 @@
  * Conventions
  *  - All pointers are device pointers unless stated otherwise; sizes are in
  *    elements unless stated otherwise.
- *  - `stream` is a cudaStream_t passed as void*; all work is enqueued on it and
- *    every entry point returns without synchronising.
+ *  - `stream` is a cudaStream_t passed as void*; all work is ordered on it and
+ *    every entry point returns without synchronising.  (gkv_quantize and
+ *    gkv_dequantize may run their rotated-tier kernels on a library-owned
+ *    stream of the same GPU, started after the work already on `stream` and
+ *    joined back into `stream` before the call returns, so later work on
+ *    `stream` sees their results.)
  *  - Return value: GKV_OK (0) or a negative gkv_status; gkv_last_error()
  *    returns a message for the calling thread's last failure.
  *  - Kernels record problems they find in the data (an index list entry outside
