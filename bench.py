@@ -351,6 +351,47 @@ def time_compression(d: Dist, w, mode: str, steps: int, warmup: int, with_clocks
             "clocks": clocks.summary() if clocks else None, "in_bytes": in_bytes, "comp_bytes": comp_bytes}
 
 
+def copy_ceiling(host_pairs, dev) -> list:
+    """GB/s of plain copies of this rank's pinned cache: host to device alone,
+    device to host alone, and both at once on two streams (bytes of both
+    directions / time) -- the ceiling the end-to-end figure is measured against.
+    Every rank copies at the same time, so the figures show what the ranks'
+    shared host memory and PCIe links give each of them."""
+    import torch
+
+    hosts = [h for pair in host_pairs for h in pair]
+    nbytes = sum(h.numel() * h.element_size() for h in hosts)
+    dst = [torch.empty_like(h, device=dev) for h in hosts]
+    src = [torch.empty_like(h, device=dev) for h in hosts]
+    back = [torch.empty_like(h, pin_memory=True) for h in hosts]
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(fns):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for st, fn in fns:
+            with torch.cuda.stream(st):
+                fn()
+        torch.cuda.synchronize(dev)
+        return time.perf_counter() - t0
+
+    def h2d():
+        for h, x in zip(hosts, dst):
+            x.copy_(h, non_blocking=True)
+
+    def d2h():
+        for b, x in zip(back, src):
+            b.copy_(x, non_blocking=True)
+
+    timed([(s1, h2d), (s2, d2h)])  # warm-up
+    t_h2d = timed([(s1, h2d)])
+    t_d2h = timed([(s2, d2h)])
+    t_both = timed([(s1, h2d), (s2, d2h)])
+    del dst, src, back
+    torch.cuda.empty_cache()
+    return [nbytes / t_h2d / 1e9, nbytes / t_d2h / 1e9, 2 * nbytes / t_both / 1e9]
+
+
 def time_selection(dev, T: int, scores, reps: int = 20) -> float:
     """Device ms of one gkv_select_tiers call (graphkv profile) on fp32 [T] scores."""
     import ctypes
@@ -586,10 +627,13 @@ def run_ours(args):
         e2e_s = (time.perf_counter() - t0) / args.e2e_steps
         d.barrier()
         e2e_s = max(r[0] for r in d.gather([e2e_s]))
+        ceiling = d.gather(copy_ceiling(host_pairs, d.dev))  # all ranks at once: the shared host limit
         e2e = {"value": round(d.world * in_bytes_rank / e2e_s / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": in_bytes_rank + 4 * w.seq, "d2h_bytes_per_step": in_bytes_rank,
                "ms_per_step": round(1e3 * e2e_s, 3), "steps": args.e2e_steps,
-               "path": "quantize_hf_cache(host pinned legacy cache, output='legacy') -> host tensors"}
+               "path": "quantize_hf_cache(host pinned legacy cache, output='legacy') -> host tensors",
+               "copy_ceiling_gbs_per_rank": {k: [round(r[i], 1) for r in ceiling]
+                                             for i, k in enumerate(("h2d", "d2h", "both_ways"))}}
 
     if d.rank != 0:
         d.close()
