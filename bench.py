@@ -351,6 +351,35 @@ def time_compression(d: Dist, w, mode: str, steps: int, warmup: int, with_clocks
             "clocks": clocks.summary() if clocks else None, "in_bytes": in_bytes, "comp_bytes": comp_bytes}
 
 
+def bind_host_to_gpu(dev):
+    """Run this process on the CPUs local to the GPU's PCIe attachment, so that the
+    pinned host buffers allocated next land in that NUMA node's memory; returns
+    (previous CPU set, description), or (None, None) when the topology is not
+    visible."""
+    import torch
+
+    p = torch.cuda.get_device_properties(dev)
+    base = f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    try:
+        with open(f"{base}/local_cpulist") as f:
+            spec = f.read().strip()
+        with open(f"{base}/numa_node") as f:
+            node = int(f.read().strip())
+    except (OSError, ValueError):
+        return None, None
+    cpus = set()
+    for part in spec.split(","):
+        if part:
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+    before = os.sched_getaffinity(0)
+    use = cpus & before
+    if not use:
+        return None, None
+    os.sched_setaffinity(0, use)
+    return before, {"numa_node": node, "cpus": len(use)}
+
+
 def copy_ceiling(host_pairs, dev) -> list:
     """GB/s of plain copies of this rank's pinned cache: host to device alone,
     device to host alone, and both at once on two streams (bytes of both
@@ -604,6 +633,7 @@ def run_ours(args):
 
         wN = replace(w, batch=w.batch * d.world)
         shard = shard_units(w.layers, w.heads, d.world, d.rank)
+        saved_cpus, binding = bind_host_to_gpu(d.dev)
         host_pairs = []
         for (l, h0, h1) in shard:
             k, v = make_layer(wN, l, device=str(d.dev), heads=range(h0, h1))
@@ -628,12 +658,16 @@ def run_ours(args):
         d.barrier()
         e2e_s = max(r[0] for r in d.gather([e2e_s]))
         ceiling = d.gather(copy_ceiling(host_pairs, d.dev))  # all ranks at once: the shared host limit
+        del host_pairs
+        if saved_cpus is not None:
+            os.sched_setaffinity(0, saved_cpus)
         e2e = {"value": round(d.world * in_bytes_rank / e2e_s / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": in_bytes_rank + 4 * w.seq, "d2h_bytes_per_step": in_bytes_rank,
                "ms_per_step": round(1e3 * e2e_s, 3), "steps": args.e2e_steps,
                "path": "quantize_hf_cache(host pinned legacy cache, output='legacy') -> host tensors",
                "copy_ceiling_gbs_per_rank": {k: [round(r[i], 1) for r in ceiling]
-                                             for i, k in enumerate(("h2d", "d2h", "both_ways"))}}
+                                             for i, k in enumerate(("h2d", "d2h", "both_ways"))},
+               "host_binding": binding or "none (PCIe topology not visible)"}
 
     if d.rank != 0:
         d.close()
