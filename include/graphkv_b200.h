@@ -14,7 +14,8 @@
  *    gkv_dequantize may run their rotated-tier kernels on a library-owned
  *    stream of the same GPU, started after the work already on `stream` and
  *    joined back into `stream` before the call returns, so later work on
- *    `stream` sees their results.)
+ *    `stream` sees their results.  The first such call on a device creates that
+ *    stream and its two events; make it before any stream capture.)
  *  - Return value: GKV_OK (0) or a negative gkv_status; gkv_last_error()
  *    returns a message for the calling thread's last failure.
  *  - Kernels record problems they find in the data (an index list entry outside
