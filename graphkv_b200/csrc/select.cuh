@@ -65,7 +65,9 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 constexpr int kBins = 2048;  // 11-bit digits
 
 struct SelShared {
-  uint32_t hist[2][kBins];  // alternate digit passes, so a block clears one while peers read the other
+  uint32_t hist[3][kBins];  // 0, 1: alternate digit passes, so a block clears one while peers read the
+                            // other; 2: the first selection's first-digit counts, kept for the cold tier
+  uint32_t saved_bin;       // the first selection's first-digit bin
   uint32_t warp_cnt[3][kSelWarps];
   uint32_t warp_off[3][kSelWarps];
   uint32_t wsum[kSelWarps];
@@ -890,21 +892,44 @@ __device__ void exact_on_block0(const SelectParams& p, const SelState<SMEM>& st,
 // `src` and return their mark for the next sweep; a tie across the boundary is
 // resolved and marked here.  `pm`: the previous selection's pending marks,
 // applied by the first-digit sweep.  `buf`: histogram buffer of the next pass.
+// save: keep this selection's first-digit counts (hist[2]) and bin for a later
+// selection over the same keys.  from_saved: a smallest-k selection that may take
+// its first digit from those counts: the earlier (largest-k) selection marks only
+// candidates in its bin or above, so the counts below that bin are this
+// selection's too; when the k-th smallest lies below it, the first sweep is
+// skipped and the pending marks ride with the second.
 template <bool SMEM>
 __device__ MarkOp select_radix(const SelectParams& p, const SelState<SMEM>& st, SelShared& sh, const MarkOp& pm,
-                               bool init, const float* src, int k, bool largest, uint8_t mark, int& buf) {
+                               bool init, const float* src, int k, bool largest, uint8_t mark, int& buf,
+                               bool save = false, bool from_saved = false) {
   BinPick bp{0u, (uint32_t)k, 0u, true};
   uint32_t prefix = 0u;
-  for (int d = 0; d < 3; ++d) {
+  int d0 = 0;
+  MarkOp first_pm = pm;
+  if (save && threadIdx.x == 0) sh.saved_bin = 0;  // no reuse unless the first digit is found
+  if (from_saved && !largest) {
+    const BinPick sb = find_bin(sh, 2, digit_bins(0), (uint32_t)k, false);
+    if (sb.found && sb.bin < sh.saved_bin) {
+      bp = sb;
+      prefix = sb.bin << digit_shift(0);
+      d0 = 1;
+    }
+  }
+  for (int d = d0; d < 3; ++d) {
     for (int i = threadIdx.x; i < kBins; i += kSelThreads) sh.hist[buf][i] = 0;
     __syncthreads();
     if (d == 0 && init) hist_sweep<SMEM, true>(p, st, sh.hist[buf], pm, src, 0, 0u);
-    else hist_sweep<SMEM, false>(p, st, sh.hist[buf], d == 0 ? pm : no_mark(), src, d, prefix);
+    else hist_sweep<SMEM, false>(p, st, sh.hist[buf], d == d0 ? first_pm : no_mark(), src, d, prefix);
+    if (save && d == 0) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < kBins; i += kSelThreads) sh.hist[2][i] = sh.hist[buf][i];
+    }
     cluster_sync();
     bp = find_bin(sh, buf, digit_bins(d), bp.remaining, largest);
     buf ^= 1;
     // fewer candidates than k: mark all of them; the final count check reports it
     if (!bp.found) return MarkOp{src, largest ? 0u : 0xFFFFFFFFu, mark, largest, true};
+    if (save && d == 0 && threadIdx.x == 0) sh.saved_bin = bp.bin;
     prefix |= bp.bin << digit_shift(d);
   }
   if (bp.remaining < bp.count) {  // candidates equal to the k-th key straddle the boundary
@@ -1010,8 +1035,11 @@ __device__ void select_body(const SelectParams& p, SelState<SMEM> st, SelShared&
   MarkOp pm = no_mark();
   bool init = true;
   int buf = 0;
+  // the cold tier may reuse the protection's first digit (same keys, no outlier
+  // selection in between)
+  const bool reuse = p.keep_protect > 0 && p.keep_outlier == 0 && p.keep_cold > 0;
   if (p.keep_protect > 0) {
-    pm = select_radix<SMEM>(p, st, sh, pm, init, scores_src, p.keep_protect, true, kRet, buf);
+    pm = select_radix<SMEM>(p, st, sh, pm, init, scores_src, p.keep_protect, true, kRet, buf, reuse);
     init = false;
   }
   if (p.keep_outlier > 0) {
@@ -1019,7 +1047,7 @@ __device__ void select_body(const SelectParams& p, SelState<SMEM> st, SelShared&
     init = false;
   }
   if (p.keep_cold > 0) {
-    pm = select_radix<SMEM>(p, st, sh, pm, init, scores_src, p.keep_cold, false, kCold, buf);
+    pm = select_radix<SMEM>(p, st, sh, pm, init, scores_src, p.keep_cold, false, kCold, buf, false, reuse);
     init = false;
   }
   if (init) {  // no score selection: sink and tail only
