@@ -51,7 +51,7 @@ def _rank(rank, world, port, wkey, out):
 @pytest.mark.parametrize("world", [2, 3])
 def test_gathered_stats_equal_the_reference_stats(wkey, golden, world):
     port = 29400 + 7 * world + len(wkey) + (os.getpid() % 200)
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:  # no fork of a threaded process
         out = m.dict()
         mp.spawn(_rank, args=(world, port, wkey, out), nprocs=world, join=True)
         results = [out[r] for r in range(world)]
